@@ -1,0 +1,245 @@
+/*
+ * ltm_b200.h -- C ABI of the B200-native quantized Titan-block forward.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, returns an
+ * ltm_status and never throws.  Device pointers are CUDA global-memory
+ * pointers on the current device; `stream` is a cudaStream_t passed as void*
+ * (NULL = legacy default stream).  All launches are asynchronous on `stream`.
+ * On error, ltm_last_error_string() describes the failure of the calling
+ * thread's last call.
+ *
+ * The reference interfaces each group replaces (paths inside the
+ * Obsidian-Memory-Transformer project) are cited beside the declarations,
+ * with the formula each one computes.
+ */
+#ifndef LTM_B200_H
+#define LTM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LTM_API __attribute__((visibility("default")))
+#else
+#define LTM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status -- */
+/* Replaces CUDA_CHECK -> std::runtime_error (include/core/utils/cuda_utils.cuh:19-45):
+ * no exception crosses the ABI; the C++ wrapper rethrows. */
+typedef enum ltm_status {
+  LTM_OK = 0,
+  LTM_ERR_INVALID_ARG = 1,
+  LTM_ERR_CUDA = 2,
+  LTM_ERR_COMM = 3,
+  LTM_ERR_TIMEOUT = 4,   /* a bounded in-kernel wait expired (device error word) */
+  LTM_ERR_UNSUPPORTED = 5,
+  LTM_ERR_NO_DEVICE = 6
+} ltm_status;
+
+typedef enum ltm_dtype {
+  LTM_DTYPE_F32 = 0,
+  LTM_DTYPE_F16 = 1,
+  LTM_DTYPE_BF16 = 2
+} ltm_dtype;
+
+/* Activation fused into a linear's epilogue. GELU is the tanh form of
+ * src/core/ops/fused_ops.cu:136-142; SIGMOID is 1/(1+exp(-x)). */
+typedef enum ltm_epilogue {
+  LTM_EPI_NONE = 0,
+  LTM_EPI_GELU = 1,
+  LTM_EPI_SIGMOID = 2
+} ltm_epilogue;
+
+/* Weight/activation quantization scheme of a block (extension of
+ * QuantizationConfig, include/core/quantization/quantizer.cuh:24-52). */
+typedef enum ltm_scheme {
+  LTM_SCHEME_W8A32 = 0, /* int8 per-output-channel weights, fp32 activations   */
+  LTM_SCHEME_W8A8 = 1,  /* int8 weights, per-token dynamic int8 activations     */
+  LTM_SCHEME_W4A16 = 2  /* int4 group-128 asymmetric weights, 16-bit activations */
+} ltm_scheme;
+
+LTM_API const char* ltm_version(void);
+/* Message of the calling thread's last failed call ("" if none). */
+LTM_API const char* ltm_last_error_string(void);
+/* Reads and clears the device error word set by bounded in-kernel waits on
+ * the current device (0 = none; otherwise the code of the wait that expired). */
+LTM_API ltm_status ltm_device_error(int* code_out);
+
+/* ---------------------------------------------------------- quantization -- */
+/* Replaces Quantizer<T>::quantize with per_channel=true, symmetric=true,
+ * channel_axis=0 (include/core/quantization/quantizer.cuh:183,
+ * src/core/quantization/quantizer.cu:263-310):
+ *   s[n] = max_k |w[n,k]| / 127 ;  q[n,k] = clamp(round_half_away(w/s[n]), -127, 127)
+ *   (s[n] == 0  =>  q[n,:] = 0).  Scales live on the device.
+ * w: [N,K] row-major in w_dtype; q: int8 [N,K]; s: fp32 [N]. */
+LTM_API ltm_status ltm_quantize_int8_per_channel(const void* w, ltm_dtype w_dtype, int64_t N, int64_t K,
+                                         int8_t* q, float* s, void* stream);
+
+/* Replaces Quantizer<T>::dequantize, per-channel symmetric
+ * (src/core/quantization/quantizer.cu:144-161,312-328):  out[n,k] = q[n,k] * s[n]. */
+LTM_API ltm_status ltm_dequantize_int8_per_channel(const int8_t* q, const float* s, int64_t N, int64_t K,
+                                           void* out, ltm_dtype out_dtype, void* stream);
+
+/* Per-token dynamic activation quantization (same formula as the per-channel
+ * weight quantizer, rows = tokens): a: [M,K] in a_dtype -> q int8 [M,K], s fp32 [M].
+ * New entry point; the reference declares dynamic ranges only
+ * (include/core/quantization/quantizer.cuh:38-39,191). */
+LTM_API ltm_status ltm_quantize_act_int8_per_token(const void* a, ltm_dtype a_dtype, int64_t M, int64_t K,
+                                           int8_t* q, float* s, void* stream);
+
+/* INT4 asymmetric group quantization + packing; implements
+ * QuantizationPrecision::INT4 (include/core/quantization/quantizer.cuh:12),
+ * following the asymmetric form of src/core/quantization/quantizer.cu:291-293
+ * for unsigned nibbles.  Per (row n, group g of `group_size` consecutive k):
+ *   mn = min(0, min w), mx = max(0, max w), s = (mx - mn) / 15,
+ *   zp = clamp(round_half_away(-mn / s), 0, 15),
+ *   q  = clamp(round_half_away(w / s + zp), 0, 15)      (s == 0 => q = zp = 0)
+ *   packed[n, k/2] = q[n,2j] | q[n,2j+1] << 4            (low nibble = even k)
+ * w: [N,K]; packed: uint8 [N,K/2]; s: fp32 [N,K/group]; zp: uint8 [N,K/group].
+ * group_size must be 128 and divide K. */
+LTM_API ltm_status ltm_quantize_int4_grouped(const void* w, ltm_dtype w_dtype, int64_t N, int64_t K,
+                                     int group_size, uint8_t* packed, float* s, uint8_t* zp,
+                                     void* stream);
+
+/* out[n,k] = (q[n,k] - zp[n,g]) * s[n,g], g = k / group_size. */
+LTM_API ltm_status ltm_dequantize_int4_grouped(const uint8_t* packed, const float* s, const uint8_t* zp,
+                                       int64_t N, int64_t K, int group_size, void* out,
+                                       ltm_dtype out_dtype, void* stream);
+
+/* --------------------------------------------------------------- linears -- */
+/* Quantized replacements of ops::matmul + bias add (src/core/ops/mma_ops.cu:59-92,
+ * src/core/ops/fused_ops.cu:187-210) and of the per-token FFN kernel
+ * (src/core/transformer/titan_inspired_block.cu:39-98).  Weights are [N,K]
+ * row-major (out x in), matching the reference kernels' indexing.
+ *
+ * W8A8:  acc[m,n] = sum_k qa[m,k]*qw[n,k] (exact int32);
+ *        y[m,n]   = act(acc * sa[m] * sw[n] + bias[n])  stored as y_dtype.
+ *        sa may be NULL (= 1); bias may be NULL (= 0).  Requires K % 16 == 0,
+ *        N % 32 == 0.  tcgen05 kind::i8 tensor-core GEMM on sm_100a. */
+LTM_API ltm_status ltm_linear_w8a8(const int8_t* qa, const float* sa, const int8_t* qw, const float* sw,
+                           const float* bias, ltm_epilogue act, void* y, ltm_dtype y_dtype,
+                           int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Exactness probe of the W8A8 GEMM: writes the raw int32 accumulators. */
+LTM_API ltm_status ltm_linear_w8a8_acc_i32(const int8_t* qa, const int8_t* qw, int32_t* acc, int64_t M,
+                                   int64_t N, int64_t K, void* stream);
+
+/* W4A16: y = act(a @ dequant(W)^T + bias), a: [M,K] f16/bf16; the weight is
+ * dequantized to a_dtype (as Quantizer::dequantize writes T) and contracted
+ * on tcgen05 kind::f16 with fp32 accumulation; y stored as a_dtype.
+ * Requires K % 128 == 0 (group 128), N % 32 == 0. */
+LTM_API ltm_status ltm_linear_w4a16(const void* a, ltm_dtype a_dtype, const uint8_t* packed,
+                            const float* s, const uint8_t* zp, const float* bias,
+                            ltm_epilogue act, void* y, int64_t M, int64_t N, int64_t K,
+                            void* stream);
+
+/* W8A32: y = act((a @ qw^T) * sw[n] + bias[n]) with fp32 a and y (the fp32
+ * TitanBlock<float> path with int8 per-channel weights). */
+LTM_API ltm_status ltm_linear_w8a32(const float* a, const int8_t* qw, const float* sw, const float* bias,
+                            ltm_epilogue act, float* y, int64_t M, int64_t N, int64_t K,
+                            void* stream);
+
+/* ----------------------------------------------------------------- block -- */
+/* Field-for-field mirror of ltm::transformer::TitanBlockConfig
+ * (include/core/transformer/titan_inspired_block.cuh:19-50): same names, same
+ * order, same defaults (ltm_block_config_default).  bools are int (0/1). */
+typedef struct ltm_block_config {
+  int hidden_dim;
+  int ffn_dim;
+  int num_heads;
+  int head_dim;
+  int memory_slots;
+  int memory_dim;
+  float memory_update_rate;
+  int use_memory_compression;
+  float memory_compression_ratio;
+  int use_flash_attention;
+  int use_alibi;
+  int use_rotary;
+  float dropout_prob;
+  int use_parallel_attention;
+  int use_memory_gating;
+  int use_layer_norm;
+  int use_bias;
+  int fuse_operations;
+  int learn_memory;
+  int learn_compression;
+  int gradient_checkpointing;
+} ltm_block_config;
+
+/* Quantization extension of the block (kept separate so the field layout of
+ * ltm_block_config stays that of TitanBlockConfig). */
+typedef struct ltm_quant_config {
+  ltm_scheme scheme;
+  int group_size;           /* INT4 group (128) */
+  ltm_dtype act_dtype;      /* F32 for W8A32; F16 or BF16 otherwise */
+  int memory_write;         /* 1: write the bank after the read (TB-v1 write) */
+  int use_attention_scores; /* 1: slot weights from the mean memory query */
+} ltm_quant_config;
+
+/* Host fp32 master weights of one block, all row-major [out, in].  Biases may
+ * be NULL when use_bias == 0.  `memory` is the bank [memory_slots, hidden_dim]. */
+typedef struct ltm_block_weights {
+  const float *w_qkv, *b_qkv;   /* [3H,H], [3H]: rows Q | K | V, head h at rows h*dh.. */
+  const float *w_o, *b_o;       /* [H,H] */
+  const float *w_qm, *b_qm;     /* memory-attention query  [H,H] */
+  const float *w_km, *b_km;     /* memory-attention key    [H,H] (applied to the bank) */
+  const float *w_vm, *b_vm;     /* memory-attention value  [H,H] (applied to the bank) */
+  const float *w_om, *b_om;     /* memory-attention output [H,H] */
+  const float *w_g, *b_g;       /* compression gate        [H,H] */
+  const float *w_1, *b_1;       /* FFN up   [F,H] */
+  const float *w_2, *b_2;       /* FFN down [H,F] */
+  const float *ln1_g, *ln1_b;   /* [H] */
+  const float *ln2_g, *ln2_b;   /* [H] */
+  const float* memory;          /* [Ms,H] */
+} ltm_block_weights;
+
+typedef struct ltm_block ltm_block;
+
+LTM_API void ltm_block_config_default(ltm_block_config* cfg);
+
+/* Replaces `explicit TitanBlock(const TitanBlockConfig&)` + initialize()
+ * (titan_inspired_block.cuh:69,76).  Weights are supplied by
+ * ltm_block_load_weights instead of curand init. */
+LTM_API ltm_status ltm_block_create(const ltm_block_config* cfg, const ltm_quant_config* qcfg, int device,
+                            ltm_block** out);
+/* Quantizes and uploads the host fp32 master weights (synchronous). */
+LTM_API ltm_status ltm_block_load_weights(ltm_block* blk, const ltm_block_weights* w);
+
+/* Replaces TitanBlock<T>::forward (titan_inspired_block.cuh:86-91,
+ * titan_inspired_block.cu:254-345) with the TB-v1 semantics.  x, y: device
+ * [B,S,H] in act_dtype (x and y must not alias).  attention_mask must be NULL
+ * (self-attention is causal; an explicit mask returns LTM_ERR_UNSUPPORTED).
+ * Workspace grows on the first call at a new B*S and is reused afterwards. */
+LTM_API ltm_status ltm_block_forward(ltm_block* blk, const void* x, void* y, const void* attention_mask,
+                             int B, int S, void* stream);
+
+/* Copies the memory bank [Ms,H] (act_dtype) to a device buffer
+ * (getMemoryBank(), titan_inspired_block.cuh:133). */
+LTM_API ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stream);
+LTM_API ltm_status ltm_block_destroy(ltm_block* blk);
+
+/* ----------------------------------------------------------------- model -- */
+/* Multi-layer model (token embedding gather + n_layers Titan blocks), the
+ * forward of TitanModel (python_bindings/ltm/model.py:159-215) without the
+ * LM head. */
+typedef struct ltm_model ltm_model;
+LTM_API ltm_status ltm_model_create(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
+                            int n_layers, int vocab_size, int device, ltm_model** out);
+/* embedding: host fp32 [vocab, H] */
+LTM_API ltm_status ltm_model_load_embedding(ltm_model* m, const float* embedding);
+LTM_API ltm_status ltm_model_load_layer(ltm_model* m, int layer, const ltm_block_weights* w);
+/* tokens: device int32 [B,S]; hidden_out: device [B,S,H] act_dtype. */
+LTM_API ltm_status ltm_model_forward(ltm_model* m, const int32_t* tokens, void* hidden_out, int B, int S,
+                             void* stream);
+LTM_API ltm_status ltm_model_destroy(ltm_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LTM_B200_H */

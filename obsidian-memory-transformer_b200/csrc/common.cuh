@@ -1,0 +1,310 @@
+// common.cuh -- shared host/device helpers of the B200 Titan-block library:
+// status plumbing for the C ABI, dtype traits, and the sm_100a PTX wrappers
+// (mbarrier, TMA, tcgen05) used by the tensor-core kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/ltm_b200.h"
+
+namespace ltm_b200 {
+
+// ------------------------------------------------------------------ status --
+void set_error(const std::string& msg);
+void clear_error();
+
+struct Fail {
+  ltm_status st;
+};
+
+// Device address (current device) of the error word that bounded in-kernel
+// waits write when they expire (0 = none).  Kernels receive it as a parameter.
+int* device_error_ptr();
+
+enum DeviceErrorCode : int {
+  kErrNone = 0,
+  kErrWaitFull = 1,     // consumer waited too long for a TMA stage
+  kErrWaitEmpty = 2,    // producer waited too long for a free stage
+  kErrWaitAccum = 3,    // epilogue waited too long for the accumulator
+  kErrWaitOther = 4,
+};
+
+#define LTM_CUDA_TRY(expr)                                                              \
+  do {                                                                                  \
+    cudaError_t _e = (expr);                                                            \
+    if (_e != cudaSuccess) {                                                            \
+      ::ltm_b200::set_error(std::string(#expr) + ": " + cudaGetErrorString(_e));       \
+      throw ::ltm_b200::Fail{LTM_ERR_CUDA};                                             \
+    }                                                                                   \
+  } while (0)
+
+#define LTM_REQUIRE(cond, msg)                                                          \
+  do {                                                                                  \
+    if (!(cond)) {                                                                      \
+      ::ltm_b200::set_error(std::string("invalid argument: ") + (msg));                 \
+      throw ::ltm_b200::Fail{LTM_ERR_INVALID_ARG};                                      \
+    }                                                                                   \
+  } while (0)
+
+#define LTM_UNSUPPORTED(msg)                                                            \
+  do {                                                                                  \
+    ::ltm_b200::set_error(std::string("unsupported: ") + (msg));                        \
+    throw ::ltm_b200::Fail{LTM_ERR_UNSUPPORTED};                                        \
+  } while (0)
+
+// Wraps a C-ABI body: converts Fail / std exceptions into a status.
+template <class F>
+ltm_status guarded(F&& f) {
+  try {
+    clear_error();
+    f();
+    return LTM_OK;
+  } catch (const Fail& e) {
+    return e.st;
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return LTM_ERR_CUDA;
+  }
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    throw Fail{LTM_ERR_CUDA};
+  }
+}
+
+inline size_t dtype_size(ltm_dtype d) { return d == LTM_DTYPE_F32 ? 4 : 2; }
+
+// -------------------------------------------------------------- dtype I/O --
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <class T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Dispatch a runtime dtype onto a template functor taking the element type.
+template <class F>
+void dispatch_dtype(ltm_dtype d, F&& f) {
+  switch (d) {
+    case LTM_DTYPE_F32: f(float{}); break;
+    case LTM_DTYPE_F16: f(__half{}); break;
+    case LTM_DTYPE_BF16: f(__nv_bfloat16{}); break;
+    default: LTM_REQUIRE(false, "unknown dtype");
+  }
+}
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+// ------------------------------------------------------- PTX: sync/timing --
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Upper bound of any single in-kernel wait.  Kernels that exceed it record an
+// error code in the device error word and unwind instead of spinning forever.
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity.  Returns false (and
+// records `code` in the device error word and the CTA abort flag) when the
+// limit expires or another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------- PTX: TMA --
+__device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// --------------------------------------------------------- PTX: tcgen05 --
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot_smem)),
+               "r"(ncols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma issued so far by this thread completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, int8 x int8 -> int32.
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A * B^T, f16/bf16 inputs -> fp32.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Loads 32 consecutive 32-bit columns of this warp's 32 TMEM lanes
+// (thread i of the warp receives lane base+i).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row groups 1024 bytes apart), the
+// layout a SWIZZLE_128B TMA box of 128-byte rows produces.  Fields: start
+// address>>4 [0,14), leading byte offset>>4 [16,30) (unused for this layout),
+// stride byte offset>>4 [32,46), descriptor version 1 [46,48), swizzle mode
+// 2 = 128B [61,64).
+__device__ __forceinline__ uint64_t make_desc_kmajor_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(16 >> 4) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::i8 (signed x signed -> s32),
+// both operands K-major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+  return (2u << 4)                       // D format: s32
+         | (1u << 7)                     // A: signed 8-bit
+         | (1u << 10)                    // B: signed 8-bit
+         | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16 (f16 or bf16 inputs, fp32
+// accumulate), both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
+  return (1u << 4)                                   // D format: f32
+         | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// -------------------------------------------------------- TMA descriptors --
+// 2-D tiled tensor map over a row-major [rows, cols] matrix of `elem_bytes`
+// elements with the 128-byte swizzle; box = box_cols x box_rows.
+void make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols,
+                 uint32_t box_rows);
+
+}  // namespace ltm_b200

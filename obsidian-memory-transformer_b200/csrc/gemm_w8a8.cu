@@ -1,0 +1,226 @@
+// gemm_w8a8.cu -- W8A8 linear on the 5th-generation tensor cores.
+//
+//   acc[m,n] = sum_k qa[m,k] * qw[n,k]     int8 x int8 -> exact int32 in TMEM
+//   y        = epilogue(acc)                dequant, bias, act, rope/resid/gate-mix
+//
+// One CTA computes a 128 x BN tile.  Warp roles (192 threads):
+//   warp 0      TMA producer: 128 x 128-byte tiles of qa and BN x 128-byte
+//               tiles of qw into a STAGES-deep ring (128-byte swizzle)
+//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8
+//               (K = 32 each) per stage, tcgen05.commit frees the stage
+//   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (warp w reads
+//               TMEM lanes 32*(w%4)..+31 = tile rows), fused epilogue, stores
+// Every mbarrier wait is bounded (common.cuh); an expired wait records a code
+// in the device error word and the CTA unwinds, releasing its TMEM.
+//
+// Replaces the CUTLASS 2.x Sm80 half GEMM of the reference
+// (src/core/ops/mma_ops.cu:20-92) for the quantized linears.
+#include <type_traits>
+
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace ltm_b200 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle row
+
+template <int BN, int STAGES>
+struct W8A8Smem {
+  static constexpr uint32_t kA = kBM * kBK;
+  static constexpr uint32_t kB = BN * kBK;
+  static constexpr uint32_t kStage = kA + kB;
+  static constexpr uint32_t kBarOff = STAGES * kStage;
+  static constexpr uint32_t kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
+};
+
+template <int BN, int STAGES, int MODE, class OutT>
+__global__ void __launch_bounds__(192, (BN <= 128 ? 2 : 1))
+    w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   int M, int N, int K, Epilogue ep, int* err) {
+  using L = W8A8Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * kBM;
+  const int nkb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(accf, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tslot, BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait_bounded(empty + s, ph ^ 1, abort_flag, err, kErrWaitEmpty)) break;
+        uint8_t* a_dst = smem + s * L::kStage;
+        mbar_arrive_expect_tx(full + s, L::kStage);
+        tma_load_2d(a_dst, &tmA, full + s, kb * kBK, m0);
+        tma_load_2d(a_dst + L::kA, &tmB, full + s, kb * kBK, n0);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // Drain this CTA's copies still in flight before the CTA unwinds.
+        volatile int never = 0;
+        for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
+          mbar_wait_bounded(full + (j % STAGES), (j / STAGES) & 1, &never, err, kErrWaitOther);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait_bounded(full + s, ph, abort_flag, err, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
+        const uint32_t b_addr = a_addr + L::kA;
+#pragma unroll
+        for (int k = 0; k < kBK / 32; ++k) {
+          tc_mma_i8(tmem, make_desc_kmajor_sw128(a_addr + k * 32),
+                    make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+        }
+        tc_commit(empty + s);
+      }
+      tc_commit(accf);
+      if (*abort_flag) {
+        volatile int never = 0;
+        mbar_wait_bounded(accf, 0, &never, err, kErrWaitOther);
+      }
+    }
+  } else {
+    // Epilogue warpgroup: warps 2..5 -> TMEM lane quarter (warp % 4).
+    const int q = warp & 3;
+    const bool ok = mbar_wait_bounded(accf, 0, abort_flag, err, kErrWaitAccum);
+    tc_fence_after();
+    const int64_t m = static_cast<int64_t>(m0) + q * 32 + lane;
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
+        tmem_wait_ld();
+        const int64_t n = static_cast<int64_t>(n0) + c * 32;
+        if (m < M && n < N && !*abort_flag) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if constexpr (MODE == kEpiAccI32)
+              v[i] = __int_as_float(static_cast<int>(r[i]));
+            else
+              v[i] = static_cast<float>(static_cast<int>(r[i]));
+          }
+          epilogue_store32<MODE, OutT>(ep, m, n, v);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+template <int BN, int STAGES, int MODE, class OutT>
+void launch_w8a8_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                      const Epilogue& ep, cudaStream_t stream) {
+  using L = W8A8Smem<BN, STAGES>;
+  auto kern = w8a8_tc_kernel<BN, STAGES, MODE, OutT>;
+  LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
+  kern<<<grid, 192, L::kBytes, stream>>>(ta, tb, M, N, K, ep, device_error_ptr());
+  check_launch("w8a8_tc_kernel");
+}
+
+}  // namespace
+
+// Launches the W8A8 GEMM with the given epilogue. qa: [M,K], qw: [N,K].
+void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
+                 ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream) {
+  LTM_REQUIRE(M >= 0 && N >= 0 && K >= 0, "negative size");
+  LTM_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "size exceeds int32");
+  if (M == 0 || N == 0) return;
+  LTM_REQUIRE(K > 0, "K must be positive");
+  LTM_REQUIRE(K % 16 == 0, "K must be a multiple of 16");
+  LTM_REQUIRE(N % 32 == 0, "N must be a multiple of 32");
+  LTM_REQUIRE(qa && qw && ep.out, "NULL pointer");
+  const size_t osz = (mode == kEpiAccI32) ? 4 : dtype_size(out_dt);
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(ep.out) & 15) == 0, "output must be 16-byte aligned");
+  LTM_REQUIRE((ep.ldo * osz) % 16 == 0, "output row stride must be a multiple of 16 bytes");
+  if (mode == kEpiResid || mode == kEpiGateMix) {
+    LTM_REQUIRE((ep.ld_aux * osz) % 16 == 0, "aux row stride must be a multiple of 16 bytes");
+  }
+  constexpr int BN = 128;
+  constexpr int STAGES = 3;
+  CUtensorMap ta, tb;
+  make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
+  make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, BN);
+  dispatch_epilogue(mode, out_dt, [&](auto mode_c, auto out_tag) {
+    constexpr int MODE = decltype(mode_c)::value;
+    using OutT = decltype(out_tag);
+    launch_w8a8_inst<BN, STAGES, MODE, OutT>(ta, tb, static_cast<int>(M), static_cast<int>(N),
+                                             static_cast<int>(K), ep, stream);
+  });
+}
+
+}  // namespace ltm_b200
+
+using namespace ltm_b200;
+
+extern "C" ltm_status ltm_linear_w8a8(const int8_t* qa, const float* sa, const int8_t* qw,
+                                      const float* sw, const float* bias, ltm_epilogue act, void* y,
+                                      ltm_dtype y_dtype, int64_t M, int64_t N, int64_t K,
+                                      void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(act == LTM_EPI_NONE || act == LTM_EPI_GELU || act == LTM_EPI_SIGMOID,
+                "unknown epilogue");
+    Epilogue ep;
+    ep.act = act;
+    ep.row_scale = sa;
+    ep.col_scale = sw;
+    ep.bias = bias;
+    ep.out = y;
+    ep.ldo = N;
+    launch_w8a8(qa, qw, M, N, K, kEpiPlain, y_dtype, ep, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_linear_w8a8_acc_i32(const int8_t* qa, const int8_t* qw, int32_t* acc,
+                                              int64_t M, int64_t N, int64_t K, void* stream) {
+  return guarded([&] {
+    Epilogue ep;
+    ep.out = acc;
+    ep.ldo = N;
+    launch_w8a8(qa, qw, M, N, K, kEpiAccI32, LTM_DTYPE_F32, ep, as_stream(stream));
+  });
+}

@@ -1,0 +1,188 @@
+// norm.cu -- LayerNorm of (x + x) with an optional fused per-token INT8
+// quantization of its output and of the raw input, plus the embedding gather.
+//
+// LN follows src/core/ops/fused_ops.cu:15-86 as TitanBlock::layerNorm calls
+// it (residual = input, src/core/transformer/titan_inspired_block.cu:374-389):
+// v = x + x, two-pass mean / variance over the row, eps 1e-5,
+// y = (v - mean) * rsqrt(var + eps) * gamma + beta.  One CTA per row, each
+// thread owns one 16-byte vector of the row in registers, so the row is read
+// from HBM exactly once; reductions are warp shuffles + one shared-memory hop.
+#include "common.cuh"
+
+namespace ltm_b200 {
+namespace {
+
+template <int NW>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) t += (i * 32 < static_cast<int>(blockDim.x)) ? red[i] : 0.0f;
+  return t;
+}
+
+template <int NW>
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) t = fmaxf(t, (i * 32 < static_cast<int>(blockDim.x)) ? red[i] : 0.0f);
+  return t;
+}
+
+__device__ __forceinline__ int8_t q8(float v, float s) {
+  if (s == 0.0f) return 0;
+  float r = roundf(__fdiv_rn(v, s));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+template <class T, int V>
+__device__ __forceinline__ void store_q(int8_t* dst, const float (&v)[V], float s) {
+  int8_t o[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) o[i] = q8(v[i], s);
+  if constexpr (V == 8)
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+  else
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(o);
+}
+
+// One CTA per row; thread t owns elements [t*V, t*V+V).  NW = max warps.
+template <class T, int NW>
+__global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x, int H,
+                                                        const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta,
+                                                        T* __restrict__ y, int8_t* __restrict__ yq,
+                                                        float* __restrict__ ys,
+                                                        int8_t* __restrict__ xq,
+                                                        float* __restrict__ xs, int do_norm) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float red[NW];
+  const int64_t row = blockIdx.x;
+  const int e0 = threadIdx.x * V;
+  const bool active = e0 < H;
+  float xv[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) xv[i] = 0.0f;
+  if (active) {
+    uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + row * H + e0));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < V; ++i) xv[i] = to_f32(e[i]);
+  }
+  if (xq) {
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[i]));
+    am = block_max<NW>(am, red);
+    const float s = __fdiv_rn(am, 127.0f);
+    if (active) store_q<T, V>(xq + row * H + e0, xv, s);
+    if (threadIdx.x == 0) xs[row] = s;
+  }
+  float yv[V];
+  if (do_norm) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) sum += xv[i] + xv[i];
+    const float mean = block_sum<NW>(sum, red) / static_cast<float>(H);
+    float sq = 0.0f;
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float d = (xv[i] + xv[i]) - mean;
+        sq += d * d;
+      }
+    }
+    const float var = block_sum<NW>(sq, red) / static_cast<float>(H);
+    const float rstd = rsqrtf(var + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = active ? e0 + i : 0;
+      yv[i] = ((xv[i] + xv[i]) - mean) * rstd * __ldg(gamma + c) + __ldg(beta + c);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) yv[i] = xv[i];
+  }
+  if (y && active) {
+    uint4 raw;
+    T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < V; ++i) e[i] = from_f32<T>(yv[i]);
+    *reinterpret_cast<uint4*>(y + row * H + e0) = raw;
+  }
+  if (yq) {
+    float am = 0.0f;
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(yv[i]));
+    }
+    am = block_max<NW>(am, red);
+    const float s = __fdiv_rn(am, 127.0f);
+    if (active) store_q<T, V>(yq + row * H + e0, yv, s);
+    if (threadIdx.x == 0) ys[row] = s;
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__ table, int vocab,
+                                                           int H, const int32_t* __restrict__ tok,
+                                                           int64_t T_, T* __restrict__ out, int* err) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= T_) return;
+  const int lane = threadIdx.x & 31;
+  const int id = tok[t];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && lane == 0) atomicCAS(err, 0, 16);
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<int64_t>(ok ? id : 0) * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + t * H);
+  for (int j = lane; j < H / V; j += 32) dst[j] = ok ? __ldg(src + j) : make_uint4(0, 0, 0, 0);
+}
+
+}  // namespace
+
+// y (optional, dtype T) = LN(x + x); yq/ys (optional) = per-token int8 of the
+// fp32 LN output; xq/xs (optional) = per-token int8 of x.  do_norm = 0 skips
+// the normalisation (y = x).
+void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float* gamma,
+                  const float* beta, void* y, int8_t* yq, float* ys, int8_t* xq, float* xs,
+                  bool do_norm, cudaStream_t stream) {
+  if (rows == 0) return;
+  const int V = static_cast<int>(16 / dtype_size(dt));
+  LTM_REQUIRE(H % V == 0, "hidden size must be a multiple of 16 bytes");
+  const int threads = ((H / V + 31) / 32) * 32;
+  LTM_REQUIRE(threads <= 1024, "hidden size too large for the row-resident LayerNorm");
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    ln_x2_kernel<T, 32><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
+        static_cast<const T*>(x), H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs,
+        do_norm ? 1 : 0);
+  });
+  check_launch("ln_x2_kernel");
+}
+
+void launch_embed_gather(const void* table, ltm_dtype dt, int vocab, int H, const int32_t* tok,
+                         int64_t T, void* out, cudaStream_t stream) {
+  if (T == 0) return;
+  LTM_REQUIRE((H * dtype_size(dt)) % 16 == 0, "hidden size must be a multiple of 16 bytes");
+  dispatch_dtype(dt, [&](auto tag) {
+    using TT = decltype(tag);
+    embed_gather_kernel<TT><<<static_cast<unsigned>((T + 7) / 8), 256, 0, stream>>>(
+        static_cast<const TT*>(table), vocab, H, tok, T, static_cast<TT*>(out), device_error_ptr());
+  });
+  check_launch("embed_gather_kernel");
+}
+
+}  // namespace ltm_b200

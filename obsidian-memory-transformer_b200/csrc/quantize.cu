@@ -1,0 +1,266 @@
+// quantize.cu -- INT8 per-row (weights per output channel, activations per
+// token) and INT4 grouped asymmetric quantize/pack/dequantize kernels.
+//
+// Bandwidth-bound: one warp owns one row (INT8) or one 128-element group
+// (INT4); loads are 128-bit where the row layout allows, reductions are warp
+// shuffles.  Division and rounding are IEEE round-to-nearest division
+// (__fdiv_rn) followed by round-half-away-from-zero (roundf), the arithmetic
+// of the reference kernels src/core/quantization/quantizer.cu:94-142, so the
+// codes are bit-exact against a CPU evaluation of the same formula.
+#include "common.cuh"
+
+namespace ltm_b200 {
+namespace {
+
+template <class T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ int8_t quant_sym_i8(float v, float s) {
+  if (s == 0.0f) return 0;
+  float r = roundf(__fdiv_rn(v, s));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// One warp per row: s = absmax/127, q = clamp(round(x/s)).
+template <class T, bool VEC>
+__global__ void __launch_bounds__(256) rowwise_int8_kernel(const T* __restrict__ x, int64_t rows,
+                                                           int64_t K, int8_t* __restrict__ q,
+                                                           float* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * K;
+  int8_t* qr = q + row * K;
+  float amax = 0.0f;
+  if constexpr (VEC) {
+    constexpr int V = Vec16<T>::N;
+    const int64_t nv = K / V;
+    const uint4* xv = reinterpret_cast<const uint4*>(xr);
+    for (int64_t j = lane; j < nv; j += 32) {
+      uint4 raw = __ldg(xv + j);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(to_f32(e[i])));
+    }
+    amax = warp_max(amax);
+    const float s = __fdiv_rn(amax, 127.0f);
+    for (int64_t j = lane; j < nv; j += 32) {
+      uint4 raw = __ldg(xv + j);
+      const T* e = reinterpret_cast<const T*>(&raw);
+      int8_t out[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = quant_sym_i8(to_f32(e[i]), s);
+      if constexpr (V == 8) {
+        *reinterpret_cast<uint2*>(qr + j * V) = *reinterpret_cast<const uint2*>(out);
+      } else {
+        *reinterpret_cast<uint32_t*>(qr + j * V) = *reinterpret_cast<const uint32_t*>(out);
+      }
+    }
+    if (lane == 0) scales[row] = s;
+  } else {
+    for (int64_t j = lane; j < K; j += 32) amax = fmaxf(amax, fabsf(to_f32(xr[j])));
+    amax = warp_max(amax);
+    const float s = __fdiv_rn(amax, 127.0f);
+    for (int64_t j = lane; j < K; j += 32) qr[j] = quant_sym_i8(to_f32(xr[j]), s);
+    if (lane == 0) scales[row] = s;
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) dequant_int8_kernel(const int8_t* __restrict__ q,
+                                                           const float* __restrict__ s,
+                                                           int64_t N, int64_t K, T* __restrict__ out) {
+  const int64_t total = N * K;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t n = i / K;
+    out[i] = from_f32<T>(static_cast<float>(q[i]) * s[n]);
+  }
+}
+
+// One warp per (row, 128-element group); lane l owns elements 4l..4l+3.
+template <class T>
+__global__ void __launch_bounds__(256) int4_group_quant_kernel(const T* __restrict__ w, int64_t N,
+                                                               int64_t K, uint8_t* __restrict__ packed,
+                                                               float* __restrict__ scales,
+                                                               uint8_t* __restrict__ zeros) {
+  const int lane = threadIdx.x & 31;
+  const int64_t groups_per_row = K / 128;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gid >= N * groups_per_row) return;
+  const int64_t n = gid / groups_per_row;
+  const int64_t g = gid - n * groups_per_row;
+  const T* src = w + n * K + g * 128 + lane * 4;
+  float v[4];
+  if constexpr (sizeof(T) == 4) {
+    float4 t = __ldg(reinterpret_cast<const float4*>(src));
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+    uint2 raw = __ldg(reinterpret_cast<const uint2*>(src));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = to_f32(e[i]);
+  }
+  float mn = fminf(fminf(v[0], v[1]), fminf(v[2], v[3]));
+  float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+  mn = fminf(warp_min(mn), 0.0f);
+  mx = fmaxf(warp_max(mx), 0.0f);
+  const float s = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+  float zp = 0.0f;
+  uint32_t code[4] = {0, 0, 0, 0};
+  if (s != 0.0f) {
+    zp = fminf(fmaxf(roundf(__fdiv_rn(-mn, s)), 0.0f), 15.0f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float r = roundf(__fadd_rn(__fdiv_rn(v[i], s), zp));
+      r = fminf(fmaxf(r, 0.0f), 15.0f);
+      code[i] = static_cast<uint32_t>(r);
+    }
+  }
+  const uint16_t two = static_cast<uint16_t>((code[0] | (code[1] << 4)) |
+                                             ((code[2] | (code[3] << 4)) << 8));
+  *reinterpret_cast<uint16_t*>(packed + n * (K / 2) + g * 64 + lane * 2) = two;
+  if (lane == 0) {
+    scales[n * groups_per_row + g] = s;
+    zeros[n * groups_per_row + g] = static_cast<uint8_t>(zp);
+  }
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) int4_dequant_kernel(const uint8_t* __restrict__ packed,
+                                                           const float* __restrict__ s,
+                                                           const uint8_t* __restrict__ zp,
+                                                           int64_t N, int64_t K, int group,
+                                                           T* __restrict__ out) {
+  const int64_t total_bytes = N * K / 2;
+  const int64_t gpr = K / group;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total_bytes;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = 2 * i;
+    const int64_t n = e / K;
+    const int64_t k = e - n * K;
+    const int64_t gi = n * gpr + k / group;
+    const float sc = s[gi];
+    const float z = static_cast<float>(zp[gi]);
+    const uint8_t b = packed[i];
+    out[e] = from_f32<T>((static_cast<float>(b & 0xF) - z) * sc);
+    out[e + 1] = from_f32<T>((static_cast<float>(b >> 4) - z) * sc);
+  }
+}
+
+int elementwise_grid(int64_t total) {
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+  return static_cast<int>(blocks < cap ? (blocks < 1 ? 1 : blocks) : cap);
+}
+
+}  // namespace
+
+void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, int8_t* q,
+                         float* s, cudaStream_t stream) {
+  if (rows == 0 || K == 0) return;
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    const bool vec = ((K * sizeof(T)) % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
+    if (vec)
+      rowwise_int8_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
+    else
+      rowwise_int8_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
+  });
+  check_launch("rowwise_int8_kernel");
+}
+
+}  // namespace ltm_b200
+
+using namespace ltm_b200;
+
+extern "C" ltm_status ltm_quantize_int8_per_channel(const void* w, ltm_dtype w_dtype, int64_t N,
+                                                    int64_t K, int8_t* q, float* s, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(N >= 0 && K >= 0, "negative size");
+    LTM_REQUIRE((N == 0 || K == 0) || (w && q && s), "NULL pointer");
+    if (N > 0 && K == 0) {
+      LTM_CUDA_TRY(cudaMemsetAsync(s, 0, N * sizeof(float), as_stream(stream)));
+      return;
+    }
+    launch_rowwise_int8(w, w_dtype, N, K, q, s, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_quantize_act_int8_per_token(const void* a, ltm_dtype a_dtype, int64_t M,
+                                                      int64_t K, int8_t* q, float* s, void* stream) {
+  return ltm_quantize_int8_per_channel(a, a_dtype, M, K, q, s, stream);
+}
+
+extern "C" ltm_status ltm_dequantize_int8_per_channel(const int8_t* q, const float* s, int64_t N,
+                                                      int64_t K, void* out, ltm_dtype out_dtype,
+                                                      void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(N >= 0 && K >= 0, "negative size");
+    if (N == 0 || K == 0) return;
+    LTM_REQUIRE(q && s && out, "NULL pointer");
+    dispatch_dtype(out_dtype, [&](auto tag) {
+      using T = decltype(tag);
+      dequant_int8_kernel<T><<<elementwise_grid(N * K), 256, 0, as_stream(stream)>>>(
+          q, s, N, K, static_cast<T*>(out));
+    });
+    check_launch("dequant_int8_kernel");
+  });
+}
+
+extern "C" ltm_status ltm_quantize_int4_grouped(const void* w, ltm_dtype w_dtype, int64_t N,
+                                                int64_t K, int group_size, uint8_t* packed,
+                                                float* s, uint8_t* zp, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(N >= 0 && K >= 0, "negative size");
+    if (group_size != 128) LTM_UNSUPPORTED("INT4 group_size must be 128");
+    LTM_REQUIRE(K % 128 == 0, "K must be a multiple of the group size");
+    if (N == 0 || K == 0) return;
+    LTM_REQUIRE(w && packed && s && zp, "NULL pointer");
+    const int64_t groups = N * (K / 128);
+    const unsigned blocks = static_cast<unsigned>((groups + 7) / 8);
+    dispatch_dtype(w_dtype, [&](auto tag) {
+      using T = decltype(tag);
+      LTM_REQUIRE((reinterpret_cast<uintptr_t>(w) & (4 * sizeof(T) - 1)) == 0,
+                  "weight pointer misaligned for 4-element loads");
+      int4_group_quant_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const T*>(w), N, K, packed, s, zp);
+    });
+    check_launch("int4_group_quant_kernel");
+  });
+}
+
+extern "C" ltm_status ltm_dequantize_int4_grouped(const uint8_t* packed, const float* s,
+                                                  const uint8_t* zp, int64_t N, int64_t K,
+                                                  int group_size, void* out, ltm_dtype out_dtype,
+                                                  void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(N >= 0 && K >= 0, "negative size");
+    LTM_REQUIRE(group_size > 0 && group_size % 2 == 0 && K % group_size == 0,
+                "group_size must be even and divide K");
+    if (N == 0 || K == 0) return;
+    LTM_REQUIRE(packed && s && zp && out, "NULL pointer");
+    dispatch_dtype(out_dtype, [&](auto tag) {
+      using T = decltype(tag);
+      int4_dequant_kernel<T><<<elementwise_grid(N * K / 2), 256, 0, as_stream(stream)>>>(
+          packed, s, zp, N, K, group_size, static_cast<T*>(out));
+    });
+    check_launch("int4_dequant_kernel");
+  });
+}

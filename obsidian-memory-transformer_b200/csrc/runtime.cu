@@ -1,0 +1,111 @@
+// runtime.cu -- error strings, device error word, device properties and the
+// TMA descriptor encoder (driver entry point resolved through the runtime, so
+// the library needs no link-time dependency on libcuda).
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace ltm_b200 {
+
+__device__ int g_device_error = 0;
+
+int* device_error_ptr() {
+  static std::mutex mu;
+  static std::vector<int*> cache;
+  int dev = 0;
+  LTM_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    LTM_CUDA_TRY(cudaGetSymbolAddress(&p, g_device_error));
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+void clear_error() { t_last_error.clear(); }
+
+int device_sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  LTM_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    LTM_CUDA_TRY(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    throw Fail{LTM_ERR_CUDA};
+  }
+  return fn;
+}
+}  // namespace
+
+void make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                 uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols,
+                 uint32_t box_rows) {
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  LTM_REQUIRE((row_stride_elems * elem_bytes) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  LTM_REQUIRE(box_cols * elem_bytes <= 128, "TMA box inner extent exceeds the 128-byte swizzle");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));
+    throw Fail{LTM_ERR_CUDA};
+  }
+}
+
+}  // namespace ltm_b200
+
+using namespace ltm_b200;
+
+extern "C" const char* ltm_version(void) { return "ltm_b200 0.1.0 (sm_100a)"; }
+
+extern "C" const char* ltm_last_error_string(void) { return t_last_error.c_str(); }
+
+extern "C" ltm_status ltm_device_error(int* code_out) {
+  return guarded([&] {
+    LTM_REQUIRE(code_out != nullptr, "code_out is NULL");
+    int zero = 0, v = 0;
+    LTM_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+    LTM_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+    *code_out = v;
+  });
+}

@@ -1,0 +1,417 @@
+"""Python caller of the B200 Titan-block C ABI (libltm_b200.so).
+
+This module plays the role the reference's pybind module `_ltm`
+(python_bindings/src/main.cpp:206-269) plays for its C++ library: it exposes
+`TitanBlockConfig` with the same fields and defaults, a `TitanBlock` /
+`TitanModel` pair, and the INT8/INT4 quantize, dequantize and quantized
+linear entry points.  Every call goes through the C ABI declared in
+include/ltm_b200.h; PyTorch only provides device memory and streams.
+There is no CPU fallback: without the built library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libltm_b200.so"
+
+# ltm_status
+OK, ERR_INVALID_ARG, ERR_CUDA, ERR_COMM, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_NO_DEVICE = range(7)
+# ltm_dtype
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+# ltm_epilogue
+EPI_NONE, EPI_GELU, EPI_SIGMOID = 0, 1, 2
+# ltm_scheme
+SCHEME_W8A32, SCHEME_W8A8, SCHEME_W4A16 = 0, 1, 2
+
+
+class LtmError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"ltm_b200 status {status}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+class BlockConfigC(C.Structure):
+    _fields_ = [
+        ("hidden_dim", C.c_int), ("ffn_dim", C.c_int), ("num_heads", C.c_int),
+        ("head_dim", C.c_int), ("memory_slots", C.c_int), ("memory_dim", C.c_int),
+        ("memory_update_rate", C.c_float), ("use_memory_compression", C.c_int),
+        ("memory_compression_ratio", C.c_float), ("use_flash_attention", C.c_int),
+        ("use_alibi", C.c_int), ("use_rotary", C.c_int), ("dropout_prob", C.c_float),
+        ("use_parallel_attention", C.c_int), ("use_memory_gating", C.c_int),
+        ("use_layer_norm", C.c_int), ("use_bias", C.c_int), ("fuse_operations", C.c_int),
+        ("learn_memory", C.c_int), ("learn_compression", C.c_int),
+        ("gradient_checkpointing", C.c_int),
+    ]
+
+
+class QuantConfigC(C.Structure):
+    _fields_ = [("scheme", C.c_int), ("group_size", C.c_int), ("act_dtype", C.c_int),
+                ("memory_write", C.c_int), ("use_attention_scores", C.c_int)]
+
+
+WEIGHT_FIELDS = ("w_qkv", "b_qkv", "w_o", "b_o", "w_qm", "b_qm", "w_km", "b_km", "w_vm", "b_vm",
+                 "w_om", "b_om", "w_g", "b_g", "w_1", "b_1", "w_2", "b_2", "ln1_g", "ln1_b",
+                 "ln2_g", "ln2_b", "memory")
+
+
+class BlockWeightsC(C.Structure):
+    _fields_ = [(n, C.POINTER(C.c_float)) for n in WEIGHT_FIELDS]
+
+
+def _declare(L):
+    vp, i64, ci = C.c_void_p, C.c_int64, C.c_int
+    sig = {
+        "ltm_version": ([], C.c_char_p),
+        "ltm_last_error_string": ([], C.c_char_p),
+        "ltm_device_error": ([C.POINTER(C.c_int)], ci),
+        "ltm_quantize_int8_per_channel": ([vp, ci, i64, i64, vp, vp, vp], ci),
+        "ltm_dequantize_int8_per_channel": ([vp, vp, i64, i64, vp, ci, vp], ci),
+        "ltm_quantize_act_int8_per_token": ([vp, ci, i64, i64, vp, vp, vp], ci),
+        "ltm_quantize_int4_grouped": ([vp, ci, i64, i64, ci, vp, vp, vp, vp], ci),
+        "ltm_dequantize_int4_grouped": ([vp, vp, vp, i64, i64, ci, vp, ci, vp], ci),
+        "ltm_linear_w8a8": ([vp, vp, vp, vp, vp, ci, vp, ci, i64, i64, i64, vp], ci),
+        "ltm_linear_w8a8_acc_i32": ([vp, vp, vp, i64, i64, i64, vp], ci),
+        "ltm_linear_w4a16": ([vp, ci, vp, vp, vp, vp, ci, vp, i64, i64, i64, vp], ci),
+        "ltm_linear_w8a32": ([vp, vp, vp, vp, ci, vp, i64, i64, i64, vp], ci),
+        "ltm_block_config_default": ([C.POINTER(BlockConfigC)], None),
+        "ltm_block_create": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), ci,
+                              C.POINTER(vp)], ci),
+        "ltm_block_load_weights": ([vp, C.POINTER(BlockWeightsC)], ci),
+        "ltm_block_forward": ([vp, vp, vp, vp, ci, ci, vp], ci),
+        "ltm_block_get_memory": ([vp, vp, vp], ci),
+        "ltm_block_destroy": ([vp], ci),
+        "ltm_model_create": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), ci, ci, ci,
+                              C.POINTER(vp)], ci),
+        "ltm_model_load_embedding": ([vp, vp], ci),
+        "ltm_model_load_layer": ([vp, ci, C.POINTER(BlockWeightsC)], ci),
+        "ltm_model_forward": ([vp, vp, vp, ci, ci, vp], ci),
+        "ltm_model_destroy": ([vp], ci),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+
+
+def lib() -> C.CDLL:
+    """The loaded C-ABI library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with "
+                               "`python obsidian-memory-transformer_b200/build.py`")
+        _lib = C.CDLL(str(LIB_PATH))
+        _declare(_lib)
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        msg = lib().ltm_last_error_string().decode(errors="replace")
+        raise LtmError(status, msg)
+
+
+def version() -> str:
+    return lib().ltm_version().decode()
+
+
+def device_error() -> int:
+    code = C.c_int(0)
+    _check(lib().ltm_device_error(C.byref(code)))
+    return code.value
+
+
+# ---------------------------------------------------------------- torch glue --
+def _torch():
+    import torch  # noqa: WPS433
+    return torch
+
+
+def dtype_code(t) -> int:
+    torch = _torch()
+    return {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}[t]
+
+
+def torch_dtype(code: int):
+    torch = _torch()
+    return {DTYPE_F32: torch.float32, DTYPE_F16: torch.float16, DTYPE_BF16: torch.bfloat16}[code]
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    torch = _torch()
+    s = torch.cuda.current_stream() if stream is None else stream
+    return C.c_void_p(s.cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise ValueError("ltm_b200 operates on CUDA tensors only")
+            if not t.is_contiguous():
+                raise ValueError("ltm_b200 expects contiguous tensors")
+
+
+# -------------------------------------------------------------- quantization --
+def quantize_int8_per_channel(w, stream=None):
+    """w [N,K] (f32/f16/bf16) -> (q int8 [N,K], s f32 [N])."""
+    torch = _torch()
+    _need_cuda(w)
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    s = torch.empty((N,), dtype=torch.float32, device=w.device)
+    _check(lib().ltm_quantize_int8_per_channel(_ptr(w), dtype_code(w.dtype), N, K, _ptr(q), _ptr(s),
+                                               _stream(stream)))
+    return q, s
+
+
+def quantize_act_int8_per_token(a, stream=None):
+    torch = _torch()
+    _need_cuda(a)
+    M, K = a.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=a.device)
+    s = torch.empty((M,), dtype=torch.float32, device=a.device)
+    _check(lib().ltm_quantize_act_int8_per_token(_ptr(a), dtype_code(a.dtype), M, K, _ptr(q),
+                                                 _ptr(s), _stream(stream)))
+    return q, s
+
+
+def dequantize_int8_per_channel(q, s, dtype=None, stream=None):
+    torch = _torch()
+    _need_cuda(q, s)
+    dtype = dtype or torch.float32
+    out = torch.empty(q.shape, dtype=dtype, device=q.device)
+    _check(lib().ltm_dequantize_int8_per_channel(_ptr(q), _ptr(s), q.shape[0], q.shape[1],
+                                                 _ptr(out), dtype_code(dtype), _stream(stream)))
+    return out
+
+
+def quantize_int4_grouped(w, group_size: int = 128, stream=None):
+    """w [N,K] -> (packed uint8 [N,K/2], s f32 [N,K/g], zp uint8 [N,K/g])."""
+    torch = _torch()
+    _need_cuda(w)
+    N, K = w.shape
+    packed = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
+    s = torch.empty((N, K // group_size), dtype=torch.float32, device=w.device)
+    zp = torch.empty((N, K // group_size), dtype=torch.uint8, device=w.device)
+    _check(lib().ltm_quantize_int4_grouped(_ptr(w), dtype_code(w.dtype), N, K, group_size,
+                                           _ptr(packed), _ptr(s), _ptr(zp), _stream(stream)))
+    return packed, s, zp
+
+
+def dequantize_int4_grouped(packed, s, zp, group_size: int = 128, dtype=None, stream=None):
+    torch = _torch()
+    _need_cuda(packed, s, zp)
+    dtype = dtype or torch.float32
+    N, K = packed.shape[0], packed.shape[1] * 2
+    out = torch.empty((N, K), dtype=dtype, device=packed.device)
+    _check(lib().ltm_dequantize_int4_grouped(_ptr(packed), _ptr(s), _ptr(zp), N, K, group_size,
+                                             _ptr(out), dtype_code(dtype), _stream(stream)))
+    return out
+
+
+# ------------------------------------------------------------------- linears --
+def linear_w8a8(qa, sa, qw, sw, bias=None, act: int = EPI_NONE, out_dtype=None, stream=None):
+    torch = _torch()
+    _need_cuda(qa, sa, qw, sw, bias)
+    out_dtype = out_dtype or torch.float16
+    M, K = qa.shape
+    N = qw.shape[0]
+    y = torch.empty((M, N), dtype=out_dtype, device=qa.device)
+    _check(lib().ltm_linear_w8a8(_ptr(qa), _ptr(sa), _ptr(qw), _ptr(sw), _ptr(bias), act, _ptr(y),
+                                 dtype_code(out_dtype), M, N, K, _stream(stream)))
+    return y
+
+
+def linear_w8a8_acc_i32(qa, qw, stream=None):
+    torch = _torch()
+    _need_cuda(qa, qw)
+    M, K = qa.shape
+    N = qw.shape[0]
+    acc = torch.empty((M, N), dtype=torch.int32, device=qa.device)
+    _check(lib().ltm_linear_w8a8_acc_i32(_ptr(qa), _ptr(qw), _ptr(acc), M, N, K, _stream(stream)))
+    return acc
+
+
+def linear_w4a16(a, packed, s, zp, bias=None, act: int = EPI_NONE, stream=None):
+    torch = _torch()
+    _need_cuda(a, packed, s, zp, bias)
+    M, K = a.shape
+    N = packed.shape[0]
+    y = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    _check(lib().ltm_linear_w4a16(_ptr(a), dtype_code(a.dtype), _ptr(packed), _ptr(s), _ptr(zp),
+                                  _ptr(bias), act, _ptr(y), M, N, K, _stream(stream)))
+    return y
+
+
+def linear_w8a32(a, qw, sw, bias=None, act: int = EPI_NONE, stream=None):
+    torch = _torch()
+    _need_cuda(a, qw, sw, bias)
+    M, K = a.shape
+    N = qw.shape[0]
+    y = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    _check(lib().ltm_linear_w8a32(_ptr(a), _ptr(qw), _ptr(sw), _ptr(bias), act, _ptr(y), M, N, K,
+                                  _stream(stream)))
+    return y
+
+
+# --------------------------------------------------------------------- block --
+@dataclasses.dataclass
+class TitanBlockConfig:
+    """Field-for-field mirror of ltm::transformer::TitanBlockConfig
+    (include/core/transformer/titan_inspired_block.cuh:19-50)."""
+    hidden_dim: int = 768
+    ffn_dim: int = 3072
+    num_heads: int = 12
+    head_dim: int = 64
+    memory_slots: int = 512
+    memory_dim: int = 64
+    memory_update_rate: float = 0.9
+    use_memory_compression: bool = True
+    memory_compression_ratio: float = 0.5
+    use_flash_attention: bool = True
+    use_alibi: bool = False
+    use_rotary: bool = True
+    dropout_prob: float = 0.1
+    use_parallel_attention: bool = True
+    use_memory_gating: bool = True
+    use_layer_norm: bool = True
+    use_bias: bool = True
+    fuse_operations: bool = True
+    learn_memory: bool = True
+    learn_compression: bool = True
+    gradient_checkpointing: bool = True
+
+    def to_c(self) -> BlockConfigC:
+        c = BlockConfigC()
+        for f in dataclasses.fields(self):
+            v = getattr(self, f.name)
+            setattr(c, f.name, int(v) if isinstance(v, bool) else v)
+        return c
+
+
+@dataclasses.dataclass
+class QuantConfig:
+    scheme: int = SCHEME_W8A8
+    group_size: int = 128
+    act_dtype: int = DTYPE_F16
+    memory_write: bool = False
+    use_attention_scores: bool = True
+
+    def to_c(self) -> QuantConfigC:
+        return QuantConfigC(self.scheme, self.group_size, self.act_dtype, int(self.memory_write),
+                            int(self.use_attention_scores))
+
+
+def _weights_c(w: dict):
+    keep = {n: np.ascontiguousarray(w[n], dtype=np.float32) for n in WEIGHT_FIELDS
+            if w.get(n) is not None}
+    st = BlockWeightsC(*[keep[n].ctypes.data_as(C.POINTER(C.c_float)) if n in keep else None
+                         for n in WEIGHT_FIELDS])
+    return st, keep
+
+
+class TitanBlock:
+    """ltm::transformer::TitanBlock<T> over the C ABI (T = act dtype)."""
+
+    def __init__(self, config: TitanBlockConfig, quant: QuantConfig | None = None, device: int = 0):
+        self.config = config
+        self.quant = quant or QuantConfig()
+        self.device = device
+        h = C.c_void_p()
+        _check(lib().ltm_block_create(C.byref(config.to_c()), C.byref(self.quant.to_c()), device,
+                                      C.byref(h)))
+        self._h = h
+
+    def load_weights(self, w: dict) -> None:
+        st, keep = _weights_c(w)
+        _check(lib().ltm_block_load_weights(self._h, C.byref(st)))
+        del keep
+
+    def forward(self, x, attention_mask=None, stream=None):
+        """x: CUDA tensor [B,S,H] in the act dtype -> y of the same shape."""
+        torch = _torch()
+        _need_cuda(x)
+        B, S, H = x.shape
+        y = torch.empty_like(x)
+        _check(lib().ltm_block_forward(self._h, _ptr(x), _ptr(y), _ptr(attention_mask), B, S,
+                                       _stream(stream)))
+        return y
+
+    __call__ = forward
+
+    def memory(self, stream=None):
+        torch = _torch()
+        out = torch.empty((self.config.memory_slots, self.config.hidden_dim),
+                          dtype=torch_dtype(self.quant.act_dtype), device=f"cuda:{self.device}")
+        _check(lib().ltm_block_get_memory(self._h, _ptr(out), _stream(stream)))
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().ltm_block_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+class TitanModel:
+    """Embedding gather + n Titan blocks (TitanModel.forward without the LM head)."""
+
+    def __init__(self, config: TitanBlockConfig, quant: QuantConfig, n_layers: int,
+                 vocab_size: int, device: int = 0):
+        self.config, self.quant, self.n_layers, self.vocab = config, quant, n_layers, vocab_size
+        self.device = device
+        h = C.c_void_p()
+        _check(lib().ltm_model_create(C.byref(config.to_c()), C.byref(quant.to_c()), n_layers,
+                                      vocab_size, device, C.byref(h)))
+        self._h = h
+
+    def load_embedding(self, emb: np.ndarray) -> None:
+        e = np.ascontiguousarray(emb, dtype=np.float32)
+        _check(lib().ltm_model_load_embedding(self._h, C.c_void_p(e.ctypes.data)))
+
+    def load_layer(self, i: int, w: dict) -> None:
+        st, keep = _weights_c(w)
+        _check(lib().ltm_model_load_layer(self._h, i, C.byref(st)))
+        del keep
+
+    def forward(self, tokens, out=None, stream=None):
+        """tokens: CUDA int32 [B,S] -> hidden [B,S,H] (act dtype)."""
+        torch = _torch()
+        _need_cuda(tokens)
+        B, S = tokens.shape
+        if out is None:
+            out = torch.empty((B, S, self.config.hidden_dim), dtype=torch_dtype(self.quant.act_dtype),
+                              device=tokens.device)
+        _check(lib().ltm_model_forward(self._h, _ptr(tokens), _ptr(out), B, S, _stream(stream)))
+        return out
+
+    __call__ = forward
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().ltm_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
