@@ -144,6 +144,29 @@ LTM_API ltm_status ltm_linear_w8a32(const float* a, const int8_t* qw, const floa
                             ltm_epilogue act, float* y, int64_t M, int64_t N, int64_t K,
                             void* stream);
 
+/* ------------------------------------------------------------------- ops -- */
+/* y = LN(x + r) * gamma + beta over rows of H, eps 1e-5, two-pass mean /
+ * variance; replaces ops::layerNormResidual (src/core/ops/fused_ops.cu:15-86,
+ * 233-259).  TitanBlock::layerNorm passes r = x
+ * (src/core/transformer/titan_inspired_block.cu:374-389).  gamma, beta: fp32 [H]. */
+LTM_API ltm_status ltm_layernorm_residual(const void* x, const void* r, const float* gamma,
+                                          const float* beta, void* y, ltm_dtype dtype,
+                                          int64_t rows, int64_t H, void* stream);
+
+/* o = softmax(q k^T / sqrt(head_dim)) v per head, fp32 softmax and accumulation;
+ * the attention core of FlashAttention<T>::forward
+ * (src/core/attention/flash_attention.cu:188-268,380-445; TB-v1 adds the max
+ * subtraction and the causal mask) and of MemoryAttention<T>::forward
+ * (src/core/attention/memory_attention.cu:38-88,416-510: queries x memory slots).
+ * Rows are head-sliced: query t of batch b, head h is q[(b*Sq + t)*ldq + h*head_dim ..];
+ * key j is k[(b*kv_batch_rows + j)*ldk + h*head_dim ..] (kv_batch_rows = 0 shares
+ * K/V across the batch, as the memory bank does); same for v / ldv and o / ldo.
+ * causal: key j is visible to query t iff j <= t + (Skv - Sq).  head_dim 64 or 128. */
+LTM_API ltm_status ltm_attention_forward(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                                         const void* v, int64_t ldv, void* o, int64_t ldo, int B,
+                                         int Sq, int Skv, int64_t kv_batch_rows, int num_heads,
+                                         int head_dim, int causal, ltm_dtype dtype, void* stream);
+
 /* ----------------------------------------------------------------- block -- */
 /* Field-for-field mirror of ltm::transformer::TitanBlockConfig
  * (include/core/transformer/titan_inspired_block.cuh:19-50): same names, same

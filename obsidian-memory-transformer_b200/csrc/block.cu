@@ -1,7 +1,454 @@
-// block.cu -- Titan block / model orchestration over the kernels (C ABI).
-#include "common.cuh"
+// block.cu -- Titan block and multi-layer model over the kernels (C ABI).
+//
+// TB-v1 block forward (x, y: [B*S, H] in the activation dtype):
+//   h   = LN(x + x)                      (+ per-token int8 of h and of x for W8A8)
+//   qkvm= h [Wq;Wk;Wv;Wqm]^T + b         RoPE on the Q and K columns in the epilogue
+//   kvm = M [Wkm;Wvm]^T + b              memory keys / values from the bank M [Ms,H]
+//   os  = causal_attn(q, k, v)           om = attn(qm, K_M, V_M)   (bank shared by the batch)
+//   s   = os Wo^T + bo                   m  = om Wom^T + bom
+//   y   = s + g*m + (1-g)*x,  g = sigmoid(x Wg^T + bg)   (gate-mix epilogue of the gate GEMM)
+//   out = y + W2 GELU(W1 LN(y + y) + b1) + b2            (residual epilogue of the FFN-down GEMM)
+// with the memory write after the read (optional, see memory.cu).
+// Reference: TitanBlock<T>::forward, src/core/transformer/titan_inspired_block.cu:254-345.
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "block.cuh"
+
+namespace ltm_b200 {
+
+// ------------------------------------------------------------ device memory --
+DevBuf::~DevBuf() { release(); }
+void DevBuf::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+void DevBuf::ensure(size_t n) {
+  if (n <= bytes) return;
+  release();
+  LTM_CUDA_TRY(cudaMalloc(&ptr, n));
+  bytes = n;
+}
+
+namespace {
+
+template <class T>
+__global__ void f32_to_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = from_f32<T>(src[i]);
+}
+
+template <class T>
+__global__ void add3_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                            const T* __restrict__ c, T* __restrict__ y, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = from_f32<T>(to_f32(a[i]) + to_f32(b[i]) + to_f32(c[i]));
+}
+
+int grid_for(int64_t n) {
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+  int64_t g = (n + 255) / 256;
+  return static_cast<int>(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+}  // namespace
+
+void upload_f32_as(const float* host, int64_t n, ltm_dtype dt, void* dev, cudaStream_t stream) {
+  if (n == 0) return;
+  if (dt == LTM_DTYPE_F32) {
+    LTM_CUDA_TRY(cudaMemcpyAsync(dev, host, n * sizeof(float), cudaMemcpyHostToDevice, stream));
+    return;
+  }
+  DevBuf tmp;
+  tmp.ensure(n * sizeof(float));
+  LTM_CUDA_TRY(cudaMemcpyAsync(tmp.ptr, host, n * sizeof(float), cudaMemcpyHostToDevice, stream));
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    f32_to_kernel<T><<<grid_for(n), 256, 0, stream>>>(static_cast<const float*>(tmp.ptr),
+                                                      static_cast<T*>(dev), n);
+  });
+  check_launch("f32_to_kernel");
+  LTM_CUDA_TRY(cudaStreamSynchronize(stream));
+}
+
+void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n, ltm_dtype dt,
+                 cudaStream_t stream) {
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    add3_kernel<T><<<grid_for(n), 256, 0, stream>>>(static_cast<const T*>(a), static_cast<const T*>(b),
+                                                    static_cast<const T*>(c), static_cast<T*>(y), n);
+  });
+  check_launch("add3_kernel");
+}
+
+// ------------------------------------------------------------ quantized W --
+void QLinear::load(const ltm_quant_config& q, const float* w_host, const float* b_host,
+                   int64_t n, int64_t k, cudaStream_t stream) {
+  N = n;
+  K = k;
+  scheme = q.scheme;
+  DevBuf wd;
+  wd.ensure(N * K * sizeof(float));
+  LTM_CUDA_TRY(cudaMemcpyAsync(wd.ptr, w_host, N * K * sizeof(float), cudaMemcpyHostToDevice, stream));
+  if (scheme == LTM_SCHEME_W4A16) {
+    if (K % 128 != 0) LTM_UNSUPPORTED("W4A16 needs the input width to be a multiple of 128");
+    q4.ensure(N * K / 2);
+    s4.ensure(N * (K / 128) * sizeof(float));
+    z4.ensure(N * (K / 128));
+    LTM_REQUIRE(ltm_quantize_int4_grouped(wd.ptr, LTM_DTYPE_F32, N, K, 128, q4.as<uint8_t>(),
+                                          s4.as<float>(), z4.as<uint8_t>(), stream) == LTM_OK,
+                "int4 weight quantization failed");
+  } else {
+    q8.ensure(N * K);
+    s8.ensure(N * sizeof(float));
+    launch_rowwise_int8(wd.ptr, LTM_DTYPE_F32, N, K, q8.as<int8_t>(), s8.as<float>(), stream);
+  }
+  if (b_host) {
+    bias.ensure(N * sizeof(float));
+    LTM_CUDA_TRY(cudaMemcpyAsync(bias.ptr, b_host, N * sizeof(float), cudaMemcpyHostToDevice, stream));
+  } else {
+    bias.release();
+  }
+  LTM_CUDA_TRY(cudaStreamSynchronize(stream));
+}
+
+// Runs y = epilogue(a W^T) for the block's scheme.  a_act: activation in the
+// act dtype (W8A32 / W4A16); aq/as: its per-token int8 codes (W8A8).
+void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode,
+                  ltm_dtype dt, Epilogue ep, cudaStream_t stream) const {
+  ep.bias = bias.as<float>();
+  if (scheme == LTM_SCHEME_W8A8) {
+    ep.row_scale = as;
+    ep.col_scale = s8.as<float>();
+    launch_w8a8(aq, q8.as<int8_t>(), M, N, K, mode, dt, ep, stream);
+  } else if (scheme == LTM_SCHEME_W8A32) {
+    ep.row_scale = nullptr;
+    ep.col_scale = s8.as<float>();
+    launch_w8a32(static_cast<const float*>(a_act), q8.as<int8_t>(), M, N, K, mode, ep, stream);
+  } else {
+    ep.row_scale = nullptr;
+    ep.col_scale = nullptr;
+    launch_w4a16(a_act, dt, q4.as<uint8_t>(), s4.as<float>(), z4.as<uint8_t>(), M, N, K, mode, ep,
+                 stream);
+  }
+}
+
+}  // namespace ltm_b200
 
 using namespace ltm_b200;
+
+// ---------------------------------------------------------------- the block --
+struct ltm_block {
+  ltm_block_config cfg{};
+  ltm_quant_config q{};
+  int device = 0;
+  int H = 0, F = 0, nh = 0, dh = 0, Ms = 0;
+  ltm_dtype dt = LTM_DTYPE_F16;
+  bool loaded = false;
+  QLinear qkvm, kvm, o, om, g, w1, w2;
+  DevBuf ln1_g, ln1_b, ln2_g, ln2_b;
+  DevBuf memory;  // [Ms, H] act dtype
+  DevBuf rope;    // [rope_S, dh/2] float2
+  int rope_S = 0;
+  // workspace
+  int64_t ws_T = 0;
+  DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, sp, mp, y, zq, zs, z,
+      u, uq, us;
+  MemoryWriteState mw;
+
+  size_t act_bytes() const { return dtype_size(dt); }
+
+  void ensure_rope(int S) {
+    if (S <= rope_S) return;
+    const int half = dh / 2;
+    std::vector<float> tab(static_cast<size_t>(S) * dh);
+    for (int p = 0; p < S; ++p)
+      for (int i = 0; i < half; ++i) {
+        const float inv = 1.0f / powf(10000.0f, (2.0f * static_cast<float>(i)) / static_cast<float>(dh));
+        const float th = static_cast<float>(p) * inv;
+        tab[2 * (static_cast<size_t>(p) * half + i)] = static_cast<float>(std::cos(static_cast<double>(th)));
+        tab[2 * (static_cast<size_t>(p) * half + i) + 1] = static_cast<float>(std::sin(static_cast<double>(th)));
+      }
+    rope.ensure(tab.size() * sizeof(float));
+    LTM_CUDA_TRY(cudaMemcpy(rope.ptr, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice));
+    rope_S = S;
+  }
+
+  void ensure_ws(int64_t T) {
+    if (T <= ws_T) return;
+    const size_t a = act_bytes();
+    const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
+    if (w8a8) {
+      hq.ensure(T * H);
+      hs.ensure(T * 4);
+      xq.ensure(T * H);
+      xs.ensure(T * 4);
+      osq.ensure(T * H);
+      oss.ensure(T * 4);
+      omq.ensure(T * H);
+      oms.ensure(T * 4);
+      zq.ensure(T * H);
+      zs.ensure(T * 4);
+      uq.ensure(T * F);
+      us.ensure(T * 4);
+    } else {
+      h.ensure(T * H * a);
+      z.ensure(T * H * a);
+    }
+    qkv.ensure(T * 4 * H * a);
+    os.ensure(T * H * a);
+    om_.ensure(T * H * a);
+    sp.ensure(T * H * a);
+    mp.ensure(T * H * a);
+    y.ensure(T * H * a);
+    u.ensure(T * F * a);
+    ws_T = T;
+  }
+
+  void forward(const void* x, void* out, int B, int S, cudaStream_t st) {
+    const int64_t T = static_cast<int64_t>(B) * S;
+    ensure_ws(T);
+    if (cfg.use_rotary) ensure_rope(S);
+    const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
+
+    // 1. LN1 (+ per-token int8 of LN1(x) and of x for W8A8)
+    if (w8a8) {
+      launch_ln_x2(x, dt, T, H, ln1_g.as<float>(), ln1_b.as<float>(), nullptr, hq.as<int8_t>(),
+                   hs.as<float>(), xq.as<int8_t>(), xs.as<float>(), cfg.use_layer_norm != 0, st);
+    } else if (cfg.use_layer_norm) {
+      launch_ln_x2(x, dt, T, H, ln1_g.as<float>(), ln1_b.as<float>(), h.ptr, nullptr, nullptr,
+                   nullptr, nullptr, true, st);
+    }
+    const void* hin = (w8a8 || cfg.use_layer_norm) ? h.ptr : x;
+
+    // 2. memory keys / values from the bank
+    if (w8a8) launch_rowwise_int8(memory.ptr, dt, Ms, H, mq.as<int8_t>(), ms.as<float>(), st);
+    {
+      Epilogue ep;
+      ep.out = kvmb.ptr;
+      ep.ldo = 2 * H;
+      kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st);
+    }
+    // 3. fused Q | K | V | Qm projection with RoPE on Q, K
+    {
+      Epilogue ep;
+      ep.out = qkv.ptr;
+      ep.ldo = 4 * H;
+      ep.rope = rope.as<float2>();
+      ep.rope_cols = cfg.use_rotary ? 2 * H : 0;
+      ep.seq_len = S;
+      ep.head_dim = dh;
+      qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
+               ep, st);
+    }
+    // 4. causal self-attention, memory attention
+    {
+      const size_t a = act_bytes();
+      AttnParams p{};
+      p.q = qkv.ptr;
+      p.k = static_cast<const char*>(qkv.ptr) + H * a;
+      p.v = static_cast<const char*>(qkv.ptr) + 2 * H * a;
+      p.o = os.ptr;
+      p.ldq = p.ldk = p.ldv = 4 * H;
+      p.ldo = H;
+      p.q_batch_rows = S;
+      p.kv_batch_rows = S;
+      p.Sq = S;
+      p.Skv = S;
+      p.nh = nh;
+      p.causal_offset = 0;
+      launch_attention(p, B, dh, true, dt, st);
+      AttnParams pm = p;
+      pm.q = static_cast<const char*>(qkv.ptr) + 3 * H * a;
+      pm.k = kvmb.ptr;
+      pm.v = static_cast<const char*>(kvmb.ptr) + H * a;
+      pm.o = om_.ptr;
+      pm.ldk = pm.ldv = 2 * H;
+      pm.kv_batch_rows = 0;
+      pm.Skv = Ms;
+      launch_attention(pm, B, dh, false, dt, st);
+    }
+    // 5. output projections
+    if (w8a8) {
+      launch_rowwise_int8(os.ptr, dt, T, H, osq.as<int8_t>(), oss.as<float>(), st);
+      launch_rowwise_int8(om_.ptr, dt, T, H, omq.as<int8_t>(), oms.as<float>(), st);
+    }
+    {
+      Epilogue ep;
+      ep.out = sp.ptr;
+      ep.ldo = H;
+      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st);
+      ep.out = mp.ptr;
+      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st);
+    }
+    // 6. gated memory integration
+    if (cfg.use_memory_gating) {
+      Epilogue ep;
+      ep.act = LTM_EPI_SIGMOID;
+      ep.out = y.ptr;
+      ep.ldo = H;
+      ep.aux0 = sp.ptr;
+      ep.aux1 = mp.ptr;
+      ep.aux2 = x;
+      ep.ld_aux = H;
+      if (q.memory_write) mw.prepare_gate_epilogue(ep, H, st);
+      g.run(x, xq.as<int8_t>(), xs.as<float>(), T, kEpiGateMix, dt, ep, st);
+    } else {
+      launch_add3(sp.ptr, mp.ptr, x, y.ptr, T * H, dt, st);
+    }
+    // 7. FFN with residual
+    if (w8a8) {
+      launch_ln_x2(y.ptr, dt, T, H, ln2_g.as<float>(), ln2_b.as<float>(), nullptr, zq.as<int8_t>(),
+                   zs.as<float>(), nullptr, nullptr, cfg.use_layer_norm != 0, st);
+    } else if (cfg.use_layer_norm) {
+      launch_ln_x2(y.ptr, dt, T, H, ln2_g.as<float>(), ln2_b.as<float>(), z.ptr, nullptr, nullptr,
+                   nullptr, nullptr, true, st);
+    }
+    const void* zin = (w8a8 || cfg.use_layer_norm) ? z.ptr : y.ptr;
+    {
+      Epilogue ep;
+      ep.act = LTM_EPI_GELU;
+      ep.out = u.ptr;
+      ep.ldo = F;
+      w1.run(zin, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st);
+    }
+    if (w8a8) launch_rowwise_int8(u.ptr, dt, T, F, uq.as<int8_t>(), us.as<float>(), st);
+    {
+      Epilogue ep;
+      ep.out = out;
+      ep.ldo = H;
+      ep.aux0 = y.ptr;
+      ep.ld_aux = H;
+      w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, kEpiResid, dt, ep, st);
+    }
+    // 8. memory write after the read
+    if (q.memory_write && cfg.use_memory_gating) {
+      const size_t a = act_bytes();
+      mw.update_bank(memory.ptr, kvmb.ptr, static_cast<const char*>(qkv.ptr) + 3 * H * a, 4 * H, T,
+                     H, nh, dh, Ms, cfg.memory_update_rate, q.use_attention_scores != 0, dt, st);
+    }
+  }
+};
+
+namespace {
+
+void validate(const ltm_block_config& c, const ltm_quant_config& q) {
+  LTM_REQUIRE(c.hidden_dim > 0 && c.ffn_dim > 0 && c.num_heads > 0 && c.head_dim > 0 &&
+                  c.memory_slots > 0,
+              "block dimensions must be positive");
+  LTM_REQUIRE(c.num_heads * c.head_dim == c.hidden_dim, "num_heads * head_dim must equal hidden_dim");
+  if (c.head_dim != 64 && c.head_dim != 128) LTM_UNSUPPORTED("head_dim must be 64 or 128");
+  LTM_REQUIRE(c.hidden_dim % 32 == 0 && c.ffn_dim % 32 == 0,
+              "hidden_dim and ffn_dim must be multiples of 32");
+  if (c.use_alibi) LTM_UNSUPPORTED("ALiBi position bias");
+  switch (q.scheme) {
+    case LTM_SCHEME_W8A32:
+      LTM_REQUIRE(q.act_dtype == LTM_DTYPE_F32, "W8A32 computes in fp32 activations");
+      break;
+    case LTM_SCHEME_W8A8:
+    case LTM_SCHEME_W4A16:
+      LTM_REQUIRE(q.act_dtype == LTM_DTYPE_F16 || q.act_dtype == LTM_DTYPE_BF16,
+                  "W8A8 / W4A16 compute in f16 or bf16 activations");
+      break;
+    default: LTM_REQUIRE(false, "unknown quantization scheme");
+  }
+  if (q.scheme == LTM_SCHEME_W4A16) {
+    LTM_REQUIRE(q.group_size == 128, "W4A16 group size must be 128");
+    LTM_REQUIRE(c.hidden_dim % 128 == 0 && c.ffn_dim % 128 == 0,
+                "W4A16 needs hidden_dim and ffn_dim multiples of 128");
+  }
+}
+
+std::vector<float> cat_rows(const float* a, int64_t na, const float* b, int64_t nb, int64_t k) {
+  std::vector<float> r(static_cast<size_t>((na + nb) * k));
+  std::memcpy(r.data(), a, sizeof(float) * na * k);
+  std::memcpy(r.data() + na * k, b, sizeof(float) * nb * k);
+  return r;
+}
+
+void load_block(ltm_block* b, const ltm_block_weights* w, cudaStream_t st) {
+  const int H = b->H, F = b->F;
+  const bool ub = b->cfg.use_bias != 0;
+  LTM_REQUIRE(w && w->w_qkv && w->w_o && w->w_qm && w->w_km && w->w_vm && w->w_om && w->w_g &&
+                  w->w_1 && w->w_2 && w->memory,
+              "missing weight");
+  if (ub)
+    LTM_REQUIRE(w->b_qkv && w->b_o && w->b_qm && w->b_km && w->b_vm && w->b_om && w->b_g && w->b_1 &&
+                    w->b_2,
+                "missing bias");
+  if (b->cfg.use_layer_norm)
+    LTM_REQUIRE(w->ln1_g && w->ln1_b && w->ln2_g && w->ln2_b, "missing LayerNorm parameters");
+  auto wq = cat_rows(w->w_qkv, 3 * H, w->w_qm, H, H);
+  std::vector<float> bq;
+  if (ub) bq = cat_rows(w->b_qkv, 3 * H, w->b_qm, H, 1);
+  b->qkvm.load(b->q, wq.data(), ub ? bq.data() : nullptr, 4 * H, H, st);
+  auto wk = cat_rows(w->w_km, H, w->w_vm, H, H);
+  std::vector<float> bk;
+  if (ub) bk = cat_rows(w->b_km, H, w->b_vm, H, 1);
+  b->kvm.load(b->q, wk.data(), ub ? bk.data() : nullptr, 2 * H, H, st);
+  b->o.load(b->q, w->w_o, ub ? w->b_o : nullptr, H, H, st);
+  b->om.load(b->q, w->w_om, ub ? w->b_om : nullptr, H, H, st);
+  b->g.load(b->q, w->w_g, ub ? w->b_g : nullptr, H, H, st);
+  b->w1.load(b->q, w->w_1, ub ? w->b_1 : nullptr, F, H, st);
+  b->w2.load(b->q, w->w_2, ub ? w->b_2 : nullptr, H, F, st);
+  if (b->cfg.use_layer_norm) {
+    for (auto pr : {std::make_pair(&b->ln1_g, w->ln1_g), std::make_pair(&b->ln1_b, w->ln1_b),
+                    std::make_pair(&b->ln2_g, w->ln2_g), std::make_pair(&b->ln2_b, w->ln2_b)}) {
+      pr.first->ensure(H * sizeof(float));
+      LTM_CUDA_TRY(cudaMemcpy(pr.first->ptr, pr.second, H * sizeof(float), cudaMemcpyHostToDevice));
+    }
+  }
+  b->memory.ensure(static_cast<size_t>(b->Ms) * H * dtype_size(b->dt));
+  upload_f32_as(w->memory, static_cast<int64_t>(b->Ms) * H, b->dt, b->memory.ptr, st);
+  b->kvmb.ensure(static_cast<size_t>(b->Ms) * 2 * H * dtype_size(b->dt));
+  if (b->q.scheme == LTM_SCHEME_W8A8) {
+    b->mq.ensure(static_cast<size_t>(b->Ms) * H);
+    b->ms.ensure(static_cast<size_t>(b->Ms) * sizeof(float));
+  }
+  LTM_CUDA_TRY(cudaStreamSynchronize(st));
+  b->loaded = true;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    LTM_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != dev) LTM_CUDA_TRY(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+ltm_block* make_block(const ltm_block_config* cfg, const ltm_quant_config* qcfg, int device) {
+  LTM_REQUIRE(cfg && qcfg, "NULL config");
+  validate(*cfg, *qcfg);
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    set_error("no CUDA device");
+    throw Fail{LTM_ERR_NO_DEVICE};
+  }
+  LTM_REQUIRE(device >= 0 && device < ndev, "device index out of range");
+  auto b = std::make_unique<ltm_block>();
+  b->cfg = *cfg;
+  b->q = *qcfg;
+  b->device = device;
+  b->H = cfg->hidden_dim;
+  b->F = cfg->ffn_dim;
+  b->nh = cfg->num_heads;
+  b->dh = cfg->head_dim;
+  b->Ms = cfg->memory_slots;
+  b->dt = qcfg->act_dtype;
+  return b.release();
+}
+
+}  // namespace
 
 extern "C" void ltm_block_config_default(ltm_block_config* c) {
   if (!c) return;
@@ -28,23 +475,130 @@ extern "C" void ltm_block_config_default(ltm_block_config* c) {
   c->gradient_checkpointing = 1;
 }
 
-#define LTM_PENDING(name, ...)                                                 \
-  extern "C" ltm_status name(__VA_ARGS__) {                                    \
-    return guarded([&] { LTM_UNSUPPORTED(#name " is not built yet"); });       \
-  }
+extern "C" ltm_status ltm_block_create(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
+                                       int device, ltm_block** out) {
+  return guarded([&] {
+    LTM_REQUIRE(out, "out is NULL");
+    *out = make_block(cfg, qcfg, device);
+  });
+}
 
-LTM_PENDING(ltm_linear_w4a16, const void*, ltm_dtype, const uint8_t*, const float*, const uint8_t*,
-            const float*, ltm_epilogue, void*, int64_t, int64_t, int64_t, void*)
-LTM_PENDING(ltm_linear_w8a32, const float*, const int8_t*, const float*, const float*, ltm_epilogue,
-            float*, int64_t, int64_t, int64_t, void*)
-LTM_PENDING(ltm_block_create, const ltm_block_config*, const ltm_quant_config*, int, ltm_block**)
-LTM_PENDING(ltm_block_load_weights, ltm_block*, const ltm_block_weights*)
-LTM_PENDING(ltm_block_forward, ltm_block*, const void*, void*, const void*, int, int, void*)
-LTM_PENDING(ltm_block_get_memory, ltm_block*, void*, void*)
-LTM_PENDING(ltm_block_destroy, ltm_block*)
-LTM_PENDING(ltm_model_create, const ltm_block_config*, const ltm_quant_config*, int, int, int,
-            ltm_model**)
-LTM_PENDING(ltm_model_load_embedding, ltm_model*, const float*)
-LTM_PENDING(ltm_model_load_layer, ltm_model*, int, const ltm_block_weights*)
-LTM_PENDING(ltm_model_forward, ltm_model*, const int32_t*, void*, int, int, void*)
-LTM_PENDING(ltm_model_destroy, ltm_model*)
+extern "C" ltm_status ltm_block_load_weights(ltm_block* blk, const ltm_block_weights* w) {
+  return guarded([&] {
+    LTM_REQUIRE(blk, "block is NULL");
+    DeviceGuard g(blk->device);
+    load_block(blk, w, nullptr);
+  });
+}
+
+extern "C" ltm_status ltm_block_forward(ltm_block* blk, const void* x, void* y,
+                                        const void* attention_mask, int B, int S, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded, "block not created or weights not loaded");
+    if (attention_mask) LTM_UNSUPPORTED("explicit attention masks (self-attention is causal)");
+    LTM_REQUIRE(B >= 0 && S >= 0, "negative batch or sequence length");
+    if (B == 0 || S == 0) return;
+    LTM_REQUIRE(x && y && x != y, "x and y must be distinct device buffers");
+    DeviceGuard g(blk->device);
+    blk->forward(x, y, B, S, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded && out, "bad argument");
+    DeviceGuard g(blk->device);
+    LTM_CUDA_TRY(cudaMemcpyAsync(out, blk->memory.ptr,
+                                 static_cast<size_t>(blk->Ms) * blk->H * dtype_size(blk->dt),
+                                 cudaMemcpyDeviceToDevice, as_stream(stream)));
+  });
+}
+
+extern "C" ltm_status ltm_block_destroy(ltm_block* blk) {
+  return guarded([&] {
+    if (!blk) return;
+    DeviceGuard g(blk->device);
+    cudaDeviceSynchronize();
+    delete blk;
+  });
+}
+
+// ---------------------------------------------------------------- the model --
+struct ltm_model {
+  std::vector<std::unique_ptr<ltm_block>> layers;
+  ltm_block_config cfg{};
+  ltm_quant_config q{};
+  int device = 0, vocab = 0;
+  DevBuf emb, a, b;
+  int64_t ws_T = 0;
+};
+
+extern "C" ltm_status ltm_model_create(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
+                                       int n_layers, int vocab_size, int device, ltm_model** out) {
+  return guarded([&] {
+    LTM_REQUIRE(out && n_layers > 0 && vocab_size > 0, "bad argument");
+    auto m = std::make_unique<ltm_model>();
+    for (int i = 0; i < n_layers; ++i) m->layers.emplace_back(make_block(cfg, qcfg, device));
+    m->cfg = *cfg;
+    m->q = *qcfg;
+    m->device = device;
+    m->vocab = vocab_size;
+    *out = m.release();
+  });
+}
+
+extern "C" ltm_status ltm_model_load_embedding(ltm_model* m, const float* embedding) {
+  return guarded([&] {
+    LTM_REQUIRE(m && embedding, "bad argument");
+    DeviceGuard g(m->device);
+    const int64_t n = static_cast<int64_t>(m->vocab) * m->cfg.hidden_dim;
+    m->emb.ensure(n * dtype_size(m->q.act_dtype));
+    upload_f32_as(embedding, n, m->q.act_dtype, m->emb.ptr, nullptr);
+  });
+}
+
+extern "C" ltm_status ltm_model_load_layer(ltm_model* m, int layer, const ltm_block_weights* w) {
+  return guarded([&] {
+    LTM_REQUIRE(m && layer >= 0 && layer < static_cast<int>(m->layers.size()), "bad layer index");
+    DeviceGuard g(m->device);
+    load_block(m->layers[layer].get(), w, nullptr);
+  });
+}
+
+extern "C" ltm_status ltm_model_forward(ltm_model* m, const int32_t* tokens, void* hidden_out, int B,
+                                        int S, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(m && m->emb.ptr, "model not created or embedding not loaded");
+    for (auto& l : m->layers) LTM_REQUIRE(l->loaded, "a layer has no weights");
+    LTM_REQUIRE(B >= 0 && S >= 0, "negative batch or sequence length");
+    if (B == 0 || S == 0) return;
+    LTM_REQUIRE(tokens && hidden_out, "NULL pointer");
+    DeviceGuard g(m->device);
+    cudaStream_t st = as_stream(stream);
+    const int64_t T = static_cast<int64_t>(B) * S;
+    const int H = m->cfg.hidden_dim;
+    const size_t bytes = T * H * dtype_size(m->q.act_dtype);
+    if (T > m->ws_T) {
+      m->a.ensure(bytes);
+      m->b.ensure(bytes);
+      m->ws_T = T;
+    }
+    launch_embed_gather(m->emb.ptr, m->q.act_dtype, m->vocab, H, tokens, T, m->a.ptr, st);
+    const void* cur = m->a.ptr;
+    const size_t L = m->layers.size();
+    for (size_t i = 0; i < L; ++i) {
+      void* dst = (i + 1 == L) ? hidden_out : (cur == m->a.ptr ? m->b.ptr : m->a.ptr);
+      m->layers[i]->forward(cur, dst, B, S, st);
+      cur = dst;
+    }
+  });
+}
+
+extern "C" ltm_status ltm_model_destroy(ltm_model* m) {
+  return guarded([&] {
+    if (!m) return;
+    DeviceGuard g(m->device);
+    cudaDeviceSynchronize();
+    delete m;
+  });
+}

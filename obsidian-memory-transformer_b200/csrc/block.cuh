@@ -1,0 +1,81 @@
+// block.cuh -- internal interfaces between the kernels and the block
+// orchestration (device buffers, quantized weights, launchers).
+#pragma once
+
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace ltm_b200 {
+
+// Owning device allocation (grow-only).
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf();
+  void ensure(size_t n);
+  void release();
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(ptr);
+  }
+};
+
+// A quantized weight [N,K] with per-channel int8 or group-128 int4 codes.
+struct QLinear {
+  int64_t N = 0, K = 0;
+  int scheme = LTM_SCHEME_W8A8;
+  DevBuf q8, s8, q4, s4, z4, bias;
+  void load(const ltm_quant_config& q, const float* w_host, const float* b_host, int64_t n,
+            int64_t k, cudaStream_t stream);
+  void run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode, ltm_dtype dt,
+           Epilogue ep, cudaStream_t stream) const;
+};
+
+struct AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t ldq, ldk, ldv, ldo;
+  int64_t q_batch_rows;
+  int64_t kv_batch_rows;
+  int Sq, Skv, nh;
+  int causal_offset;
+  float scale_log2;
+};
+
+// Memory-bank write after the read (TB-v1):
+//   c   = mean_t g_t * x_t                 (accumulated by the gate-mix epilogue)
+//   w_s = rate * mean_heads softmax_s(qbar_h . K_M[s,h] / sqrt(dh))   (or rate)
+//   M_s = (1 - w_s) M_s + w_s c
+struct MemoryWriteState {
+  DevBuf colsum, qsum, wslot;
+  void prepare_gate_epilogue(Epilogue& ep, int H, cudaStream_t st);
+  void update_bank(void* memory, const void* kvm, const void* qm, int64_t ldq, int64_t T, int H,
+                   int nh, int dh, int Ms, float rate, bool use_scores, ltm_dtype dt,
+                   cudaStream_t st);
+};
+
+void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, int8_t* q, float* s,
+                         cudaStream_t stream);
+void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
+                 ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream);
+void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
+                  const Epilogue& ep, cudaStream_t stream);
+void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s4, const uint8_t* z4,
+                  int64_t M, int64_t N, int64_t K, int mode, const Epilogue& ep, cudaStream_t stream);
+void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float* gamma,
+                  const float* beta, void* y, int8_t* yq, float* ys, int8_t* xq, float* xs,
+                  bool do_norm, cudaStream_t stream, const void* residual = nullptr);
+void launch_embed_gather(const void* table, ltm_dtype dt, int vocab, int H, const int32_t* tok,
+                         int64_t T, void* out, cudaStream_t stream);
+void launch_attention(const AttnParams& p, int B, int D, bool causal, ltm_dtype dt,
+                      cudaStream_t stream);
+void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n, ltm_dtype dt,
+                 cudaStream_t stream);
+void upload_f32_as(const float* host, int64_t n, ltm_dtype dt, void* dev, cudaStream_t stream);
+
+}  // namespace ltm_b200

@@ -302,9 +302,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
 
 // -------------------------------------------------------- TMA descriptors --
 // 2-D tiled tensor map over a row-major [rows, cols] matrix of `elem_bytes`
-// elements with the 128-byte swizzle; box = box_cols x box_rows.
+// elements (128-byte swizzle unless given); box = box_cols x box_rows.
 void make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols,
-                 uint32_t box_rows);
+                 uint32_t box_rows, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 }  // namespace ltm_b200

@@ -37,7 +37,26 @@ struct Epilogue {
   const void* aux1 = nullptr;
   const void* aux2 = nullptr;
   int64_t ld_aux = 0;
+  // GATEMIX: optional column sums of g*x over the rows (memory write), fp32 [N]
+  float* colsum = nullptr;
 };
+
+// Sum over the warp's 32 rows of v[c]; lane c receives column c (31 shuffles,
+// recursive halving).  Must be called by all 32 lanes.
+__device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < s; ++j) {
+      const float send = upper ? v[j] : v[j + s];
+      const float keep = upper ? v[j + s] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
 
 __device__ __forceinline__ float gelu_tanh(float x) {
   // src/core/ops/fused_ops.cu:136-142
@@ -73,9 +92,11 @@ __device__ __forceinline__ void store32(T* p, const float (&v)[32]) {
 }
 
 // Applies the epilogue to 32 values of row `m`, columns [n0, n0+32) and stores.
+// GATEMIX with ep.colsum: g*x is written to gx_out when given (the caller
+// reduces it across the warp), else added to ep.colsum element by element.
 template <int MODE, class OutT>
 __device__ __forceinline__ void epilogue_store32(const Epilogue& ep, int64_t m, int64_t n0,
-                                                 float (&v)[32]) {
+                                                 float (&v)[32], float* gx_out = nullptr) {
   if constexpr (MODE == kEpiAccI32) {
     int32_t* o = static_cast<int32_t*>(ep.out) + m * ep.ldo + n0;
 #pragma unroll
@@ -125,6 +146,15 @@ __device__ __forceinline__ void epilogue_store32(const Epilogue& ep, int64_t m, 
 #pragma unroll
       for (int i = 0; i < 32; ++i) s[i] = s[i] + v[i] * mem[i];
       load32(static_cast<const OutT*>(ep.aux2) + m * ep.ld_aux + n0, mem);
+      if (ep.colsum) {
+        if (gx_out) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) gx_out[i] = v[i] * mem[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) atomicAdd(ep.colsum + n0 + i, v[i] * mem[i]);
+        }
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = s[i] + (1.0f - v[i]) * mem[i];
     }

@@ -1,0 +1,160 @@
+// gemm_w8a32.cu -- fp32-activation linear with int8 per-channel weights:
+//   y = epilogue( (a @ qw^T) * sw[n] + bias[n] )
+// the fp32 TitanBlock<float> path (FP32 FFMA: exact-enough for the 1e-4
+// parity bar, which tensor-core tf32 would not meet).  128 x 128 CTA tile,
+// K step 32, 8 x 8 outputs per thread, int8 weights widened to fp32 while
+// staging into shared memory; the 128 x 128 result is staged through shared
+// memory so the shared epilogue sees 32 consecutive columns per row.
+#include "block.cuh"
+#include "epilogue.cuh"
+
+namespace ltm_b200 {
+namespace {
+
+constexpr int kT = 128, kKS = 32, kPad = 4;
+
+template <int MODE>
+__global__ void __launch_bounds__(256) w8a32_kernel(const float* __restrict__ A,
+                                                    const int8_t* __restrict__ W, int M, int N, int K,
+                                                    Epilogue ep) {
+  extern __shared__ __align__(16) float sm[];
+  float* As = sm;                          // [kKS][kT + kPad]
+  float* Ws = As + kKS * (kT + kPad);      // [kKS][kT + kPad]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.y * kT, n0 = blockIdx.x * kT;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+  for (int k0 = 0; k0 < K; k0 += kKS) {
+    // A tile: 128 rows x 32 k -> As[k][m]
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int idx = tid + it * 256;  // 0..1023 float4 slots
+      const int r = idx >> 3, c4 = (idx & 7) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int gm = m0 + r, gk = k0 + c4;
+      if (gm < M) {
+        if (gk + 3 < K) {
+          v = *reinterpret_cast<const float4*>(A + static_cast<int64_t>(gm) * K + gk);
+        } else {
+          const float* src = A + static_cast<int64_t>(gm) * K;
+          v.x = gk < K ? src[gk] : 0.f;
+          v.y = gk + 1 < K ? src[gk + 1] : 0.f;
+          v.z = gk + 2 < K ? src[gk + 2] : 0.f;
+          v.w = gk + 3 < K ? src[gk + 3] : 0.f;
+        }
+      }
+      As[(c4 + 0) * (kT + kPad) + r] = v.x;
+      As[(c4 + 1) * (kT + kPad) + r] = v.y;
+      As[(c4 + 2) * (kT + kPad) + r] = v.z;
+      As[(c4 + 3) * (kT + kPad) + r] = v.w;
+    }
+    // W tile: 128 rows x 32 k int8 -> Ws[k][n]
+    {
+      const int r = tid >> 1, c16 = (tid & 1) * 16;
+      const int gn = n0 + r, gk = k0 + c16;
+      int8_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = 0;
+      if (gn < N) {
+        const int8_t* src = W + static_cast<int64_t>(gn) * K;
+        if (gk + 15 < K && ((reinterpret_cast<uintptr_t>(src + gk) & 15) == 0)) {
+          *reinterpret_cast<uint4*>(w) = *reinterpret_cast<const uint4*>(src + gk);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = gk + i < K ? src[gk + i] : 0;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) Ws[(c16 + i) * (kT + kPad) + r] = static_cast<float>(w[i]);
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kKS; ++k) {
+      float a[8], b[8];
+      const float4 a0 = *reinterpret_cast<const float4*>(As + k * (kT + kPad) + ty * 8);
+      const float4 a1 = *reinterpret_cast<const float4*>(As + k * (kT + kPad) + ty * 8 + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(Ws + k * (kT + kPad) + tx * 8);
+      const float4 b1 = *reinterpret_cast<const float4*>(Ws + k * (kT + kPad) + tx * 8 + 4);
+      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  // stage the tile, then run the shared epilogue on 32-column row chunks
+  float* Cs = sm;  // [128][128 + kPad]
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) Cs[(ty * 8 + i) * (kT + kPad) + tx * 8 + j] = acc[i][j];
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int idx = tid + it * 256;
+    const int r = idx >> 2, ch = idx & 3;
+    const int64_t m = m0 + r, n = n0 + ch * 32;
+    if (m < M && n < N) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = Cs[r * (kT + kPad) + ch * 32 + i];
+      epilogue_store32<MODE, float>(ep, m, n, v);
+    }
+  }
+}
+
+}  // namespace
+
+void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
+                  const Epilogue& ep, cudaStream_t stream) {
+  LTM_REQUIRE(M >= 0 && N >= 0 && K >= 0, "negative size");
+  LTM_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "size exceeds int32");
+  if (M == 0 || N == 0) return;
+  LTM_REQUIRE(N % 32 == 0, "N must be a multiple of 32");
+  LTM_REQUIRE(K % 4 == 0, "K must be a multiple of 4");
+  LTM_REQUIRE(a && qw && ep.out, "NULL pointer");
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0,
+              "fp32 operands must be 16-byte aligned");
+  LTM_REQUIRE(ep.ldo % 4 == 0, "output row stride must be a multiple of 4");
+  LTM_REQUIRE(mode != kEpiAccI32, "no int32 accumulator mode on the fp32 path");
+  const size_t smem = static_cast<size_t>(kT) * (kT + kPad) * sizeof(float);  // >= 2*kKS*(kT+kPad)
+  dim3 grid((N + kT - 1) / kT, (M + kT - 1) / kT);
+  dispatch_epilogue(mode, LTM_DTYPE_F32, [&](auto mode_c, auto) {
+    constexpr int MODE = decltype(mode_c)::value;
+    if constexpr (MODE != kEpiAccI32) {
+      auto kern = w8a32_kernel<MODE>;
+      LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+      kern<<<grid, 256, smem, stream>>>(a, qw, static_cast<int>(M), static_cast<int>(N),
+                                        static_cast<int>(K), ep);
+    }
+  });
+  check_launch("w8a32_kernel");
+}
+
+}  // namespace ltm_b200
+
+using namespace ltm_b200;
+
+extern "C" ltm_status ltm_linear_w8a32(const float* a, const int8_t* qw, const float* sw,
+                                       const float* bias, ltm_epilogue act, float* y, int64_t M,
+                                       int64_t N, int64_t K, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(act == LTM_EPI_NONE || act == LTM_EPI_GELU || act == LTM_EPI_SIGMOID,
+                "unknown epilogue");
+    Epilogue ep;
+    ep.act = act;
+    ep.col_scale = sw;
+    ep.bias = bias;
+    ep.out = y;
+    ep.ldo = N;
+    launch_w8a32(a, qw, M, N, K, kEpiPlain, ep, as_stream(stream));
+  });
+}

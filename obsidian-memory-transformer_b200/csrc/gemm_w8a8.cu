@@ -17,7 +17,7 @@
 // (src/core/ops/mma_ops.cu:20-92) for the quantized linears.
 #include <type_traits>
 
-#include "common.cuh"
+#include "block.cuh"
 #include "epilogue.cuh"
 
 namespace ltm_b200 {
@@ -128,16 +128,26 @@ __global__ void __launch_bounds__(192, (BN <= 128 ? 2 : 1))
         tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
         tmem_wait_ld();
         const int64_t n = static_cast<int64_t>(n0) + c * 32;
-        if (m < M && n < N && !*abort_flag) {
-          float v[32];
+        const bool valid = m < M && n < N && !*abort_flag;
+        float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if constexpr (MODE == kEpiAccI32)
-              v[i] = __int_as_float(static_cast<int>(r[i]));
-            else
-              v[i] = static_cast<float>(static_cast<int>(r[i]));
+        for (int i = 0; i < 32; ++i) {
+          if constexpr (MODE == kEpiAccI32)
+            v[i] = __int_as_float(static_cast<int>(r[i]));
+          else
+            v[i] = static_cast<float>(static_cast<int>(r[i]));
+        }
+        if constexpr (MODE == kEpiGateMix) {
+          float gx[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) gx[i] = 0.0f;
+          if (valid) epilogue_store32<MODE, OutT>(ep, m, n, v, gx);
+          if (ep.colsum) {
+            const float cs = warp_colsum32(gx);
+            if (n < N) atomicAdd(ep.colsum + n + lane, cs);
           }
-          epilogue_store32<MODE, OutT>(ep, m, n, v);
+        } else {
+          if (valid) epilogue_store32<MODE, OutT>(ep, m, n, v);
         }
       }
     }

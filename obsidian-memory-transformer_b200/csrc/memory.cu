@@ -1,0 +1,138 @@
+// memory.cu -- memory-bank write after the read (TB-v1), bandwidth-bound.
+//
+//   c_j = (1/T) sum_t g[t,j] * x[t,j]      (column sums accumulated by the
+//                                            gate-mix epilogue of the gate GEMM)
+//   w_s = rate * (1/nh) sum_h softmax_s( qbar_h . K_M[s, h] / sqrt(dh) ),
+//         qbar = (1/T) sum_t qm[t]          (use_attention_scores; else w_s = rate)
+//   M[s,j] <- (1 - w_s) M[s,j] + w_s c_j
+//
+// Follows MemoryBank<T>::store / storeStateKernel
+// (src/core/ltm/memory_bank.cu:39-68,242-274: EMA with weight
+// update_rate * attention_score[slot], state broadcast to every slot) with the
+// pooled state of the paper's compression (mean over the segment).
+#include "block.cuh"
+
+namespace ltm_b200 {
+namespace {
+
+// out[j] += sum over rows of x[t, j] (x: [T, ld] act dtype, first H columns).
+template <class T>
+__global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ x, int64_t ld, int64_t rows,
+                                                     int H, float* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int cx = threadIdx.x & 31, ry = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + cx;
+  const int64_t per = (rows + gridDim.y - 1) / gridDim.y;
+  const int64_t r0 = blockIdx.y * per, r1 = min(rows, r0 + per);
+  float acc = 0.0f;
+  if (col < H)
+    for (int64_t r = r0 + ry; r < r1; r += 8) acc += to_f32(x[r * ld + col]);
+  red[ry][cx] = acc;
+  __syncthreads();
+  if (ry == 0 && col < H) {
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i][cx];
+    atomicAdd(out + col, t);
+  }
+}
+
+// One CTA per head: slot softmax of the mean memory query against K_M.
+template <class T>
+__global__ void __launch_bounds__(256) slot_weight_kernel(const float* __restrict__ qsum,
+                                                          float inv_T, const T* __restrict__ kvm,
+                                                          int64_t ldk, int Ms, int dh, int nh,
+                                                          float rate, float* __restrict__ wslot) {
+  extern __shared__ float sc[];  // [Ms] scores, then reduction scratch
+  __shared__ float red[32];
+  const int h = blockIdx.x;
+  const float scale = rsqrtf(static_cast<float>(dh));
+  float mx = -INFINITY;
+  for (int s = threadIdx.x; s < Ms; s += blockDim.x) {
+    const T* kr = kvm + static_cast<int64_t>(s) * ldk + h * dh;
+    float d = 0.0f;
+    for (int e = 0; e < dh; ++e) d += qsum[h * dh + e] * inv_T * to_f32(kr[e]);
+    d *= scale;
+    sc[s] = d;
+    mx = fmaxf(mx, d);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -INFINITY;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
+  __syncthreads();
+  float sum = 0.0f;
+  for (int s = threadIdx.x; s < Ms; s += blockDim.x) {
+    const float e = expf(sc[s] - mx);
+    sc[s] = e;
+    sum += e;
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  sum = 0.0f;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) sum += red[i];
+  const float f = rate / (sum * static_cast<float>(nh));
+  for (int s = threadIdx.x; s < Ms; s += blockDim.x) atomicAdd(wslot + s, sc[s] * f);
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) bank_update_kernel(T* __restrict__ mem,
+                                                          const float* __restrict__ colsum,
+                                                          float inv_T, const float* __restrict__ wslot,
+                                                          float rate, int Ms, int H) {
+  const int64_t n = static_cast<int64_t>(Ms) * H;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(i / H), j = static_cast<int>(i - static_cast<int64_t>(s) * H);
+    const float w = wslot ? wslot[s] : rate;
+    const float c = colsum[j] * inv_T;
+    mem[i] = from_f32<T>((1.0f - w) * to_f32(mem[i]) + w * c);
+  }
+}
+
+}  // namespace
+
+void MemoryWriteState::prepare_gate_epilogue(Epilogue& ep, int H, cudaStream_t st) {
+  colsum.ensure(H * sizeof(float));
+  LTM_CUDA_TRY(cudaMemsetAsync(colsum.ptr, 0, H * sizeof(float), st));
+  ep.colsum = colsum.as<float>();
+}
+
+void MemoryWriteState::update_bank(void* memory, const void* kvm, const void* qm, int64_t ldq,
+                                   int64_t T, int H, int nh, int dh, int Ms, float rate,
+                                   bool use_scores, ltm_dtype dt, cudaStream_t st) {
+  if (T == 0) return;
+  const float inv_T = 1.0f / static_cast<float>(T);
+  dispatch_dtype(dt, [&](auto tag) {
+    using TT = decltype(tag);
+    const float* w = nullptr;
+    if (use_scores) {
+      qsum.ensure(H * sizeof(float));
+      wslot.ensure(Ms * sizeof(float));
+      LTM_CUDA_TRY(cudaMemsetAsync(qsum.ptr, 0, H * sizeof(float), st));
+      LTM_CUDA_TRY(cudaMemsetAsync(wslot.ptr, 0, Ms * sizeof(float), st));
+      const int splits = static_cast<int>(std::min<int64_t>(64, (T + 63) / 64));
+      dim3 g1((H + 31) / 32, splits);
+      colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(qm), ldq, T, H, qsum.as<float>());
+      check_launch("colsum_kernel");
+      const size_t smem = static_cast<size_t>(Ms) * sizeof(float);
+      LTM_REQUIRE(smem <= 200 * 1024, "memory_slots too large for the slot-weight kernel");
+      auto kern = slot_weight_kernel<TT>;
+      LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+      kern<<<nh, 256, smem, st>>>(qsum.as<float>(), inv_T, static_cast<const TT*>(kvm), 2 * H, Ms,
+                                  dh, nh, rate, wslot.as<float>());
+      check_launch("slot_weight_kernel");
+      w = wslot.as<float>();
+    }
+    const int64_t n = static_cast<int64_t>(Ms) * H;
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
+    bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), colsum.as<float>(),
+                                                 inv_T, w, rate, Ms, H);
+    check_launch("bank_update_kernel");
+  });
+}
+
+}  // namespace ltm_b200

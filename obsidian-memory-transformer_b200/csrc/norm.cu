@@ -7,7 +7,7 @@
 // y = (v - mean) * rsqrt(var + eps) * gamma + beta.  One CTA per row, each
 // thread owns one 16-byte vector of the row in registers, so the row is read
 // from HBM exactly once; reductions are warp shuffles + one shared-memory hop.
-#include "common.cuh"
+#include "block.cuh"
 
 namespace ltm_b200 {
 namespace {
@@ -60,7 +60,8 @@ __device__ __forceinline__ void store_q(int8_t* dst, const float (&v)[V], float 
 
 // One CTA per row; thread t owns elements [t*V, t*V+V).  NW = max warps.
 template <class T, int NW>
-__global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x, int H,
+__global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x,
+                                                        const T* __restrict__ res, int H,
                                                         const float* __restrict__ gamma,
                                                         const float* __restrict__ beta,
                                                         T* __restrict__ y, int8_t* __restrict__ yq,
@@ -72,14 +73,23 @@ __global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x,
   const int64_t row = blockIdx.x;
   const int e0 = threadIdx.x * V;
   const bool active = e0 < H;
-  float xv[V];
+  float xv[V], rv[V];
 #pragma unroll
-  for (int i = 0; i < V; ++i) xv[i] = 0.0f;
+  for (int i = 0; i < V; ++i) xv[i] = rv[i] = 0.0f;
   if (active) {
     uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + row * H + e0));
     const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
     for (int i = 0; i < V; ++i) xv[i] = to_f32(e[i]);
+    if (res == x) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) rv[i] = xv[i];
+    } else {
+      uint4 rr = __ldg(reinterpret_cast<const uint4*>(res + row * H + e0));
+      const T* er = reinterpret_cast<const T*>(&rr);
+#pragma unroll
+      for (int i = 0; i < V; ++i) rv[i] = to_f32(er[i]);
+    }
   }
   if (xq) {
     float am = 0.0f;
@@ -94,13 +104,13 @@ __global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x,
   if (do_norm) {
     float sum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < V; ++i) sum += xv[i] + xv[i];
+    for (int i = 0; i < V; ++i) sum += xv[i] + rv[i];
     const float mean = block_sum<NW>(sum, red) / static_cast<float>(H);
     float sq = 0.0f;
     if (active) {
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        const float d = (xv[i] + xv[i]) - mean;
+        const float d = (xv[i] + rv[i]) - mean;
         sq += d * d;
       }
     }
@@ -109,7 +119,7 @@ __global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x,
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const int c = active ? e0 + i : 0;
-      yv[i] = ((xv[i] + xv[i]) - mean) * rstd * __ldg(gamma + c) + __ldg(beta + c);
+      yv[i] = ((xv[i] + rv[i]) - mean) * rstd * __ldg(gamma + c) + __ldg(beta + c);
     }
   } else {
 #pragma unroll
@@ -158,7 +168,7 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__
 // the normalisation (y = x).
 void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float* gamma,
                   const float* beta, void* y, int8_t* yq, float* ys, int8_t* xq, float* xs,
-                  bool do_norm, cudaStream_t stream) {
+                  bool do_norm, cudaStream_t stream, const void* residual) {
   if (rows == 0) return;
   const int V = static_cast<int>(16 / dtype_size(dt));
   LTM_REQUIRE(H % V == 0, "hidden size must be a multiple of 16 bytes");
@@ -167,8 +177,8 @@ void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float*
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     ln_x2_kernel<T, 32><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
-        static_cast<const T*>(x), H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs,
-        do_norm ? 1 : 0);
+        static_cast<const T*>(x), static_cast<const T*>(residual ? residual : x), H, gamma, beta,
+        static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
   });
   check_launch("ln_x2_kernel");
 }
@@ -186,3 +196,20 @@ void launch_embed_gather(const void* table, ltm_dtype dt, int vocab, int H, cons
 }
 
 }  // namespace ltm_b200
+
+using namespace ltm_b200;
+
+extern "C" ltm_status ltm_layernorm_residual(const void* x, const void* r, const float* gamma,
+                                             const float* beta, void* y, ltm_dtype dtype,
+                                             int64_t rows, int64_t H, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(rows >= 0 && H > 0 && H < (1 << 20), "bad size");
+    if (rows == 0) return;
+    LTM_REQUIRE(x && r && gamma && beta && y, "NULL pointer");
+    const uintptr_t mis = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(r) |
+                          reinterpret_cast<uintptr_t>(y);
+    LTM_REQUIRE((mis & 15) == 0, "operands must be 16-byte aligned");
+    launch_ln_x2(x, dtype, rows, static_cast<int>(H), gamma, beta, y, nullptr, nullptr, nullptr,
+                 nullptr, true, as_stream(stream), r);
+  });
+}

@@ -7,7 +7,7 @@
 // (__fdiv_rn) followed by round-half-away-from-zero (roundf), the arithmetic
 // of the reference kernels src/core/quantization/quantizer.cu:94-142, so the
 // codes are bit-exact against a CPU evaluation of the same formula.
-#include "common.cuh"
+#include "block.cuh"
 
 namespace ltm_b200 {
 namespace {

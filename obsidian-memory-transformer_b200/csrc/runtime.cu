@@ -75,16 +75,18 @@ EncodeTiledFn encode_fn() {
 
 void make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
                  uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols,
-                 uint32_t box_rows) {
+                 uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   LTM_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
   LTM_REQUIRE((row_stride_elems * elem_bytes) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
-  LTM_REQUIRE(box_cols * elem_bytes <= 128, "TMA box inner extent exceeds the 128-byte swizzle");
+  if (swizzle == CU_TENSOR_MAP_SWIZZLE_128B)
+    LTM_REQUIRE(box_cols * elem_bytes <= 128, "TMA box inner extent exceeds the 128-byte swizzle");
+  LTM_REQUIRE((box_cols * elem_bytes) % 16 == 0, "TMA box inner extent must be a multiple of 16 bytes");
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r)));

@@ -81,6 +81,9 @@ def _declare(L):
         "ltm_linear_w8a8_acc_i32": ([vp, vp, vp, i64, i64, i64, vp], ci),
         "ltm_linear_w4a16": ([vp, ci, vp, vp, vp, vp, ci, vp, i64, i64, i64, vp], ci),
         "ltm_linear_w8a32": ([vp, vp, vp, vp, ci, vp, i64, i64, i64, vp], ci),
+        "ltm_layernorm_residual": ([vp, vp, vp, vp, vp, ci, i64, i64, vp], ci),
+        "ltm_attention_forward": ([vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, i64, ci, ci, ci,
+                                   ci, vp], ci),
         "ltm_block_config_default": ([C.POINTER(BlockConfigC)], None),
         "ltm_block_create": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), ci,
                               C.POINTER(vp)], ci),
@@ -265,6 +268,35 @@ def linear_w8a32(a, qw, sw, bias=None, act: int = EPI_NONE, stream=None):
     _check(lib().ltm_linear_w8a32(_ptr(a), _ptr(qw), _ptr(sw), _ptr(bias), act, _ptr(y), M, N, K,
                                   _stream(stream)))
     return y
+
+
+# ----------------------------------------------------------------------- ops --
+def layernorm_residual(x, r, gamma, beta, stream=None):
+    """y = LN(x + r) * gamma + beta over the last dim (eps 1e-5)."""
+    torch = _torch()
+    _need_cuda(x, r, gamma, beta)
+    H = x.shape[-1]
+    y = torch.empty_like(x)
+    _check(lib().ltm_layernorm_residual(_ptr(x), _ptr(r), _ptr(gamma), _ptr(beta), _ptr(y),
+                                        dtype_code(x.dtype), x.numel() // H, H, _stream(stream)))
+    return y
+
+
+def attention(q, k, v, B: int, Sq: int, Skv: int, num_heads: int, head_dim: int, causal: bool,
+              kv_shared: bool = False, out=None, stream=None):
+    """q: [B*Sq, ldq] head-sliced rows; k, v: [B*Skv, ld] (or [Skv, ld] when kv_shared).
+    Returns o [B*Sq, num_heads*head_dim]."""
+    torch = _torch()
+    for t in (q, k, v):
+        if not t.is_cuda or t.stride(-1) != 1:
+            raise ValueError("attention operands must be CUDA tensors with unit column stride")
+    if out is None:
+        out = torch.empty((B * Sq, num_heads * head_dim), dtype=q.dtype, device=q.device)
+    _check(lib().ltm_attention_forward(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v),
+                                       v.stride(0), _ptr(out), out.stride(0), B, Sq, Skv,
+                                       0 if kv_shared else Skv, num_heads, head_dim, int(causal),
+                                       dtype_code(q.dtype), _stream(stream)))
+    return out
 
 
 # --------------------------------------------------------------------- block --
