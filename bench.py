@@ -1,0 +1,496 @@
+#!/usr/bin/env python
+"""Headline benchmark: Titan-block tokens/s of the quantized prefill.
+
+Workload (one step): a 12-layer Titan model prefill with W8A8 linears and
+fp16 activations -- hidden 768, 12 heads (head_dim 64), FFN 3072, 512 memory
+slots, vocab 32000, batch 8, seq 2048, per-token dynamic INT8 activations --
+embedding gather + 12 TB-v1 blocks on synthetic seeded tokens / weights.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun as N independent replicas (one process per GPU, no
+data-path collective: the prefill of independent batches does not shard), so
+`value` is the aggregate over all ranks and scaling is weak.  Rank 0 prints one
+JSON line.  `--impl reference` times the CPU restatement of the reference's
+algorithm (the oracle; the reference itself does not compile) on the host
+cores with the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT), str(ROOT / "obsidian-memory-transformer_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+WL = dict(layers=12, B=8, S=2048, H=768, nh=12, F=3072, Ms=512, vocab=32000)
+WORKLOAD_NAME = ("12-layer Titan prefill, W8A8 INT8 linears + fp16 activations, hidden 768, "
+                 "12 heads, FFN 3072, 512 memory slots, vocab 32000, batch 8, seq 2048")
+METRIC = "Titan-block tokens/s (12-layer W8A8 prefill)"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
+    ap.add_argument("--layers", type=int, default=WL["layers"], help=argparse.SUPPRESS)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- plumbing --
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return d, "measured (MEASURED_PEAKS.json)"
+    return dict(FALLBACK_PEAKS), "fallback (profiling recipe)"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        rows = []
+        with open(self.out.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.out.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- our path --
+def build_model(torch, ltm, n_layers: int, device: int):
+    from ltm_b200 import synthetic
+    cfg = ltm.TitanBlockConfig(hidden_dim=WL["H"], ffn_dim=WL["F"], num_heads=WL["nh"],
+                               head_dim=WL["H"] // WL["nh"], memory_slots=WL["Ms"])
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W8A8, act_dtype=ltm.DTYPE_F16)
+    model = ltm.TitanModel(cfg, q, n_layers, WL["vocab"], device=device)
+    model.load_embedding(synthetic.embedding(WL["vocab"], WL["H"], 7))
+    for i in range(n_layers):
+        model.load_layer(i, synthetic.block_weights(WL["H"], WL["F"], WL["Ms"], 1000 + i))
+    return model
+
+
+def per_layer_ops():
+    """(name, kind, shape, launches per layer) of the kernels of one block."""
+    B, S, H, F, Ms = WL["B"], WL["S"], WL["H"], WL["F"], WL["Ms"]
+    T = B * S
+    return [
+        ("gemm_qkvm", "w8a8", (T, 4 * H, H), 1),
+        ("gemm_kvm", "w8a8", (Ms, 2 * H, H), 1),
+        ("gemm_o_om_gate", "w8a8", (T, H, H), 3),
+        ("gemm_ffn_up", "w8a8", (T, F, H), 1),
+        ("gemm_ffn_down", "w8a8", (T, H, F), 1),
+        ("attn_self_causal", "attn", (B, S, S, True), 1),
+        ("attn_memory", "attn", (B, S, Ms, False), 1),
+        ("ln_quant", "ln", (T, H), 2),
+        ("quant_rows_h", "quant", (T, H), 2),
+        ("quant_rows_f", "quant", (T, F), 1),
+        ("quant_bank", "quant", (Ms, H), 1),
+    ]
+
+
+def probe_kernels(torch, ltm, reps: int = 10):
+    """Times each kernel of one block standalone at the workload's shapes with
+    CUDA events on the launching stream (L2 flushed before every launch)."""
+    dev = torch.device("cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    H, nh = WL["H"], WL["nh"]
+    dh = H // nh
+    res = []
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    for name, kind, shape, per_layer in per_layer_ops():
+        if kind == "w8a8":
+            M, N, K = shape
+            qa = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=gen)
+            qw = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=gen)
+            sa = torch.rand(M, device=dev) * 0.01
+            sw = torch.rand(N, device=dev) * 0.01
+            bias = torch.zeros(N, device=dev)
+            y = torch.empty((M, N), dtype=torch.float16, device=dev)
+
+            def call():
+                ltm._check(ltm.lib().ltm_linear_w8a8(ltm._ptr(qa), ltm._ptr(sa), ltm._ptr(qw),
+                                                     ltm._ptr(sw), ltm._ptr(bias), 0, ltm._ptr(y),
+                                                     ltm.DTYPE_F16, M, N, K, ltm._stream()))
+            flops = 2.0 * M * N * K
+            nbytes = M * K + N * K + 2 * M * N + 4 * (M + 2 * N)
+        elif kind == "attn":
+            B, Sq, Skv, causal = shape
+            q = torch.randn((B * Sq, 4 * H), dtype=torch.float16, device=dev, generator=gen)
+            kv = q if causal else torch.randn((Skv, 2 * H), dtype=torch.float16, device=dev,
+                                              generator=gen)
+            o = torch.empty((B * Sq, H), dtype=torch.float16, device=dev)
+            if causal:
+                qq, kk, vv = q[:, :H], q[:, H:2 * H], q[:, 2 * H:3 * H]
+            else:
+                qq, kk, vv = q[:, 3 * H:], kv[:, :H], kv[:, H:]
+
+            def call():
+                ltm.attention(qq, kk, vv, B, Sq, Skv, nh, dh, causal, kv_shared=not causal, out=o)
+            pairs = B * nh * (Sq * (Sq + 1) / 2 if causal else Sq * Skv)
+            flops = 4.0 * pairs * dh
+            nbytes = 2 * (B * Sq * H * 2 + (B if causal else 1) * Skv * H * 2)
+        elif kind == "ln":
+            T, Hh = shape
+            x = torch.randn((T, Hh), dtype=torch.float16, device=dev, generator=gen)
+            g = torch.ones(Hh, device=dev)
+            b = torch.zeros(Hh, device=dev)
+
+            def call():
+                ltm.layernorm_residual(x, x, g, b)
+            flops = 0.0
+            nbytes = 2 * T * Hh + T * Hh  # f16 in, int8 out (fused-quant variant writes int8)
+        else:
+            T, K = shape
+            x = torch.randn((T, K), dtype=torch.float16, device=dev, generator=gen)
+
+            def call():
+                ltm.quantize_act_int8_per_token(x)
+            flops = 0.0
+            nbytes = 2 * T * K + T * K + 4 * T
+        call()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            call()
+            e.record()
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+        ms = statistics.median(times)
+        res.append(dict(name=name, kind=kind, shape=list(shape), ms=ms, launches_per_layer=per_layer,
+                        flops=flops, bytes=nbytes))
+    del flush
+    return res
+
+
+def int8_peak(torch):
+    """cuBLASLt int8 GEMM (torch._int_mm) throughput at 8192^3, TOP/s."""
+    try:
+        n = 8192
+        a = torch.randint(-64, 64, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-64, 64, (n, n), dtype=torch.int8, device="cuda")
+        torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = 1e9
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch._int_mm(a, b)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    except Exception:  # noqa: BLE001 - report the derived figure instead
+        return None
+
+
+def traffic_from_profiles(kernel: str):
+    """DRAM bytes per launch of `kernel` recorded from an ncu capture in
+    profiles/traffic.md (table rows: | kernel | workload | bytes/launch | ...)."""
+    f = ROOT / "profiles" / "traffic.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        cells = [c.strip() for c in line.strip().strip("|").split("|")]
+        if len(cells) >= 3 and cells[0] == kernel:
+            try:
+                return float(cells[2])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_baseline(threads_hint=None):
+    """The oracle's TB-v1 model on the host cores, bounded sample: 1 of the 12
+    layers at the full batch (tokens/s scaled by 1/12)."""
+    from ltm_b200 import synthetic
+    from oracle import oracle as orc
+    if threads_hint:
+        orc.set_threads(threads_hint)
+    H, nh, F, Ms, V = WL["H"], WL["nh"], WL["F"], WL["Ms"], WL["vocab"]
+    cfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W8A8, dtype=orc.F16)
+    w = synthetic.block_weights(H, F, Ms, 1000)
+    emb = synthetic.embedding(V, H, 7)
+    B, S = WL["B"], WL["S"]
+    tok = synthetic.tokens(B, S, V, 3)
+    t0 = time.perf_counter()
+    orc.model_forward(cfg, [w], emb, tok, B, S)
+    dt = time.perf_counter() - t0
+    tps = B * S / dt / WL["layers"]
+    return {"value": tps, "unit": "tokens/s", "cores": orc.num_threads(), "kind": "port",
+            "sample": f"oracle TB-v1, 1 of {WL['layers']} layers, batch {B} x seq {S}, "
+                      f"{dt:.1f} s; tokens/s scaled to {WL['layers']} layers"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import ltm_b200 as ltm
+    ws, rank, local = dist_env()
+    assert ws == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {ws}"
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    model = build_model(torch, ltm, args.layers, local)
+    from ltm_b200 import synthetic
+    B, S, H = WL["B"], WL["S"], WL["H"]
+    tok_host = torch.from_numpy(synthetic.tokens(B, S, WL["vocab"], 100 + rank)).pin_memory()
+    tok = tok_host.to(dev)
+    out = torch.empty((B, S, H), dtype=torch.float16, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    args.warmup = max(args.warmup, 3)
+    for _ in range(args.warmup):
+        model.forward(tok, out)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(cvd.split(",")[local] if cvd else local)
+    launches0 = ltm.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.fill_(0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        model.forward(tok, out)
+        e.record(stream)
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    launches = ltm.launch_count() - launches0
+    my_ms = sum(s.elapsed_time(e) for s, e in evs)
+    t = torch.tensor([my_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    tokens = ws * B * S * args.steps
+    value = tokens / (total_ms * 1e-3)
+
+    # end to end through the public API: pinned H2D of the tokens, forward,
+    # D2H of each sequence's last hidden state (the prefill result)
+    last_host = torch.empty((B, H), dtype=torch.float16).pin_memory()
+    model.forward(tok, out)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_evs = []
+    for _ in range(args.steps):
+        flush.fill_(0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        tok.copy_(tok_host, non_blocking=True)
+        model.forward(tok, out)
+        last_host.copy_(out[:, -1, :], non_blocking=True)
+        e.record(stream)
+        e2e_evs.append((s, e))
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in e2e_evs)], dtype=torch.float64,
+                          device=dev)
+    if ws > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = tokens / (float(e2e_ms.item()) * 1e-3)
+
+    probe = None
+    roofline = None
+    pk, pk_src = peaks()
+    if rank == 0 and not args.no_probe:
+        probe = probe_kernels(torch, ltm)
+        i8 = int8_peak(torch)
+        L = args.layers
+        by_kind = {}
+        for r in probe:
+            k = by_kind.setdefault(r["kind"], dict(ms=0.0, flops=0.0, bytes=0.0, launches=0))
+            k["ms"] += r["ms"] * r["launches_per_layer"] * L
+            k["flops"] += r["flops"] * r["launches_per_layer"] * L
+            k["bytes"] += r["bytes"] * r["launches_per_layer"] * L
+            k["launches"] += r["launches_per_layer"] * L
+        dom = max(by_kind, key=lambda k: by_kind[k]["ms"])
+        d = by_kind[dom]
+        kname = {"w8a8": "w8a8_tc_kernel", "attn": "flash_fwd_tc_kernel",
+                 "ln": "ln_x2_kernel", "quant": "rowwise_int8_kernel"}[dom]
+        avg_ms = d["ms"] / d["launches"]
+        if dom in ("w8a8", "attn"):
+            achieved = d["flops"] / d["launches"] / (avg_ms * 1e-3) / 1e12
+            if dom == "w8a8":
+                peak = i8 if i8 else 2.0 * pk["bf16_tflops"]
+                peak_src = ("int8 torch._int_mm 8192^3 measured in this run" if i8 else
+                            "2 x bf16_tflops " + pk_src + " (derived int8)")
+            else:
+                peak = pk["bf16_tflops"]
+                peak_src = "bf16_tflops " + pk_src
+            unit, bound = "TFLOP/s", "tensor"
+        else:
+            achieved = d["bytes"] / d["launches"] / (avg_ms * 1e-3) / 1e9
+            peak = pk["hbm_gbs"]
+            peak_src = "hbm_gbs " + pk_src
+            unit, bound = "GB/s", "hbm"
+        traffic = traffic_from_profiles(kname)
+        roofline = {"bound": bound, "kernel": kname, "achieved": round(achieved, 2),
+                    "peak": round(peak, 2), "unit": unit, "frac": round(achieved / peak, 4),
+                    "traffic": traffic, "peak_source": peak_src, "launches_per_step": d["launches"],
+                    "avg_launch_ms": round(avg_ms, 5),
+                    "algorithmic_per_launch": (d["flops"] if bound == "tensor" else d["bytes"])
+                    / d["launches"]}
+        probe = {r["name"]: {"ms_per_launch": round(r["ms"], 5),
+                             "ms_per_step": round(r["ms"] * r["launches_per_layer"] * L, 4),
+                             "rate": (round(r["flops"] / (r["ms"] * 1e-3) / 1e12, 1)
+                                      if r["flops"] else
+                                      round(r["bytes"] / (r["ms"] * 1e-3) / 1e9, 1)),
+                             "rate_unit": "TFLOP/s" if r["flops"] else "GB/s"} for r in probe}
+        if i8:
+            probe["int8_peak_tops_measured"] = round(i8, 1)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded tokens U[0,32000), weights N(0,0.02), random init)",
+            "config": {"workload": WORKLOAD_NAME, "layers": args.layers, "global_batch": B * ws,
+                       "seq_len": S, "act_dtype": "f16", "parallelism": f"replicas{ws}",
+                       "l2": "flushed between timed steps (256 MiB write), per-step CUDA events"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(tok_host.numel() * 4),
+                    "d2h_bytes_per_step": int(last_host.numel() * 2)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "kernels": probe,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    model.close()
+
+
+# ---------------------------------------------------------- reference path --
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from ltm_b200 import synthetic
+    from oracle import oracle as orc
+    H, nh, F, Ms, V = WL["H"], WL["nh"], WL["F"], WL["Ms"], WL["vocab"]
+    cfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W8A8, dtype=orc.F16)
+    w = synthetic.block_weights(H, F, Ms, 1000)
+    emb = synthetic.embedding(V, H, 7)
+    Bs, S = 1, WL["S"]  # each step: 1 layer of 12, one sequence of the batch
+    tok = synthetic.tokens(Bs, S, V, 3)
+    for _ in range(args.warmup):
+        orc.model_forward(cfg, [w], emb, tok, Bs, S)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.model_forward(cfg, [w], emb, tok, Bs, S)
+    dt = time.perf_counter() - t0
+    value = args.steps * Bs * S / dt / WL["layers"]
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "impl": "reference",
+        "data": "synthetic (seeded tokens U[0,32000), weights N(0,0.02), random init)",
+        "config": {"workload": WORKLOAD_NAME, "layers": WL["layers"], "global_batch": WL["B"],
+                   "seq_len": S, "act_dtype": "f16", "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": orc.num_threads(),
+                         "kind": "port",
+                         "sample": f"each step: 1 of {WL['layers']} layers, 1 sequence of "
+                                   f"{S} tokens; tokens/s scaled to {WL['layers']} layers"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's CUDA sources do not compile; this arm times the CPU "
+                "restatement of its algorithm (oracle/) on all host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

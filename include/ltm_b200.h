@@ -70,6 +70,9 @@ LTM_API const char* ltm_last_error_string(void);
  * the current device (0 = none; otherwise the code of the wait that expired). */
 LTM_API ltm_status ltm_device_error(int* code_out);
 
+/* Number of kernels this library has launched in this process (all devices). */
+LTM_API ltm_status ltm_launch_count(uint64_t* count_out);
+
 /* ---------------------------------------------------------- quantization -- */
 /* Replaces Quantizer<T>::quantize with per_channel=true, symmetric=true,
  * channel_axis=0 (include/core/quantization/quantizer.cuh:183,

@@ -75,7 +75,10 @@ ltm_status guarded(F&& f) {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+void note_launch();
+
 inline void check_launch(const char* what) {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string(what) + ": " + cudaGetErrorString(e));

@@ -1,6 +1,7 @@
 // runtime.cu -- error strings, device error word, device properties and the
 // TMA descriptor encoder (driver entry point resolved through the runtime, so
 // the library needs no link-time dependency on libcuda).
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -28,7 +29,10 @@ int* device_error_ptr() {
 
 namespace {
 thread_local std::string t_last_error;
-}
+std::atomic<uint64_t> g_launches{0};
+}  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 void clear_error() { t_last_error.clear(); }
@@ -109,5 +113,12 @@ extern "C" ltm_status ltm_device_error(int* code_out) {
     LTM_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
     LTM_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
     *code_out = v;
+  });
+}
+
+extern "C" ltm_status ltm_launch_count(uint64_t* count_out) {
+  return guarded([&] {
+    LTM_REQUIRE(count_out != nullptr, "count_out is NULL");
+    *count_out = g_launches.load(std::memory_order_relaxed);
   });
 }

@@ -72,6 +72,7 @@ def _declare(L):
         "ltm_version": ([], C.c_char_p),
         "ltm_last_error_string": ([], C.c_char_p),
         "ltm_device_error": ([C.POINTER(C.c_int)], ci),
+        "ltm_launch_count": ([C.POINTER(C.c_uint64)], ci),
         "ltm_quantize_int8_per_channel": ([vp, ci, i64, i64, vp, vp, vp], ci),
         "ltm_dequantize_int8_per_channel": ([vp, vp, i64, i64, vp, ci, vp], ci),
         "ltm_quantize_act_int8_per_token": ([vp, ci, i64, i64, vp, vp, vp], ci),
@@ -130,6 +131,13 @@ def device_error() -> int:
     code = C.c_int(0)
     _check(lib().ltm_device_error(C.byref(code)))
     return code.value
+
+
+def launch_count() -> int:
+    """Kernels launched by the library in this process."""
+    n = C.c_uint64(0)
+    _check(lib().ltm_launch_count(C.byref(n)))
+    return n.value
 
 
 # ---------------------------------------------------------------- torch glue --
