@@ -150,9 +150,11 @@ def per_layer_ops():
 
 def probe_kernels(torch, ltm, reps: int = 10):
     """Times each kernel of one block standalone at the workload's shapes with
-    CUDA events on the launching stream (L2 flushed before every launch)."""
+    CUDA events on the launching stream (L2 flushed and cleaned before every
+    launch)."""
     dev = torch.device("cuda")
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     H, nh = WL["H"], WL["nh"]
     dh = H // nh
     res = []
@@ -212,7 +214,11 @@ def probe_kernels(torch, ltm, reps: int = 10):
         torch.cuda.synchronize()
         times = []
         for _ in range(reps):
+            # write-flush L2, then read a second L2-sized buffer so the probed
+            # kernel starts on a cold but clean L2 (no dirty-line writebacks)
             flush.fill_(1)
+            clean.sum()
+            torch.cuda._sleep(200_000)  # keeps the GPU busy while the host enqueues the launch
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             call()
@@ -222,7 +228,7 @@ def probe_kernels(torch, ltm, reps: int = 10):
         ms = statistics.median(times)
         res.append(dict(name=name, kind=kind, shape=list(shape), ms=ms, launches_per_layer=per_layer,
                         flops=flops, bytes=nbytes))
-    del flush
+    del flush, clean
     return res
 
 

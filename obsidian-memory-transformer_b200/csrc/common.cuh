@@ -104,6 +104,26 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// Symmetric INT8 code of v for scale s: clamp(round_half_away(v / s), -127, 127)
+// with v / s the IEEE round-to-nearest quotient (s == 0 -> 0), bit-identical to
+// evaluating that division, but with the quotient estimated as v * inv_s
+// (inv_s = 1/s rounded to nearest).  The estimate is within |q| * 2^-23 of the
+// exact quotient and the IEEE quotient within |q| * 2^-24, so both round to the
+// same integer unless the estimate lies within |q| * 1.5 * 2^-23 of a rounding
+// boundary k + 1/2; only then (margin 2^-20 here) is the division evaluated.
+__device__ __forceinline__ int8_t quant_i8_exact(float v, float s, float inv_s) {
+  if (s == 0.0f) return 0;
+  float t = v * inv_s;
+  const float a = fabsf(t);
+  const float f = a - floorf(a);
+  if (fabsf(f - 0.5f) <= a * 9.5367431640625e-07f) t = __fdiv_rn(v, s);  // 2^-20
+  float r = roundf(t);
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+__device__ __forceinline__ float recip_or_zero(float s) { return s == 0.0f ? 0.0f : __frcp_rn(s); }
+
 // Dispatch a runtime dtype onto a template functor taking the element type.
 template <class F>
 void dispatch_dtype(ltm_dtype d, F&& f) {

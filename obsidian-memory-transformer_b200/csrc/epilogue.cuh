@@ -11,8 +11,11 @@
 //   RESID    y = v + R[m,n]                               (FFN-down + block residual)
 //   GATEMIX  g = v (sigmoid applied);  y = s + g*mem + (1-g)*x   (memory integration)
 //   ACC_I32  raw int32 accumulators (exactness probe)
-// and stores 32 outputs with 16-byte vector stores.
+// and stores 32 outputs with 16-byte vector stores (tensor-core kernels stage
+// the tile in shared memory first for coalesced row stores).
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -91,34 +94,39 @@ __device__ __forceinline__ void store32(T* p, const float (&v)[32]) {
   }
 }
 
-// Applies the epilogue to 32 values of row `m`, columns [n0, n0+32) and stores.
-// GATEMIX with ep.colsum: g*x is written to gx_out when given (the caller
-// reduces it across the warp), else added to ep.colsum element by element.
+// Applies the epilogue math to 32 values of row `m`, columns [n0, n0+32);
+// the results stay in v.  GATEMIX with ep.colsum: g*x is written to gx_out
+// when given (the caller reduces it across the warp), else added to
+// ep.colsum element by element.  ACC_I32 leaves the raw bits untouched.
 template <int MODE, class OutT>
-__device__ __forceinline__ void epilogue_store32(const Epilogue& ep, int64_t m, int64_t n0,
-                                                 float (&v)[32], float* gx_out = nullptr) {
-  if constexpr (MODE == kEpiAccI32) {
-    int32_t* o = static_cast<int32_t*>(ep.out) + m * ep.ldo + n0;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      int4 t;
-      t.x = __float_as_int(v[4 * c + 0]);
-      t.y = __float_as_int(v[4 * c + 1]);
-      t.z = __float_as_int(v[4 * c + 2]);
-      t.w = __float_as_int(v[4 * c + 3]);
-      *reinterpret_cast<int4*>(o + 4 * c) = t;
-    }
-    return;
-  } else {
+__device__ __forceinline__ void epilogue_math32(const Epilogue& ep, int64_t m, int64_t n0,
+                                                float (&v)[32], float* gx_out = nullptr) {
+  if constexpr (MODE != kEpiAccI32) {
     const float rs = ep.row_scale ? ep.row_scale[m] : 1.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float x = v[i] * rs;
-      if (ep.col_scale) x = x * __ldg(ep.col_scale + n0 + i);
-      if (ep.bias) x = x + __ldg(ep.bias + n0 + i);
-      if (ep.act == LTM_EPI_GELU) x = gelu_tanh(x);
-      else if (ep.act == LTM_EPI_SIGMOID) x = sigmoid_f(x);
-      v[i] = x;
+    for (int i = 0; i < 32; ++i) v[i] *= rs;
+    if (ep.col_scale) {  // 16-byte aligned (checked by the launchers)
+      const float4* cs = reinterpret_cast<const float4*>(ep.col_scale + n0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 t = __ldg(cs + j);
+        v[4 * j] *= t.x; v[4 * j + 1] *= t.y; v[4 * j + 2] *= t.z; v[4 * j + 3] *= t.w;
+      }
+    }
+    if (ep.bias) {
+      const float4* bs = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 t = __ldg(bs + j);
+        v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+      }
+    }
+    if (ep.act == LTM_EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+    } else if (ep.act == LTM_EPI_SIGMOID) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = sigmoid_f(v[i]);
     }
     if constexpr (MODE == kEpiRope) {
       if (n0 < ep.rope_cols) {
@@ -158,7 +166,104 @@ __device__ __forceinline__ void epilogue_store32(const Epilogue& ep, int64_t m, 
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = s[i] + (1.0f - v[i]) * mem[i];
     }
-    store32(static_cast<OutT*>(ep.out) + m * ep.ldo + n0, v);
+  }
+}
+
+// Converts 32 epilogue values to the output type and writes them (16-byte
+// vectors) to p; ACC_I32 reinterprets v as the raw int32 accumulators.
+template <int MODE, class OutT>
+__device__ __forceinline__ void pack_store32(void* p, const float (&v)[32]) {
+  if constexpr (MODE == kEpiAccI32) {
+    int32_t* o = static_cast<int32_t*>(p);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      int4 t;
+      t.x = __float_as_int(v[4 * c + 0]);
+      t.y = __float_as_int(v[4 * c + 1]);
+      t.z = __float_as_int(v[4 * c + 2]);
+      t.w = __float_as_int(v[4 * c + 3]);
+      *reinterpret_cast<int4*>(o + 4 * c) = t;
+    }
+  } else {
+    store32(static_cast<OutT*>(p), v);
+  }
+}
+
+// Math + direct store of one 32-column row chunk (SIMT kernels).
+template <int MODE, class OutT>
+__device__ __forceinline__ void epilogue_store32(const Epilogue& ep, int64_t m, int64_t n0,
+                                                 float (&v)[32], float* gx_out = nullptr) {
+  epilogue_math32<MODE, OutT>(ep, m, n0, v, gx_out);
+  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
+  pack_store32<MODE, OutT>(static_cast<StoreT*>(ep.out) + m * ep.ldo + n0, v);
+}
+
+// Epilogue of one 128 x BN accumulator tile of a tensor-core kernel (4
+// epilogue warps, warp quarter q = TMEM lanes 32q..32q+31 = tile rows).  The
+// tile is processed in passes of 64 columns: two 32-column TMEM loads, the
+// epilogue math, conversion into this warp's staging rows in shared memory
+// (rows padded by 16 bytes: conflict-free), then coalesced 16-byte stores of
+// the warp's 32 rows x 64 columns (full 128-byte lines).
+constexpr int kEpiPassCols = 64;
+
+template <class StoreT>
+__host__ __device__ constexpr int epi_stage_row_bytes() {
+  return kEpiPassCols * static_cast<int>(sizeof(StoreT)) + 16;
+}
+
+template <int MODE, class OutT, int BN, bool ACC_INT>
+__device__ __forceinline__ void tc_tile_epilogue_passes(const Epilogue& ep, uint32_t tacc, int q,
+                                                        int lane, int64_t m0, int64_t n0, int M,
+                                                        int N, uint8_t* stg) {
+  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
+  constexpr int OB = sizeof(StoreT);
+  constexpr int ROWB = epi_stage_row_bytes<StoreT>();
+  constexpr int CPR = kEpiPassCols * OB / 16;  // 16-byte chunks per staged row
+  constexpr int EPC = 16 / OB;                 // elements per chunk
+  const int64_t m = m0 + q * 32 + lane;
+  StoreT* out = static_cast<StoreT*>(ep.out);
+#pragma unroll 1
+  for (int p = 0; p < BN / kEpiPassCols; ++p) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = p * 2 + h;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tacc + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
+      tmem_wait_ld();
+      const int64_t n = n0 + c * 32;
+      const bool valid = m < M && n < N;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if constexpr (MODE == kEpiAccI32) v[i] = __int_as_float(static_cast<int>(r[i]));
+        else if constexpr (ACC_INT) v[i] = static_cast<float>(static_cast<int>(r[i]));
+        else v[i] = __uint_as_float(r[i]);
+      }
+      if constexpr (MODE == kEpiGateMix) {
+        float gx[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) gx[i] = 0.0f;
+        if (valid) epilogue_math32<MODE, OutT>(ep, m, n, v, gx);
+        if (ep.colsum) {
+          const float cs = warp_colsum32(gx);
+          if (n < N) atomicAdd(ep.colsum + n + lane, cs);
+        }
+      } else {
+        if (valid) epilogue_math32<MODE, OutT>(ep, m, n, v);
+      }
+      pack_store32<MODE, OutT>(stg + lane * ROWB + h * 32 * OB, v);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int idx = lane; idx < 32 * CPR; idx += 32) {
+      const int rr = idx / CPR, ch = idx - rr * CPR;
+      const int64_t gm = m0 + q * 32 + rr;
+      const int64_t gn = n0 + p * kEpiPassCols + ch * EPC;
+      if (gm < M && gn < N)
+        *reinterpret_cast<uint4*>(out + gm * ep.ldo + gn) =
+            *reinterpret_cast<const uint4*>(stg + rr * ROWB + ch * 16);
+    }
+    __syncwarp();
   }
 }
 

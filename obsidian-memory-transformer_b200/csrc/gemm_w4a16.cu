@@ -6,7 +6,7 @@
 //   y      = epilogue(a @ W^T)                  fp32 accumulation in TMEM
 //
 // One CTA computes a 128 x 128 tile; K advances 64 elements (128 bytes) per
-// stage.  Warp roles (192 threads):
+// stage; the epilogue stages the tile in shared memory for coalesced stores.  Warp roles (192 threads):
 //   warp 0      TMA producer: the 128 x 64 activation tile (128-byte swizzle)
 //               and the 128 x 32-byte packed int4 weight tile
 //   warp 1      TMEM allocator + MMA issuer (4 x tcgen05.mma kind::f16, K=16)
@@ -164,35 +164,13 @@ __global__ void __launch_bounds__(192, 2)
         if (!ok) break;
       }
     }
-    // ---- epilogue
-    const bool ok = mbar_wait_bounded(accf, 0, abort_flag, err, kErrWaitAccum);
+    // ---- epilogue: the pipeline stages are free once the accumulator is
+    // complete, so stage 0 doubles as the output staging buffer
+    const bool ok = mbar_wait_bounded(accf, 0, abort_flag, err, kErrWaitAccum) && !*abort_flag;
     tc_fence_after();
-    const int64_t m = static_cast<int64_t>(m0) + q * 32 + lane;
-    if (ok) {
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
-        tmem_wait_ld();
-        const int64_t n = static_cast<int64_t>(n0) + c * 32;
-        const bool valid = m < M && n < N && !*abort_flag;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if constexpr (MODE == kEpiGateMix) {
-          float gx[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) gx[i] = 0.0f;
-          if (valid) epilogue_store32<MODE, T>(ep, m, n, v, gx);
-          if (ep.colsum) {
-            const float cs = warp_colsum32(gx);
-            if (n < N) atomicAdd(ep.colsum + n + lane, cs);
-          }
-        } else {
-          if (valid) epilogue_store32<MODE, T>(ep, m, n, v);
-        }
-      }
-    }
+    if (ok)
+      tc_tile_epilogue_passes<MODE, T, kBN, false>(ep, tmem, q, lane, m0, n0, M, N,
+                                                   smem + q * 32 * epi_stage_row_bytes<T>());
   }
 
   tc_fence_before();
@@ -217,6 +195,7 @@ void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s
   LTM_REQUIRE(mode != kEpiAccI32, "no int32 accumulator mode on the W4A16 path");
   LTM_REQUIRE((reinterpret_cast<uintptr_t>(ep.out) & 15) == 0, "output must be 16-byte aligned");
   LTM_REQUIRE((ep.ldo * 2) % 16 == 0, "output row stride must be a multiple of 16 bytes");
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0, "bias must be 16-byte aligned");
   CUtensorMap ta, tp;
   make_tma_2d(&ta, a, dt == LTM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
               2, M, K, K, kBKe, kBM);

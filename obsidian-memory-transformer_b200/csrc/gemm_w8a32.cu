@@ -123,6 +123,9 @@ void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_
                   (reinterpret_cast<uintptr_t>(ep.out) & 15) == 0,
               "fp32 operands must be 16-byte aligned");
   LTM_REQUIRE(ep.ldo % 4 == 0, "output row stride must be a multiple of 4");
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(ep.col_scale) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0,
+              "weight scales and bias must be 16-byte aligned");
   LTM_REQUIRE(mode != kEpiAccI32, "no int32 accumulator mode on the fp32 path");
   const size_t smem = static_cast<size_t>(kT) * (kT + kPad) * sizeof(float);  // >= 2*kKS*(kT+kPad)
   dim3 grid((N + kT - 1) / kT, (M + kT - 1) / kT);

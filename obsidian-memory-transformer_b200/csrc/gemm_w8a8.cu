@@ -3,13 +3,18 @@
 //   acc[m,n] = sum_k qa[m,k] * qw[n,k]     int8 x int8 -> exact int32 in TMEM
 //   y        = epilogue(acc)                dequant, bias, act, rope/resid/gate-mix
 //
-// One CTA computes a 128 x BN tile.  Warp roles (192 threads):
+// Persistent kernel, one CTA per SM, static round-robin over 128 x BN output
+// tiles (N-tile fastest, so the CTAs in flight share activation rows and the
+// whole weight stays L2-resident).  Warp roles (192 threads):
 //   warp 0      TMA producer: 128 x 128-byte tiles of qa and BN x 128-byte
-//               tiles of qw into a STAGES-deep ring (128-byte swizzle)
-//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8
-//               (K = 32 each) per stage, tcgen05.commit frees the stage
+//               tiles of qw into a STAGES-deep ring (128-byte swizzle); runs
+//               ahead across tile boundaries
+//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32)
+//               per stage into one of two TMEM accumulators (2 x BN columns),
+//               tcgen05.commit frees the stage / publishes the accumulator
 //   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (warp w reads
-//               TMEM lanes 32*(w%4)..+31 = tile rows), fused epilogue, stores
+//               TMEM lanes 32*(w%4)..+31 = tile rows), fused epilogue, staged
+//               coalesced stores; overlaps the next tile's main loop
 // Every mbarrier wait is bounded (common.cuh); an expired wait records a code
 // in the device error word and the CTA unwinds, releasing its TMEM.
 //
@@ -26,33 +31,38 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle row
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, class StoreT>
 struct W8A8Smem {
   static constexpr uint32_t kA = kBM * kBK;
   static constexpr uint32_t kB = BN * kBK;
   static constexpr uint32_t kStage = kA + kB;
-  static constexpr uint32_t kBarOff = STAGES * kStage;
+  static constexpr uint32_t kStgOff = STAGES * kStage;
+  static constexpr uint32_t kStgWarp = 32 * epi_stage_row_bytes<StoreT>();
+  static constexpr uint32_t kBarOff = kStgOff + 4 * kStgWarp;
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
 };
 
 template <int BN, int STAGES, int MODE, class OutT>
-__global__ void __launch_bounds__(192, (BN <= 128 ? 2 : 1))
+__global__ void __launch_bounds__(192, 1)
     w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, Epilogue ep, int* err) {
-  using L = W8A8Smem<BN, STAGES>;
+  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
+  using L = W8A8Smem<BN, STAGES, StoreT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* accf = empty + STAGES;  // [2] accumulator ready
+  uint64_t* acce = accf + 2;        // [2] accumulator drained by the epilogue
+  uint64_t* drain = acce + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * kBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int tiles = ((M + kBM - 1) / kBM) * num_n;
   const int nkb = (K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -60,13 +70,17 @@ __global__ void __launch_bounds__(192, (BN <= 128 ? 2 : 1))
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 4);
+    }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(tslot, BN);
+  if (warp == 1) tmem_alloc(tslot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -74,82 +88,80 @@ __global__ void __launch_bounds__(192, (BN <= 128 ? 2 : 1))
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait_bounded(empty + s, ph ^ 1, abort_flag, err, kErrWaitEmpty)) break;
-        uint8_t* a_dst = smem + s * L::kStage;
-        mbar_arrive_expect_tx(full + s, L::kStage);
-        tma_load_2d(a_dst, &tmA, full + s, kb * kBK, m0);
-        tma_load_2d(a_dst + L::kA, &tmB, full + s, kb * kBK, n0);
-        ++issued;
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_bounded(empty + s, ph ^ 1, abort_flag, err, kErrWaitEmpty)) break;
+          uint8_t* a_dst = smem + s * L::kStage;
+          mbar_arrive_expect_tx(full + s, L::kStage);
+          tma_load_2d(a_dst, &tmA, full + s, kb * kBK, m0);
+          tma_load_2d(a_dst + L::kA, &tmB, full + s, kb * kBK, n0);
+          ++it;
+        }
       }
       if (*abort_flag) {
         // Drain this CTA's copies still in flight before the CTA unwinds.
         volatile int never = 0;
-        for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
           mbar_wait_bounded(full + (j % STAGES), (j / STAGES) & 1, &never, err, kErrWaitOther);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(kBM, BN);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait_bounded(full + s, ph, abort_flag, err, kErrWaitFull)) break;
+      int it = 0, lt = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const int b = lt & 1;
+        const uint32_t use = static_cast<uint32_t>(lt >> 1);
+        if (!mbar_wait_bounded(acce + b, (use & 1) ^ 1, abort_flag, err, kErrWaitAccum)) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
-        const uint32_t b_addr = a_addr + L::kA;
+        const uint32_t tacc = tmem + b * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_bounded(full + s, ph, abort_flag, err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::kStage);
+          const uint32_t b_addr = a_addr + L::kA;
 #pragma unroll
-        for (int k = 0; k < kBK / 32; ++k) {
-          tc_mma_i8(tmem, make_desc_kmajor_sw128(a_addr + k * 32),
-                    make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+          for (int k = 0; k < kBK / 32; ++k) {
+            tc_mma_i8(tacc, make_desc_kmajor_sw128(a_addr + k * 32),
+                      make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+          }
+          tc_commit(empty + s);
+          ++it;
         }
-        tc_commit(empty + s);
+        if (!ok) break;
+        tc_commit(accf + b);
       }
-      tc_commit(accf);
       if (*abort_flag) {
         volatile int never = 0;
-        mbar_wait_bounded(accf, 0, &never, err, kErrWaitOther);
+        tc_commit(drain);
+        mbar_wait_bounded(drain, 0, &never, err, kErrWaitOther);
       }
     }
   } else {
     // Epilogue warpgroup: warps 2..5 -> TMEM lane quarter (warp % 4).
     const int q = warp & 3;
-    const bool ok = mbar_wait_bounded(accf, 0, abort_flag, err, kErrWaitAccum);
-    tc_fence_after();
-    const int64_t m = static_cast<int64_t>(m0) + q * 32 + lane;
-    if (ok) {
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
-        tmem_wait_ld();
-        const int64_t n = static_cast<int64_t>(n0) + c * 32;
-        const bool valid = m < M && n < N && !*abort_flag;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if constexpr (MODE == kEpiAccI32)
-            v[i] = __int_as_float(static_cast<int>(r[i]));
-          else
-            v[i] = static_cast<float>(static_cast<int>(r[i]));
-        }
-        if constexpr (MODE == kEpiGateMix) {
-          float gx[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) gx[i] = 0.0f;
-          if (valid) epilogue_store32<MODE, OutT>(ep, m, n, v, gx);
-          if (ep.colsum) {
-            const float cs = warp_colsum32(gx);
-            if (n < N) atomicAdd(ep.colsum + n + lane, cs);
-          }
-        } else {
-          if (valid) epilogue_store32<MODE, OutT>(ep, m, n, v);
-        }
-      }
+    uint8_t* stg = smem + L::kStgOff + q * L::kStgWarp;
+    int lt = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      const int b = lt & 1;
+      const uint32_t use = static_cast<uint32_t>(lt >> 1);
+      if (!mbar_wait_bounded(accf + b, use & 1, abort_flag, err, kErrWaitAccum)) break;
+      tc_fence_after();
+      const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN;
+      tc_tile_epilogue_passes<MODE, OutT, BN, true>(ep, tmem + b * BN, q, lane, m0, n0, M, N, stg);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce + b);
     }
   }
 
@@ -157,17 +169,23 @@ __global__ void __launch_bounds__(192, (BN <= 128 ? 2 : 1))
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
 template <int BN, int STAGES, int MODE, class OutT>
-void launch_w8a8_inst(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                      const Epilogue& ep, cudaStream_t stream) {
-  using L = W8A8Smem<BN, STAGES>;
+void launch_w8a8_inst(const int8_t* qa, const int8_t* qw, int M, int N, int K, const Epilogue& ep,
+                      cudaStream_t stream) {
+  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
+  using L = W8A8Smem<BN, STAGES, StoreT>;
+  static_assert(L::kBytes <= 232448, "shared memory budget exceeded");
+  CUtensorMap ta, tb;
+  make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
+  make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, BN);
   auto kern = w8a8_tc_kernel<BN, STAGES, MODE, OutT>;
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-  dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
   kern<<<grid, 192, L::kBytes, stream>>>(ta, tb, M, N, K, ep, device_error_ptr());
   check_launch("w8a8_tc_kernel");
 }
@@ -187,19 +205,20 @@ void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64
   const size_t osz = (mode == kEpiAccI32) ? 4 : dtype_size(out_dt);
   LTM_REQUIRE((reinterpret_cast<uintptr_t>(ep.out) & 15) == 0, "output must be 16-byte aligned");
   LTM_REQUIRE((ep.ldo * osz) % 16 == 0, "output row stride must be a multiple of 16 bytes");
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(ep.col_scale) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0,
+              "weight scales and bias must be 16-byte aligned");
   if (mode == kEpiResid || mode == kEpiGateMix) {
     LTM_REQUIRE((ep.ld_aux * osz) % 16 == 0, "aux row stride must be a multiple of 16 bytes");
   }
-  constexpr int BN = 128;
-  constexpr int STAGES = 3;
-  CUtensorMap ta, tb;
-  make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
-  make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, BN);
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   dispatch_epilogue(mode, out_dt, [&](auto mode_c, auto out_tag) {
     constexpr int MODE = decltype(mode_c)::value;
     using OutT = decltype(out_tag);
-    launch_w8a8_inst<BN, STAGES, MODE, OutT>(ta, tb, static_cast<int>(M), static_cast<int>(N),
-                                             static_cast<int>(K), ep, stream);
+    if (N % 256 == 0)
+      launch_w8a8_inst<256, 3, MODE, OutT>(qa, qw, m, n, k, ep, stream);
+    else
+      launch_w8a8_inst<128, 4, MODE, OutT>(qa, qw, m, n, k, ep, stream);
   });
 }
 

@@ -7,6 +7,8 @@
 // y = (v - mean) * rsqrt(var + eps) * gamma + beta.  One CTA per row, each
 // thread owns one 16-byte vector of the row in registers, so the row is read
 // from HBM exactly once; reductions are warp shuffles + one shared-memory hop.
+#include <type_traits>
+
 #include "block.cuh"
 
 namespace ltm_b200 {
@@ -40,18 +42,12 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return t;
 }
 
-__device__ __forceinline__ int8_t q8(float v, float s) {
-  if (s == 0.0f) return 0;
-  float r = roundf(__fdiv_rn(v, s));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
-}
 
 template <class T, int V>
-__device__ __forceinline__ void store_q(int8_t* dst, const float (&v)[V], float s) {
+__device__ __forceinline__ void store_q(int8_t* dst, const float (&v)[V], float s, float inv) {
   int8_t o[V];
 #pragma unroll
-  for (int i = 0; i < V; ++i) o[i] = q8(v[i], s);
+  for (int i = 0; i < V; ++i) o[i] = quant_i8_exact(v[i], s, inv);
   if constexpr (V == 8)
     *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
   else
@@ -97,7 +93,7 @@ __global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x,
     for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[i]));
     am = block_max<NW>(am, red);
     const float s = __fdiv_rn(am, 127.0f);
-    if (active) store_q<T, V>(xq + row * H + e0, xv, s);
+    if (active) store_q<T, V>(xq + row * H + e0, xv, s, recip_or_zero(s));
     if (threadIdx.x == 0) xs[row] = s;
   }
   float yv[V];
@@ -140,8 +136,154 @@ __global__ void __launch_bounds__(NW * 32) ln_x2_kernel(const T* __restrict__ x,
     }
     am = block_max<NW>(am, red);
     const float s = __fdiv_rn(am, 127.0f);
-    if (active) store_q<T, V>(yq + row * H + e0, yv, s);
+    if (active) store_q<T, V>(yq + row * H + e0, yv, s, recip_or_zero(s));
     if (threadIdx.x == 0) ys[row] = s;
+  }
+}
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per row, the row resident in registers: lane l owns the 16-byte
+// vectors l, l+32, ... (NV of them).  Same arithmetic as ln_x2_kernel; all
+// reductions are warp shuffles, 8 rows per CTA.  SAME: residual == x.
+template <class T, int NV, bool SAME>
+__global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x,
+                                                         const T* __restrict__ res, int64_t rows,
+                                                         int H, const float* __restrict__ gamma,
+                                                         const float* __restrict__ beta,
+                                                         T* __restrict__ y, int8_t* __restrict__ yq,
+                                                         float* __restrict__ ys,
+                                                         int8_t* __restrict__ xq,
+                                                         float* __restrict__ xs, int do_norm) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = H / V;
+  // xv holds x; sv holds x + residual (the LN input) unless SAME
+  float xv[NV][V], sv[SAME ? 1 : NV][V];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int vi = lane + 32 * j;
+    if (vi < nvec) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + row * H) + vi);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < V; ++i) xv[j][i] = to_f32(e[i]);
+      if constexpr (!SAME) {
+        uint4 rr = __ldg(reinterpret_cast<const uint4*>(res + row * H) + vi);
+        const T* er = reinterpret_cast<const T*>(&rr);
+#pragma unroll
+        for (int i = 0; i < V; ++i) sv[j][i] = xv[j][i] + to_f32(er[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) xv[j][i] = 0.0f;
+      if constexpr (!SAME) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) sv[j][i] = 0.0f;
+      }
+    }
+  }
+  auto lnin = [&](int j, int i) -> float {
+    if constexpr (SAME) return xv[j][i] + xv[j][i];
+    else return sv[j][i];
+  };
+  if (xq) {
+    float am = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[j][i]));
+    am = warp_max_f(am);
+    const float s = __fdiv_rn(am, 127.0f);
+    const float inv = recip_or_zero(s);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int vi = lane + 32 * j;
+      if (vi < nvec) store_q<T, V>(xq + row * H + vi * V, xv[j], s, inv);
+    }
+    if (lane == 0) xs[row] = s;
+  }
+  if (do_norm) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int i = 0; i < V; ++i) sum += lnin(j, i);
+    const float mean = warp_sum_f(sum) / static_cast<float>(H);
+    float sq = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      if (lane + 32 * j < nvec) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+          const float d = lnin(j, i) - mean;
+          sq += d * d;
+        }
+      }
+    }
+    const float var = warp_sum_f(sq) / static_cast<float>(H);
+    const float rstd = rsqrtf(var + 1e-5f);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int vi = lane + 32 * j;
+      const int c0 = vi < nvec ? vi * V : 0;
+      float gv[V], bv[V];
+#pragma unroll
+      for (int i = 0; i < V; i += 4) {  // gamma / beta are 16-byte aligned (checked by the launcher)
+        const float4 g4 = __ldg(reinterpret_cast<const float4*>(gamma + c0 + i));
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(beta + c0 + i));
+        gv[i] = g4.x; gv[i + 1] = g4.y; gv[i + 2] = g4.z; gv[i + 3] = g4.w;
+        bv[i] = b4.x; bv[i + 1] = b4.y; bv[i + 2] = b4.z; bv[i + 3] = b4.w;
+      }
+#pragma unroll
+      for (int i = 0; i < V; ++i) xv[j][i] = (lnin(j, i) - mean) * rstd * gv[i] + bv[i];
+    }
+  } else if constexpr (!SAME) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int i = 0; i < V; ++i) xv[j][i] = sv[j][i];
+  }
+  if (y) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int vi = lane + 32 * j;
+      if (vi < nvec) {
+        uint4 raw;
+        T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+        for (int i = 0; i < V; ++i) e[i] = from_f32<T>(xv[j][i]);
+        *(reinterpret_cast<uint4*>(y + row * H) + vi) = raw;
+      }
+    }
+  }
+  if (yq) {
+    float am = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (lane + 32 * j < nvec)
+#pragma unroll
+        for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[j][i]));
+    am = warp_max_f(am);
+    const float s = __fdiv_rn(am, 127.0f);
+    const float inv = recip_or_zero(s);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int vi = lane + 32 * j;
+      if (vi < nvec) store_q<T, V>(yq + row * H + vi * V, xv[j], s, inv);
+    }
+    if (lane == 0) ys[row] = s;
   }
 }
 
@@ -174,11 +316,34 @@ void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float*
   LTM_REQUIRE(H % V == 0, "hidden size must be a multiple of 16 bytes");
   const int threads = ((H / V + 31) / 32) * 32;
   LTM_REQUIRE(threads <= 1024, "hidden size too large for the row-resident LayerNorm");
+  LTM_REQUIRE(!do_norm || ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0,
+              "LayerNorm gamma / beta must be 16-byte aligned");
+  const int nv = (H / V + 31) / 32;  // 16-byte vectors per lane, warp-per-row layout
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
-    ln_x2_kernel<T, 32><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
-        static_cast<const T*>(x), static_cast<const T*>(residual ? residual : x), H, gamma, beta,
-        static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
+    const T* xt = static_cast<const T*>(x);
+    const T* rt = static_cast<const T*>(residual ? residual : x);
+    const unsigned wblocks = static_cast<unsigned>((rows + 7) / 8);
+    auto warp_launch = [&](auto nv_c) {
+      constexpr int NV = decltype(nv_c)::value;
+      if (rt == xt)
+        ln_x2_warp_kernel<T, NV, true><<<wblocks, 256, 0, stream>>>(
+            xt, rt, rows, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
+      else
+        ln_x2_warp_kernel<T, NV, false><<<wblocks, 256, 0, stream>>>(
+            xt, rt, rows, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
+    };
+    switch (nv) {
+      case 1: warp_launch(std::integral_constant<int, 1>{}); break;
+      case 2: warp_launch(std::integral_constant<int, 2>{}); break;
+      case 3: warp_launch(std::integral_constant<int, 3>{}); break;
+      case 4: warp_launch(std::integral_constant<int, 4>{}); break;
+      case 5: case 6: warp_launch(std::integral_constant<int, 6>{}); break;
+      case 7: case 8: warp_launch(std::integral_constant<int, 8>{}); break;
+      default:
+        ln_x2_kernel<T, 32><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
+            xt, rt, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
+    }
   });
   check_launch("ln_x2_kernel");
 }

@@ -3,10 +3,13 @@
 //
 // Bandwidth-bound: one warp owns one row (INT8) or one 128-element group
 // (INT4); loads are 128-bit where the row layout allows, reductions are warp
-// shuffles.  Division and rounding are IEEE round-to-nearest division
-// (__fdiv_rn) followed by round-half-away-from-zero (roundf), the arithmetic
-// of the reference kernels src/core/quantization/quantizer.cu:94-142, so the
-// codes are bit-exact against a CPU evaluation of the same formula.
+// shuffles.  Codes equal IEEE round-to-nearest division followed by
+// round-half-away-from-zero (roundf), the arithmetic of the reference kernels
+// src/core/quantization/quantizer.cu:94-142, so they are bit-exact against a
+// CPU evaluation of the same formula (INT8 uses the reciprocal fast path of
+// quant_i8_exact, which falls back to the division near rounding ties).
+#include <type_traits>
+
 #include "block.cuh"
 
 namespace ltm_b200 {
@@ -28,12 +31,6 @@ __device__ __forceinline__ float warp_min(float v) {
   return v;
 }
 
-__device__ __forceinline__ int8_t quant_sym_i8(float v, float s) {
-  if (s == 0.0f) return 0;
-  float r = roundf(__fdiv_rn(v, s));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
-}
 
 // One warp per row: s = absmax/127, q = clamp(round(x/s)).
 template <class T, bool VEC>
@@ -58,12 +55,13 @@ __global__ void __launch_bounds__(256) rowwise_int8_kernel(const T* __restrict__
     }
     amax = warp_max(amax);
     const float s = __fdiv_rn(amax, 127.0f);
+    const float inv = recip_or_zero(s);
     for (int64_t j = lane; j < nv; j += 32) {
       uint4 raw = __ldg(xv + j);
       const T* e = reinterpret_cast<const T*>(&raw);
       int8_t out[V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) out[i] = quant_sym_i8(to_f32(e[i]), s);
+      for (int i = 0; i < V; ++i) out[i] = quant_i8_exact(to_f32(e[i]), s, inv);
       if constexpr (V == 8) {
         *reinterpret_cast<uint2*>(qr + j * V) = *reinterpret_cast<const uint2*>(out);
       } else {
@@ -75,9 +73,56 @@ __global__ void __launch_bounds__(256) rowwise_int8_kernel(const T* __restrict__
     for (int64_t j = lane; j < K; j += 32) amax = fmaxf(amax, fabsf(to_f32(xr[j])));
     amax = warp_max(amax);
     const float s = __fdiv_rn(amax, 127.0f);
-    for (int64_t j = lane; j < K; j += 32) qr[j] = quant_sym_i8(to_f32(xr[j]), s);
+    const float inv = recip_or_zero(s);
+    for (int64_t j = lane; j < K; j += 32) qr[j] = quant_i8_exact(to_f32(xr[j]), s, inv);
     if (lane == 0) scales[row] = s;
   }
+}
+
+// Register-resident variant: lane l holds the 16-byte vectors l, l+32, ...
+// (NV of them), so the row is read from HBM once with all its loads in flight.
+template <class T, int NV>
+__global__ void __launch_bounds__(256) rowwise_int8_reg_kernel(const T* __restrict__ x, int64_t rows,
+                                                               int64_t K, int8_t* __restrict__ q,
+                                                               float* __restrict__ scales) {
+  constexpr int V = Vec16<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = static_cast<int>(K / V);
+  const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
+  uint4 raw[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int vi = lane + 32 * j;
+    raw[j] = vi < nvec ? __ldg(xv + vi) : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const T* e = reinterpret_cast<const T*>(&raw[j]);
+#pragma unroll
+    for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(to_f32(e[i])));
+  }
+  amax = warp_max(amax);
+  const float s = __fdiv_rn(amax, 127.0f);
+  const float inv = recip_or_zero(s);
+  int8_t* qr = q + row * K;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int vi = lane + 32 * j;
+    if (vi < nvec) {
+      const T* e = reinterpret_cast<const T*>(&raw[j]);
+      int8_t out[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = quant_i8_exact(to_f32(e[i]), s, inv);
+      if constexpr (V == 8)
+        *reinterpret_cast<uint2*>(qr + vi * V) = *reinterpret_cast<const uint2*>(out);
+      else
+        *reinterpret_cast<uint32_t*>(qr + vi * V) = *reinterpret_cast<const uint32_t*>(out);
+    }
+  }
+  if (lane == 0) scales[row] = s;
 }
 
 template <class T>
@@ -178,7 +223,22 @@ void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, i
     using T = decltype(tag);
     const bool vec = ((K * sizeof(T)) % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
-    if (vec)
+    const int64_t nv = (K / Vec16<T>::N + 31) / 32;
+    auto reg_launch = [&](auto nv_c) {
+      constexpr int NV = decltype(nv_c)::value;
+      rowwise_int8_reg_kernel<T, NV><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K,
+                                                                 q, s);
+    };
+    if (vec && nv <= 16) {
+      if (nv <= 1) reg_launch(std::integral_constant<int, 1>{});
+      else if (nv <= 2) reg_launch(std::integral_constant<int, 2>{});
+      else if (nv <= 3) reg_launch(std::integral_constant<int, 3>{});
+      else if (nv <= 4) reg_launch(std::integral_constant<int, 4>{});
+      else if (nv <= 6) reg_launch(std::integral_constant<int, 6>{});
+      else if (nv <= 8) reg_launch(std::integral_constant<int, 8>{});
+      else if (nv <= 12) reg_launch(std::integral_constant<int, 12>{});
+      else reg_launch(std::integral_constant<int, 16>{});
+    } else if (vec)
       rowwise_int8_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
     else
       rowwise_int8_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
