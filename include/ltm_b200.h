@@ -170,6 +170,24 @@ LTM_API ltm_status ltm_attention_forward(const void* q, int64_t ldq, const void*
                                          int Sq, int Skv, int64_t kv_batch_rows, int num_heads,
                                          int head_dim, int causal, ltm_dtype dtype, void* stream);
 
+/* Memory-bank write: MemoryBank<T>::store (src/core/ltm/memory_bank.cu:39-68,
+ * 242-274: every slot blends towards the stored state with weight
+ * update_rate * score[slot]) with the slot scores of the TB-v1 write:
+ *   qbar     = mean over the T rows of `queries`            (memory queries Q_m)
+ *   score[s] = mean over heads h of softmax_s(qbar_h . keys[s]_h / sqrt(head_dim))
+ *   w_s      = update_rate * score[s]   (update_rate alone when use_attention_scores = 0)
+ *   memory[s,:] = (1 - w_s) * memory[s,:] + w_s * state
+ * memory: [memory_slots, hidden_dim] in dtype, updated in place; keys: rows of
+ * stride ldk (the bank's memory keys K_M); queries: [T, ldq]; state: fp32
+ * [hidden_dim] (the pooled gated input mean_t g_t * x_t).  The query column
+ * sums and slot weights live in library-owned device scratch, allocated on the
+ * first call per device and grown on demand.  memory_slots <= 51200. */
+LTM_API ltm_status ltm_memory_store(void* memory, const void* keys, int64_t ldk,
+                                    const void* queries, int64_t ldq, int64_t T,
+                                    const float* state, int memory_slots, int hidden_dim,
+                                    int num_heads, float update_rate, int use_attention_scores,
+                                    ltm_dtype dtype, void* stream);
+
 /* ----------------------------------------------------------------- block -- */
 /* Field-for-field mirror of ltm::transformer::TitanBlockConfig
  * (include/core/transformer/titan_inspired_block.cuh:19-50): same names, same

@@ -59,6 +59,17 @@ struct MemoryWriteState {
                    cudaStream_t st);
 };
 
+// Memory-bank store: slot weights from the mean of the query rows against the
+// keys (use_scores) and the EMA of every slot towards state * state_scale.
+// qsum [H] and wslot [Ms] are fp32 scratch, cleared here.
+void launch_memory_store(void* memory, const void* keys, int64_t ldk, const void* queries,
+                         int64_t ldq, int64_t T, const float* state, float state_scale, int Ms,
+                         int H, int nh, float rate, bool use_scores, ltm_dtype dt, float* qsum,
+                         float* wslot, cudaStream_t st);
+void validate_memory_store(const void* memory, const void* keys, int64_t ldk, const void* queries,
+                           int64_t ldq, int64_t T, const float* state, int Ms, int H, int nh,
+                           bool use_scores);
+
 void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, int8_t* q, float* s,
                          cudaStream_t stream);
 void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,

@@ -10,6 +10,10 @@
 // (src/core/ltm/memory_bank.cu:39-68,242-274: EMA with weight
 // update_rate * attention_score[slot], state broadcast to every slot) with the
 // pooled state of the paper's compression (mean over the segment).
+#include <memory>
+#include <mutex>
+#include <vector>
+
 #include "block.cuh"
 
 namespace ltm_b200 {
@@ -79,15 +83,16 @@ __global__ void __launch_bounds__(256) slot_weight_kernel(const float* __restric
 
 template <class T>
 __global__ void __launch_bounds__(256) bank_update_kernel(T* __restrict__ mem,
-                                                          const float* __restrict__ colsum,
-                                                          float inv_T, const float* __restrict__ wslot,
+                                                          const float* __restrict__ state,
+                                                          float state_scale,
+                                                          const float* __restrict__ wslot,
                                                           float rate, int Ms, int H) {
   const int64_t n = static_cast<int64_t>(Ms) * H;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int s = static_cast<int>(i / H), j = static_cast<int>(i - static_cast<int64_t>(s) * H);
     const float w = wslot ? wslot[s] : rate;
-    const float c = colsum[j] * inv_T;
+    const float c = state[j] * state_scale;
     mem[i] = from_f32<T>((1.0f - w) * to_f32(mem[i]) + w * c);
   }
 }
@@ -100,39 +105,108 @@ void MemoryWriteState::prepare_gate_epilogue(Epilogue& ep, int H, cudaStream_t s
   ep.colsum = colsum.as<float>();
 }
 
-void MemoryWriteState::update_bank(void* memory, const void* kvm, const void* qm, int64_t ldq,
-                                   int64_t T, int H, int nh, int dh, int Ms, float rate,
-                                   bool use_scores, ltm_dtype dt, cudaStream_t st) {
-  if (T == 0) return;
-  const float inv_T = 1.0f / static_cast<float>(T);
+void launch_memory_store(void* memory, const void* keys, int64_t ldk, const void* queries,
+                         int64_t ldq, int64_t T, const float* state, float state_scale, int Ms,
+                         int H, int nh, float rate, bool use_scores, ltm_dtype dt, float* qsum,
+                         float* wslot, cudaStream_t st) {
+  if (Ms == 0 || H == 0) return;
+  const int dh = H / nh;
   dispatch_dtype(dt, [&](auto tag) {
     using TT = decltype(tag);
     const float* w = nullptr;
     if (use_scores) {
-      qsum.ensure(H * sizeof(float));
-      wslot.ensure(Ms * sizeof(float));
-      LTM_CUDA_TRY(cudaMemsetAsync(qsum.ptr, 0, H * sizeof(float), st));
-      LTM_CUDA_TRY(cudaMemsetAsync(wslot.ptr, 0, Ms * sizeof(float), st));
+      LTM_CUDA_TRY(cudaMemsetAsync(qsum, 0, H * sizeof(float), st));
+      LTM_CUDA_TRY(cudaMemsetAsync(wslot, 0, Ms * sizeof(float), st));
       const int splits = static_cast<int>(std::min<int64_t>(64, (T + 63) / 64));
       dim3 g1((H + 31) / 32, splits);
-      colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(qm), ldq, T, H, qsum.as<float>());
+      colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(queries), ldq, T, H, qsum);
       check_launch("colsum_kernel");
       const size_t smem = static_cast<size_t>(Ms) * sizeof(float);
-      LTM_REQUIRE(smem <= 200 * 1024, "memory_slots too large for the slot-weight kernel");
       auto kern = slot_weight_kernel<TT>;
       LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)));
-      kern<<<nh, 256, smem, st>>>(qsum.as<float>(), inv_T, static_cast<const TT*>(kvm), 2 * H, Ms,
-                                  dh, nh, rate, wslot.as<float>());
+      kern<<<nh, 256, smem, st>>>(qsum, 1.0f / static_cast<float>(T), static_cast<const TT*>(keys),
+                                  ldk, Ms, dh, nh, rate, wslot);
       check_launch("slot_weight_kernel");
-      w = wslot.as<float>();
+      w = wslot;
     }
     const int64_t n = static_cast<int64_t>(Ms) * H;
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
-    bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), colsum.as<float>(),
-                                                 inv_T, w, rate, Ms, H);
+    bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale, w,
+                                                 rate, Ms, H);
     check_launch("bank_update_kernel");
   });
 }
 
+void validate_memory_store(const void* memory, const void* keys, int64_t ldk, const void* queries,
+                           int64_t ldq, int64_t T, const float* state, int Ms, int H, int nh,
+                           bool use_scores) {
+  LTM_REQUIRE(Ms >= 0 && H >= 0 && T >= 0, "negative size");
+  LTM_REQUIRE(memory && state, "NULL pointer");
+  LTM_REQUIRE(nh > 0 && H % nh == 0, "hidden size must be a multiple of num_heads");
+  if (use_scores) {
+    LTM_REQUIRE(T > 0, "attention-score slot weights need at least one query row");
+    LTM_REQUIRE(keys && queries, "NULL keys / queries");
+    LTM_REQUIRE(ldk >= H && ldq >= H, "row strides smaller than the hidden size");
+    LTM_REQUIRE(static_cast<size_t>(Ms) * sizeof(float) <= 200 * 1024,
+                "memory_slots too large for the slot-weight kernel (max 51200)");
+  }
+}
+
+void MemoryWriteState::update_bank(void* memory, const void* kvm, const void* qm, int64_t ldq,
+                                   int64_t T, int H, int nh, int dh, int Ms, float rate,
+                                   bool use_scores, ltm_dtype dt, cudaStream_t st) {
+  (void)dh;
+  if (T == 0) return;
+  if (use_scores) {
+    qsum.ensure(H * sizeof(float));
+    wslot.ensure(Ms * sizeof(float));
+  }
+  validate_memory_store(memory, kvm, 2 * H, qm, ldq, T, colsum.as<float>(), Ms, H, nh, use_scores);
+  launch_memory_store(memory, kvm, 2 * H, qm, ldq, T, colsum.as<float>(),
+                      1.0f / static_cast<float>(T), Ms, H, nh, rate, use_scores, dt,
+                      qsum.as<float>(), wslot.as<float>(), st);
+}
+
+namespace {
+// Per-device scratch of ltm_memory_store (query column sums [H], slot weights
+// [Ms]); grown on demand, freed at exit.
+struct StoreScratch {
+  DevBuf qsum, wslot;
+};
+StoreScratch& store_scratch(int dev) {
+  static std::mutex mu;
+  static std::vector<std::unique_ptr<StoreScratch>> per_dev;
+  std::lock_guard<std::mutex> lk(mu);
+  if (static_cast<int>(per_dev.size()) <= dev) per_dev.resize(dev + 1);
+  if (!per_dev[dev]) per_dev[dev] = std::make_unique<StoreScratch>();
+  return *per_dev[dev];
+}
+}  // namespace
+
 }  // namespace ltm_b200
+
+using namespace ltm_b200;
+
+extern "C" ltm_status ltm_memory_store(void* memory, const void* keys, int64_t ldk,
+                                       const void* queries, int64_t ldq, int64_t T,
+                                       const float* state, int memory_slots, int hidden_dim,
+                                       int num_heads, float update_rate, int use_attention_scores,
+                                       ltm_dtype dtype, void* stream) {
+  return guarded([&] {
+    const bool scores = use_attention_scores != 0;
+    validate_memory_store(memory, keys, ldk, queries, ldq, T, state, memory_slots, hidden_dim,
+                          num_heads, scores);
+    if (memory_slots == 0 || hidden_dim == 0) return;
+    int dev = 0;
+    LTM_CUDA_TRY(cudaGetDevice(&dev));
+    StoreScratch& sc = store_scratch(dev);
+    if (scores) {
+      sc.qsum.ensure(static_cast<size_t>(hidden_dim) * sizeof(float));
+      sc.wslot.ensure(static_cast<size_t>(memory_slots) * sizeof(float));
+    }
+    launch_memory_store(memory, keys, ldk, queries, ldq, T, state, 1.0f, memory_slots, hidden_dim,
+                        num_heads, update_rate, scores, dtype, sc.qsum.as<float>(),
+                        sc.wslot.as<float>(), as_stream(stream));
+  });
+}

@@ -85,6 +85,7 @@ def _declare(L):
         "ltm_layernorm_residual": ([vp, vp, vp, vp, vp, ci, i64, i64, vp], ci),
         "ltm_attention_forward": ([vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, i64, ci, ci, ci,
                                    ci, vp], ci),
+        "ltm_memory_store": ([vp, vp, i64, vp, i64, i64, vp, ci, ci, ci, C.c_float, ci, ci, vp], ci),
         "ltm_block_config_default": ([C.POINTER(BlockConfigC)], None),
         "ltm_block_create": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), ci,
                               C.POINTER(vp)], ci),
@@ -305,6 +306,22 @@ def attention(q, k, v, B: int, Sq: int, Skv: int, num_heads: int, head_dim: int,
                                        0 if kv_shared else Skv, num_heads, head_dim, int(causal),
                                        dtype_code(q.dtype), _stream(stream)))
     return out
+
+
+def memory_store(memory, keys, queries, state, num_heads: int, update_rate: float = 0.9,
+                 use_attention_scores: bool = True, stream=None):
+    """MemoryBank::store: updates memory [Ms,H] in place (see ltm_memory_store).
+    keys / queries: CUDA tensors with unit column stride (rows may be strided);
+    state: fp32 [H]."""
+    for t in (memory, keys, queries, state):
+        if not t.is_cuda or t.stride(-1) != 1:
+            raise ValueError("memory_store operands must be CUDA tensors with unit column stride")
+    Ms, H = memory.shape
+    _check(lib().ltm_memory_store(_ptr(memory), _ptr(keys), keys.stride(0), _ptr(queries),
+                                  queries.stride(0), queries.shape[0], _ptr(state), Ms, H,
+                                  num_heads, update_rate, int(use_attention_scores),
+                                  dtype_code(memory.dtype), _stream(stream)))
+    return memory
 
 
 # --------------------------------------------------------------------- block --

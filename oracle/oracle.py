@@ -69,6 +69,7 @@ def _declare(L):
         "orc_layernorm_x2": ([f, i64, i64, f, f, f], None),
         "orc_rope_table": ([ci, ci, f], None),
         "orc_attention": ([f, i64, f, f, i64, ci, ci, ci, ci, ci, ci, ci, ci, f, i64], None),
+        "orc_memory_store": ([f, f, i64, f, i64, i64, f, ci, ci, ci, C.c_float, ci, ci], None),
         "orc_block_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci], ci),
         "orc_model_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), _p(f), ci, f, ci, i32, f, ci,
                                ci], ci),
@@ -207,6 +208,16 @@ def attention(q, k, v, B, Sq, Skv, nh, dh, causal, dtype, kv_shared=False):
     lib().orc_attention(_ptr(q), q.shape[1], _ptr(k), _ptr(v), k.shape[1], B, Sq, Skv,
                         0 if kv_shared else Skv, nh, dh, int(causal), dtype, _ptr(out), nh * dh)
     return out
+
+
+def memory_store(memory, keys, queries, state, nh: int, rate: float, use_scores: bool, dtype: int):
+    """memory [Ms,H] (returned updated copy); keys [Ms, >=H]; queries [T, >=H]; state [H]."""
+    mem = np.array(memory, dtype=np.float32, copy=True, order="C")
+    keys, queries, state = _f32(keys), _f32(queries), _f32(state)
+    Ms, H = mem.shape
+    lib().orc_memory_store(_ptr(mem), _ptr(keys), keys.shape[1], _ptr(queries), queries.shape[1],
+                           queries.shape[0], _ptr(state), Ms, H, nh, rate, int(use_scores), dtype)
+    return mem
 
 
 def _cfg(c: dict) -> OrcBlockCfg:

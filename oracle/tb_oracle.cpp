@@ -334,6 +334,40 @@ std::vector<float> concat_rows(const float* a, int64_t na, const float* b, int64
 
 }  // namespace
 
+extern "C" void orc_memory_store(float* memory, const float* keys, int64_t ldk,
+                                 const float* queries, int64_t ldq, int64_t T, const float* state,
+                                 int Ms, int H, int nh, float rate, int use_scores, int dtype) {
+  // MemoryBank<T>::store / storeStateKernel, src/core/ltm/memory_bank.cu:39-68,242-274
+  const int dh = H / nh;
+  std::vector<float> wsl(Ms, rate);
+  if (use_scores) {
+    std::vector<double> qbar(H, 0.0);
+    for (int64_t t = 0; t < T; ++t)
+      for (int j = 0; j < H; ++j) qbar[j] += queries[t * ldq + j];
+    for (int j = 0; j < H; ++j) qbar[j] /= static_cast<double>(T);
+    std::vector<double> a(Ms, 0.0), sc(Ms);
+    const double scale = 1.0 / std::sqrt(static_cast<double>(dh));
+    for (int hh = 0; hh < nh; ++hh) {
+      double mx = -1e300;
+      for (int s = 0; s < Ms; ++s) {
+        double d = 0;
+        for (int e = 0; e < dh; ++e) d += qbar[hh * dh + e] * keys[static_cast<int64_t>(s) * ldk + hh * dh + e];
+        sc[s] = d * scale;
+        mx = std::max(mx, sc[s]);
+      }
+      double den = 0;
+      for (int s = 0; s < Ms; ++s) den += std::exp(sc[s] - mx);
+      for (int s = 0; s < Ms; ++s) a[s] += std::exp(sc[s] - mx) / den;
+    }
+    for (int s = 0; s < Ms; ++s) wsl[s] = rate * static_cast<float>(a[s] / nh);
+  }
+  for (int s = 0; s < Ms; ++s)
+    for (int j = 0; j < H; ++j) {
+      float& mv = memory[static_cast<int64_t>(s) * H + j];
+      mv = rnd((1.0f - wsl[s]) * mv + wsl[s] * state[j], dtype);
+    }
+}
+
 extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights* w,
                                  float* memory_inout, const float* x, float* y, int B, int S) {
   const int H = c->H, F = c->F, nh = c->nh, dh = c->dh, Ms = c->Ms;
@@ -439,34 +473,10 @@ extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights
     std::vector<double> cacc(H, 0.0);
     for (int64_t t = 0; t < T; ++t)
       for (int j = 0; j < H; ++j) cacc[j] += static_cast<double>(g[t * H + j]) * x[t * H + j];
-    std::vector<float> wsl(Ms, c->update_rate);
-    if (c->use_attention_scores) {
-      std::vector<double> qbar(H, 0.0);
-      for (int64_t t = 0; t < T; ++t)
-        for (int j = 0; j < H; ++j) qbar[j] += qkvm[t * 4 * H + 3 * H + j];
-      for (int j = 0; j < H; ++j) qbar[j] /= static_cast<double>(T);
-      std::vector<double> a(Ms, 0.0), sc(Ms);
-      const double scale = 1.0 / std::sqrt(static_cast<double>(dh));
-      for (int hh = 0; hh < nh; ++hh) {
-        double mx = -1e300;
-        for (int s = 0; s < Ms; ++s) {
-          double d = 0;
-          for (int e = 0; e < dh; ++e) d += qbar[hh * dh + e] * kvm[static_cast<int64_t>(s) * 2 * H + hh * dh + e];
-          sc[s] = d * scale;
-          mx = std::max(mx, sc[s]);
-        }
-        double den = 0;
-        for (int s = 0; s < Ms; ++s) den += std::exp(sc[s] - mx);
-        for (int s = 0; s < Ms; ++s) a[s] += std::exp(sc[s] - mx) / den;
-      }
-      for (int s = 0; s < Ms; ++s) wsl[s] = c->update_rate * static_cast<float>(a[s] / nh);
-    }
-    for (int s = 0; s < Ms; ++s)
-      for (int j = 0; j < H; ++j) {
-        const float cj = static_cast<float>(cacc[j] / static_cast<double>(T));
-        float& mv = memory_inout[static_cast<int64_t>(s) * H + j];
-        mv = rnd((1.0f - wsl[s]) * mv + wsl[s] * cj, dt);
-      }
+    std::vector<float> state(H);
+    for (int j = 0; j < H; ++j) state[j] = static_cast<float>(cacc[j] / static_cast<double>(T));
+    orc_memory_store(memory_inout, kvm.data(), 2 * H, qkvm.data() + 3 * H, 4 * H, T, state.data(),
+                     Ms, H, nh, c->update_rate, c->use_attention_scores, dt);
   }
   return 0;
 }

@@ -66,6 +66,13 @@ void orc_attention(const float* q, int64_t ldq, const float* k, const float* v, 
                    int B, int Sq, int Skv, int kv_batch_stride_rows, int nh, int dh, int causal,
                    int dtype, float* out, int64_t ldo);
 
+/* memory-bank store: slot weights from the mean query row against the keys
+ * (use_scores) or update_rate; memory[s,:] = (1-w_s) memory[s,:] + w_s state,
+ * rounded to dtype.  keys rows of stride ldk, queries [T, ldq], state [H]. */
+void orc_memory_store(float* memory, const float* keys, int64_t ldk, const float* queries,
+                      int64_t ldq, int64_t T, const float* state, int Ms, int H, int nh,
+                      float rate, int use_scores, int dtype);
+
 typedef struct orc_block_cfg {
   int H, F, nh, dh, Ms;
   int scheme;    /* ORC_W8A32 / ORC_W8A8 / ORC_W4A16 */

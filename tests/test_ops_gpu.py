@@ -88,3 +88,38 @@ def test_linear_w4a16(ltm, orc, dt, act, M, N, K):
     ref = orc.round_to(orc.linear_w4a16(as_f32(ad), packed, s, zp, b, act, orc_dtype(dt)),
                        orc_dtype(dt))
     assert_close(as_f32(y), ref, 2e-2, 1e-2, f"w4a16 {dt}")
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("scores", [True, False])
+@pytest.mark.parametrize("Ms,H,nh,T", [(64, 256, 4, 96), (512, 768, 12, 2048), (2048, 4096, 32, 64)])
+def test_memory_store(ltm, orc, dt, scores, Ms, H, nh, T):
+    """MemoryBank::store: slot weights from the mean memory query, EMA of the bank."""
+    import torch
+    rng = np.random.default_rng(Ms + H + T)
+    mem = (rng.standard_normal((Ms, H)) / np.sqrt(H)).astype(np.float32)
+    kv = rng.standard_normal((Ms, 2 * H)).astype(np.float32)
+    qkvm = rng.standard_normal((T, 4 * H)).astype(np.float32)
+    qkvm[:, 3 * H:] += 2.0 * rng.standard_normal(H).astype(np.float32)  # a shared query direction
+    state = (0.3 * rng.standard_normal(H)).astype(np.float32)
+    memd, kvd, qd = to_device(mem, dt), to_device(kv, dt), to_device(qkvm, dt)
+    mem0 = as_f32(memd)
+    rate = 0.5
+    ltm.memory_store(memd, kvd[:, :H], qd[:, 3 * H:], torch.from_numpy(state).cuda(), nh, rate,
+                     scores)
+    ref = orc.memory_store(mem0, as_f32(kvd)[:, :H], as_f32(qd)[:, 3 * H:], state, nh, rate,
+                           scores, orc_dtype(dt))
+    atol, rtol = (1e-5, 1e-4) if dt == "f32" else (2e-3, 1e-2)
+    assert_close(as_f32(memd), ref, atol, rtol, what=f"memory store {dt}")
+    assert np.abs(ref - mem0).max() > (1e-4 if scores else 1e-2)  # the bank moved
+    assert ltm.device_error() == 0
+
+
+def test_memory_store_rejects_bad_arguments(ltm):
+    import torch
+    mem = torch.zeros((8, 64), device="cuda")
+    state = torch.zeros(64, device="cuda")
+    with pytest.raises(ltm.LtmError):
+        ltm.memory_store(mem, mem, mem[:0], state, 4, 0.9, True)  # no query rows
+    with pytest.raises(ltm.LtmError):
+        ltm.memory_store(mem, mem, mem, state, 3, 0.9, True)  # 64 % 3 != 0
