@@ -188,6 +188,24 @@ LTM_API ltm_status ltm_memory_store(void* memory, const void* keys, int64_t ldk,
                                     int num_heads, float update_rate, int use_attention_scores,
                                     ltm_dtype dtype, void* stream);
 
+/* Allocation-free variant of ltm_memory_store (same arguments, same result).
+ * It has no counterpart in the reference.  It is for callers that cannot let
+ * a library allocate device memory at call time -- a framework that plans all
+ * device memory itself, a server whose device footprint must stay fixed after
+ * start-up, a latency-critical loop where cudaMalloc would stall the device.
+ * Its scratch is one fixed 256 KiB device array per GPU that loads the library
+ * (held until exit), so hidden_dim rounded up to 64 plus memory_slots must not
+ * exceed 65536 (else LTM_ERR_INVALID_ARG).  All calls share that array and
+ * clear it at their start: calls whose GPU work overlaps (other streams or
+ * unordered host threads) race.  The first call on a device looks up the
+ * array's device address; make it before any stream capture. */
+LTM_API ltm_status ltm_memory_store_noalloc(void* memory, const void* keys, int64_t ldk,
+                                            const void* queries, int64_t ldq, int64_t T,
+                                            const float* state, int memory_slots,
+                                            int hidden_dim, int num_heads, float update_rate,
+                                            int use_attention_scores, ltm_dtype dtype,
+                                            void* stream);
+
 /* ----------------------------------------------------------------- block -- */
 /* Field-for-field mirror of ltm::transformer::TitanBlockConfig
  * (include/core/transformer/titan_inspired_block.cuh:19-50): same names, same

@@ -86,6 +86,8 @@ def _declare(L):
         "ltm_attention_forward": ([vp, i64, vp, i64, vp, i64, vp, i64, ci, ci, ci, i64, ci, ci, ci,
                                    ci, vp], ci),
         "ltm_memory_store": ([vp, vp, i64, vp, i64, i64, vp, ci, ci, ci, C.c_float, ci, ci, vp], ci),
+        "ltm_memory_store_noalloc": ([vp, vp, i64, vp, i64, i64, vp, ci, ci, ci, C.c_float, ci,
+                                      ci, vp], ci),
         "ltm_block_config_default": ([C.POINTER(BlockConfigC)], None),
         "ltm_block_create": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), ci,
                               C.POINTER(vp)], ci),
@@ -321,6 +323,22 @@ def memory_store(memory, keys, queries, state, num_heads: int, update_rate: floa
                                   queries.stride(0), queries.shape[0], _ptr(state), Ms, H,
                                   num_heads, update_rate, int(use_attention_scores),
                                   dtype_code(memory.dtype), _stream(stream)))
+    return memory
+
+
+def memory_store_noalloc(memory, keys, queries, state, num_heads: int, update_rate: float = 0.9,
+                         use_attention_scores: bool = True, stream=None):
+    """memory_store without any device allocation by the library (for callers
+    that own all device memory themselves): scratch is a fixed 256 KiB device
+    array, so round_up(H, 64) + Ms <= 65536; overlapping calls race on it."""
+    for t in (memory, keys, queries, state):
+        if not t.is_cuda or t.stride(-1) != 1:
+            raise ValueError("memory_store operands must be CUDA tensors with unit column stride")
+    Ms, H = memory.shape
+    _check(lib().ltm_memory_store_noalloc(_ptr(memory), _ptr(keys), keys.stride(0), _ptr(queries),
+                                          queries.stride(0), queries.shape[0], _ptr(state), Ms, H,
+                                          num_heads, update_rate, int(use_attention_scores),
+                                          dtype_code(memory.dtype), _stream(stream)))
     return memory
 
 

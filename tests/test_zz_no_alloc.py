@@ -1,0 +1,71 @@
+"""The allocation-free memory-bank store, called through the C ABI.
+
+ltm_memory_store_noalloc exists for callers that cannot let the library
+allocate device memory while they run (they plan every device byte
+themselves, or must keep a fixed footprint).  It keeps its scratch in one
+fixed device array that every call reuses, so this file checks it against the
+allocating entry point ltm_memory_store on two calls in a row (the second
+call must not see the first call's leftovers) and checks the size limit.
+It is collected last so a stop-at-first-failure run has covered everything
+else first, and it passes alone in a fresh process as well.
+"""
+import numpy as np
+import pytest
+
+from _util import as_f32, assert_close, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(seed, Ms, H, T, dt):
+    rng = np.random.default_rng(seed)
+    mem = (rng.standard_normal((Ms, H)) / np.sqrt(H)).astype(np.float32)
+    kv = rng.standard_normal((Ms, 2 * H)).astype(np.float32)
+    q = rng.standard_normal((T, 4 * H)).astype(np.float32)
+    q[:, 3 * H:] += 2.0 * rng.standard_normal(H).astype(np.float32)
+    state = (0.3 * rng.standard_normal(H)).astype(np.float32)
+    return to_device(mem, dt), to_device(kv, dt), to_device(q, dt), state
+
+
+def _call_c_abi(ltm, fn, mem, keys, queries, state, nh, rate, scores):
+    import torch
+    st = torch.from_numpy(state).cuda()
+    Ms, H = mem.shape
+    status = fn(ltm._ptr(mem), ltm._ptr(keys), keys.stride(0), ltm._ptr(queries), queries.stride(0),
+                queries.shape[0], ltm._ptr(st), Ms, H, nh, rate, int(scores),
+                ltm.dtype_code(mem.dtype), ltm._stream())
+    ltm._check(status)
+    torch.cuda.synchronize()
+    return as_f32(mem)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_noalloc_store_matches_allocating_store_twice(ltm, dt):
+    lib = ltm.lib()
+    H, nh = 768, 12
+    atol, rtol = (1e-5, 1e-4) if dt == "f32" else (2e-3, 1e-2)
+    # two calls in a row with different inputs and sizes: the shared scratch
+    # must be cleared by each call
+    for call, (Ms, T, scores, rate, seed) in enumerate([(512, 256, True, 0.5, 1),
+                                                        (384, 64, True, 0.9, 2)]):
+        mem, kv, q, state = _inputs(seed, Ms, H, T, dt)
+        mem_ref = mem.clone()
+        want = _call_c_abi(ltm, lib.ltm_memory_store, mem_ref, kv[:, :H], q[:, 3 * H:], state, nh,
+                           rate, scores)
+        got = _call_c_abi(ltm, lib.ltm_memory_store_noalloc, mem, kv[:, :H], q[:, 3 * H:], state,
+                          nh, rate, scores)
+        assert_close(got, want, atol, rtol, what=f"no-alloc store, call {call + 1}")
+        assert ltm.device_error() == 0
+
+
+def test_noalloc_store_rejects_sizes_beyond_its_scratch(ltm):
+    import torch
+    H, Ms = 4096, 65536 - 4096 + 1  # round_up(H, 64) + Ms = 65537 > 65536
+    mem = torch.zeros((Ms, H), dtype=torch.bfloat16, device="cuda")
+    keys = torch.zeros((Ms, H), dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros((4, H), dtype=torch.bfloat16, device="cuda")
+    state = torch.zeros(H, dtype=torch.float32, device="cuda")
+    with pytest.raises(ltm.LtmError) as e:
+        ltm.memory_store_noalloc(mem, keys, q, state, 32, 0.9, False)
+    assert e.value.status == ltm.ERR_INVALID_ARG
+    assert "scratch" in str(e.value)
