@@ -124,6 +124,35 @@ __device__ __forceinline__ int8_t quant_i8_exact(float v, float s, float inv_s) 
 
 __device__ __forceinline__ float recip_or_zero(float s) { return s == 0.0f ? 0.0f : __frcp_rn(s); }
 
+// Warp-cooperative form of quant_i8_exact for V values per lane; must be
+// called by all 32 lanes (lanes without data pass zeros).  Off the rounding
+// ties round-half-even (cvt.rni) equals round-half-away, so the common path is
+// one multiply and one convert; only when some lane of the warp holds a value
+// near a tie does the warp evaluate the IEEE quotients (warp-uniform branch).
+template <int V>
+__device__ __forceinline__ void quant_i8_exact_warp(const float (&v)[V], float s, float inv_s,
+                                                    int8_t (&out)[V]) {
+  float t[V];
+  bool near_tie = false;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    t[i] = v[i] * inv_s;
+    const float a = fabsf(t[i]);
+    near_tie |= fabsf((a - floorf(a)) - 0.5f) <= a * 9.5367431640625e-07f;  // 2^-20
+  }
+  if (__any_sync(0xffffffffu, near_tie)) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) out[i] = quant_i8_exact(v[i], s, inv_s);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    int q = __float2int_rn(t[i]);
+    q = max(-127, min(127, q));
+    out[i] = static_cast<int8_t>(s == 0.0f ? 0 : q);
+  }
+}
+
 // Dispatch a runtime dtype onto a template functor taking the element type.
 template <class F>
 void dispatch_dtype(ltm_dtype d, F&& f) {

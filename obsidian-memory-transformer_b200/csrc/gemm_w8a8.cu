@@ -5,16 +5,17 @@
 //
 // Persistent kernel, one CTA per SM, static round-robin over 128 x BN output
 // tiles (N-tile fastest, so the CTAs in flight share activation rows and the
-// whole weight stays L2-resident).  Warp roles (192 threads):
+// whole weight stays L2-resident).  Warp roles (320 threads):
 //   warp 0      TMA producer: 128 x 128-byte tiles of qa and BN x 128-byte
 //               tiles of qw into a STAGES-deep ring (128-byte swizzle); runs
 //               ahead across tile boundaries
 //   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma kind::i8 (K = 32)
 //               per stage into one of two TMEM accumulators (2 x BN columns),
 //               tcgen05.commit frees the stage / publishes the accumulator
-//   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (warp w reads
-//               TMEM lanes 32*(w%4)..+31 = tile rows), fused epilogue, staged
-//               coalesced stores; overlaps the next tile's main loop
+//   warps 2..9  epilogue (two warpgroups, each half of the tile's columns):
+//               tcgen05.ld of the int32 accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows), fused epilogue, staged coalesced
+//               stores; overlaps the next tile's main loop
 // Every mbarrier wait is bounded (common.cuh); an expired wait records a code
 // in the device error word and the CTA unwinds, releasing its TMEM.
 //
@@ -30,6 +31,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle row
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN, int STAGES, class StoreT>
 struct W8A8Smem {
@@ -38,12 +41,12 @@ struct W8A8Smem {
   static constexpr uint32_t kStage = kA + kB;
   static constexpr uint32_t kStgOff = STAGES * kStage;
   static constexpr uint32_t kStgWarp = 32 * epi_stage_row_bytes<StoreT>();
-  static constexpr uint32_t kBarOff = kStgOff + 4 * kStgWarp;
+  static constexpr uint32_t kBarOff = kStgOff + kEpiWarps * kStgWarp;
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
 };
 
 template <int BN, int STAGES, int MODE, class OutT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, Epilogue ep, int* err) {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
@@ -72,7 +75,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf + b, 1);
-      mbar_init(acce + b, 4);
+      mbar_init(acce + b, kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -148,17 +151,20 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // Epilogue warpgroup: warps 2..5 -> TMEM lane quarter (warp % 4).
+    // Epilogue warps 2..9: TMEM lane quarter q = warp % 4, column half
+    // (warp - 2) / 4 of the tile.
     const int q = warp & 3;
-    uint8_t* stg = smem + L::kStgOff + q * L::kStgWarp;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
     int lt = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
       const int b = lt & 1;
       const uint32_t use = static_cast<uint32_t>(lt >> 1);
       if (!mbar_wait_bounded(accf + b, use & 1, abort_flag, err, kErrWaitAccum)) break;
       tc_fence_after();
-      const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN;
-      tc_tile_epilogue_passes<MODE, OutT, BN, true>(ep, tmem + b * BN, q, lane, m0, n0, M, N, stg);
+      const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN + half * (BN / 2);
+      tc_tile_epilogue_passes<MODE, OutT, BN / 2, true>(ep, tmem + b * BN + half * (BN / 2), q, lane,
+                                                        m0, n0, M, N, stg);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce + b);
@@ -186,7 +192,7 @@ void launch_w8a8_inst(const int8_t* qa, const int8_t* qw, int M, int N, int K, c
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
-  kern<<<grid, 192, L::kBytes, stream>>>(ta, tb, M, N, K, ep, device_error_ptr());
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, M, N, K, ep, device_error_ptr());
   check_launch("w8a8_tc_kernel");
 }
 

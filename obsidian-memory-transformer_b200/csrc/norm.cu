@@ -43,6 +43,19 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 }
 
 
+// Warp-uniform quantize + store of V values (all lanes call; `valid` lanes store).
+template <int V>
+__device__ __forceinline__ void store_q_warp(int8_t* dst, const float (&v)[V], float s, float inv,
+                                             bool valid) {
+  int8_t o[V];
+  quant_i8_exact_warp<V>(v, s, inv, o);
+  if (!valid) return;
+  if constexpr (V == 8)
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+  else
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(o);
+}
+
 template <class T, int V>
 __device__ __forceinline__ void store_q(int8_t* dst, const float (&v)[V], float s, float inv) {
   int8_t o[V];
@@ -210,7 +223,7 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int vi = lane + 32 * j;
-      if (vi < nvec) store_q<T, V>(xq + row * H + vi * V, xv[j], s, inv);
+      store_q_warp<V>(xq + row * H + vi * V, xv[j], s, inv, vi < nvec);
     }
     if (lane == 0) xs[row] = s;
   }
@@ -269,19 +282,23 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
     }
   }
   if (yq) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (lane + 32 * j >= nvec)
+#pragma unroll
+        for (int i = 0; i < V; ++i) xv[j][i] = 0.0f;
     float am = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j)
-      if (lane + 32 * j < nvec)
 #pragma unroll
-        for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[j][i]));
+      for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[j][i]));
     am = warp_max_f(am);
     const float s = __fdiv_rn(am, 127.0f);
     const float inv = recip_or_zero(s);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int vi = lane + 32 * j;
-      if (vi < nvec) store_q<T, V>(yq + row * H + vi * V, xv[j], s, inv);
+      store_q_warp<V>(yq + row * H + vi * V, xv[j], s, inv, vi < nvec);
     }
     if (lane == 0) ys[row] = s;
   }

@@ -109,13 +109,15 @@ __global__ void __launch_bounds__(256) rowwise_int8_reg_kernel(const T* __restri
   const float inv = recip_or_zero(s);
   int8_t* qr = q + row * K;
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
+  for (int j = 0; j < NV; ++j) {  // warp-uniform: all lanes take part in the vote
     const int vi = lane + 32 * j;
-    if (vi < nvec) {
-      const T* e = reinterpret_cast<const T*>(&raw[j]);
-      int8_t out[V];
+    const T* e = reinterpret_cast<const T*>(&raw[j]);
+    float f[V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) out[i] = quant_i8_exact(to_f32(e[i]), s, inv);
+    for (int i = 0; i < V; ++i) f[i] = to_f32(e[i]);
+    int8_t out[V];
+    quant_i8_exact_warp<V>(f, s, inv, out);
+    if (vi < nvec) {
       if constexpr (V == 8)
         *reinterpret_cast<uint2*>(qr + vi * V) = *reinterpret_cast<const uint2*>(out);
       else
