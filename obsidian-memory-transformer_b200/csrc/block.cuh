@@ -85,6 +85,8 @@ void launch_embed_gather(const void* table, ltm_dtype dt, int vocab, int H, cons
                          int64_t T, void* out, cudaStream_t stream);
 void launch_attention(const AttnParams& p, int B, int D, bool causal, ltm_dtype dt,
                       cudaStream_t stream);
+void launch_attention_tc(const AttnParams& p, int B, int D, bool causal, ltm_dtype dt,
+                         cudaStream_t stream);
 void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n, ltm_dtype dt,
                  cudaStream_t stream);
 void upload_f32_as(const float* host, int64_t n, ltm_dtype dt, void* dev, cudaStream_t stream);

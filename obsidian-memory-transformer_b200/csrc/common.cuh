@@ -334,6 +334,21 @@ __device__ __forceinline__ uint64_t make_desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor of an MN-major operand tile stored with the
+// 128-byte swizzle: rows of 128 bytes (64 16-bit elements) along M/N, one row
+// per K index, 8-row groups 1024 bytes apart (stride byte offset), further
+// 64-element M/N chunks `lbo_bytes` apart (leading byte offset).  This is the
+// layout a SWIZZLE_128B TMA box of [K rows x 64 elements] produces.
+__device__ __forceinline__ uint64_t make_desc_mnmajor_sw128(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
 // Instruction descriptor of tcgen05.mma kind::i8 (signed x signed -> s32),
 // both operands K-major, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
@@ -346,10 +361,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 
 // Instruction descriptor of tcgen05.mma kind::f16 (f16 or bf16 inputs, fp32
 // accumulate), both operands K-major.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b_mn_major = false) {
   return (1u << 4)                                   // D format: f32
          | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
-         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+         ((b_mn_major ? 1u : 0u) << 16)               // B major: 0 = K, 1 = MN
+         | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // -------------------------------------------------------- TMA descriptors --
