@@ -54,13 +54,6 @@ enum AttnBar : int {
 };
 
 
-// 2^x with the hardware approximation (MUFU.EX2, flush-to-zero); 2^-inf = 0.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // Two floats rounded to a packed pair of 16-bit values (one paired convert).
 template <class T>
 __device__ __forceinline__ uint32_t pack2_16(float lo, float hi) {

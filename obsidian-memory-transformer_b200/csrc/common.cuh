@@ -153,6 +153,13 @@ __device__ __forceinline__ void quant_i8_exact_warp(const float (&v)[V], float s
   }
 }
 
+// 2^x with the hardware approximation (MUFU.EX2, flush-to-zero); 2^-inf = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Dispatch a runtime dtype onto a template functor taking the element type.
 template <class F>
 void dispatch_dtype(ltm_dtype d, F&& f) {
@@ -166,6 +173,19 @@ void dispatch_dtype(ltm_dtype d, F&& f) {
 
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
+
+// Grid size of a persistent kernel: resident CTAs per SM (from the occupancy
+// calculator for this kernel, block size and dynamic smem) x SMs, capped at
+// `want` (the CTAs the problem needs).
+template <class K>
+int persistent_grid(K kernel, int block, size_t smem, int64_t want) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t cap = static_cast<int64_t>(per_sm) * device_sm_count();
+  return static_cast<int>(want < cap ? (want < 1 ? 1 : want) : cap);
+}
 
 // ------------------------------------------------------- PTX: sync/timing --
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -61,13 +61,19 @@ __device__ __forceinline__ float warp_colsum32(float (&v)[32]) {
   return v[0];
 }
 
+// GELU, tanh approximation of src/core/ops/fused_ops.cu:136-142:
+//   x * 0.5 * (1 + tanh(z)),  z = 0.797885 * (x + 0.044715 x^3),
+// evaluated through 0.5 * (1 + tanh(z)) = 1 / (1 + 2^(-2 z log2(e))) with the
+// hardware 2^x and a fast division (relative error ~1e-6 against tanhf).
 __device__ __forceinline__ float gelu_tanh(float x) {
-  // src/core/ops/fused_ops.cu:136-142
-  const float cdf = 0.5f * (1.0f + tanhf(0.797885f * (x + 0.044715f * x * x * x)));
-  return x * cdf;
+  const float z = 0.797885f * (x + 0.044715f * x * x * x);
+  return __fdividef(x, 1.0f + ex2_approx(-2.8853900817779268f * z));
 }
 
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+// 1 / (1 + e^-x) through the hardware 2^x.
+__device__ __forceinline__ float sigmoid_f(float x) {
+  return __fdividef(1.0f, 1.0f + ex2_approx(-1.4426950408889634f * x));
+}
 
 template <class T>
 __device__ __forceinline__ void load32(const T* p, float (&v)[32]) {
@@ -130,13 +136,14 @@ __device__ __forceinline__ void epilogue_math32(const Epilogue& ep, int64_t m, i
     }
     if constexpr (MODE == kEpiRope) {
       if (n0 < ep.rope_cols) {
+        // a 32-column chunk never crosses a head (head_dim is a multiple of 32)
         const int half = ep.head_dim >> 1;
-        const int pos = static_cast<int>(m % ep.seq_len);
-        const float2* tab = ep.rope + static_cast<int64_t>(pos) * half;
+        const int pos = static_cast<int>(static_cast<uint32_t>(m) % static_cast<uint32_t>(ep.seq_len));
+        const int d0 = static_cast<int>(static_cast<uint32_t>(n0) % static_cast<uint32_t>(ep.head_dim));
+        const float2* tab = ep.rope + static_cast<int64_t>(pos) * half + (d0 >> 1);
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const int d = static_cast<int>((n0 + i) % ep.head_dim);
-          const float2 cs = __ldg(tab + (d >> 1));
+          const float2 cs = __ldg(tab + (i >> 1));
           const float a = v[i], b = v[i + 1];
           v[i] = a * cs.x - b * cs.y;
           v[i + 1] = a * cs.y + b * cs.x;

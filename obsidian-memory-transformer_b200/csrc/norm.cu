@@ -167,7 +167,8 @@ __device__ __forceinline__ float warp_max_f(float v) {
 
 // One warp per row, the row resident in registers: lane l owns the 16-byte
 // vectors l, l+32, ... (NV of them).  Same arithmetic as ln_x2_kernel; all
-// reductions are warp shuffles, 8 rows per CTA.  SAME: residual == x.
+// reductions are warp shuffles.  Persistent grid (8 warps per CTA, grid-stride
+// over rows) with the next row prefetched.  SAME: residual == x.
 template <class T, int NV, bool SAME>
 __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x,
                                                          const T* __restrict__ res, int64_t rows,
@@ -179,32 +180,36 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
                                                          float* __restrict__ xs, int do_norm) {
   constexpr int V = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * 8;
   const int nvec = H / V;
+  // persistent: the next row's loads are in flight while this row is processed
+  constexpr int NR = SAME ? 1 : NV;
+  uint4 cx[NV], cr[NR], nx[NV], nr[NR];
+  auto load = [&](int64_t rr, uint4 (&ax)[NV], uint4 (&ar)[NR]) {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int vi = lane + 32 * j;
+      ax[j] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(x + rr * H) + vi) : make_uint4(0, 0, 0, 0);
+      if constexpr (!SAME)
+        ar[j] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(res + rr * H) + vi)
+                          : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (g0 < rows) load(g0, cx, cr);
+  for (int64_t row = g0; row < rows; row += gstride) {
+  if (row + gstride < rows) load(row + gstride, nx, nr);
   // xv holds x; sv holds x + residual (the LN input) unless SAME
   float xv[NV][V], sv[SAME ? 1 : NV][V];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int vi = lane + 32 * j;
-    if (vi < nvec) {
-      uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + row * H) + vi);
-      const T* e = reinterpret_cast<const T*>(&raw);
+    const T* e = reinterpret_cast<const T*>(&cx[j]);
 #pragma unroll
-      for (int i = 0; i < V; ++i) xv[j][i] = to_f32(e[i]);
-      if constexpr (!SAME) {
-        uint4 rr = __ldg(reinterpret_cast<const uint4*>(res + row * H) + vi);
-        const T* er = reinterpret_cast<const T*>(&rr);
+    for (int i = 0; i < V; ++i) xv[j][i] = to_f32(e[i]);
+    if constexpr (!SAME) {
+      const T* er = reinterpret_cast<const T*>(&cr[j]);
 #pragma unroll
-        for (int i = 0; i < V; ++i) sv[j][i] = xv[j][i] + to_f32(er[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < V; ++i) xv[j][i] = 0.0f;
-      if constexpr (!SAME) {
-#pragma unroll
-        for (int i = 0; i < V; ++i) sv[j][i] = 0.0f;
-      }
+      for (int i = 0; i < V; ++i) sv[j][i] = xv[j][i] + to_f32(er[i]);
     }
   }
   auto lnin = [&](int j, int i) -> float {
@@ -302,6 +307,12 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
     }
     if (lane == 0) ys[row] = s;
   }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    cx[j] = nx[j];
+    if constexpr (!SAME) cr[j] = nr[j];
+  }
+  }  // rows
 }
 
 template <class T>
@@ -340,15 +351,18 @@ void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float*
     using T = decltype(tag);
     const T* xt = static_cast<const T*>(x);
     const T* rt = static_cast<const T*>(residual ? residual : x);
-    const unsigned wblocks = static_cast<unsigned>((rows + 7) / 8);
+    const int64_t want_blocks = (rows + 7) / 8;
     auto warp_launch = [&](auto nv_c) {
       constexpr int NV = decltype(nv_c)::value;
-      if (rt == xt)
-        ln_x2_warp_kernel<T, NV, true><<<wblocks, 256, 0, stream>>>(
+      if (rt == xt) {
+        auto kern = ln_x2_warp_kernel<T, NV, true>;
+        kern<<<persistent_grid(kern, 256, 0, want_blocks), 256, 0, stream>>>(
             xt, rt, rows, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
-      else
-        ln_x2_warp_kernel<T, NV, false><<<wblocks, 256, 0, stream>>>(
+      } else {
+        auto kern = ln_x2_warp_kernel<T, NV, false>;
+        kern<<<persistent_grid(kern, 256, 0, want_blocks), 256, 0, stream>>>(
             xt, rt, rows, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
+      }
     };
     switch (nv) {
       case 1: warp_launch(std::integral_constant<int, 1>{}); break;

@@ -79,52 +79,79 @@ __global__ void __launch_bounds__(256) rowwise_int8_kernel(const T* __restrict__
   }
 }
 
-// Register-resident variant: lane l holds the 16-byte vectors l, l+32, ...
-// (NV of them), so the row is read from HBM once with all its loads in flight.
+// Persistent row quantizers with the next row's loads in flight while the
+// current row is reduced and quantized.  WPR warps share one row (WPR = 1:
+// every warp owns its rows; WPR = 4: a 128-thread CTA owns a row and reduces
+// the row max through shared memory); lane l of the row group holds the
+// 16-byte vectors l, l + 32*WPR, ... (NV of them).
 template <class T, int NV>
-__global__ void __launch_bounds__(256) rowwise_int8_reg_kernel(const T* __restrict__ x, int64_t rows,
-                                                               int64_t K, int8_t* __restrict__ q,
-                                                               float* __restrict__ scales) {
-  constexpr int V = Vec16<T>::N;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int nvec = static_cast<int>(K / V);
+__device__ __forceinline__ void load_row_vecs(const T* __restrict__ x, int64_t row, int64_t K,
+                                              int nvec, int gl, int stride, uint4 (&raw)[NV]) {
   const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
-  uint4 raw[NV];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int vi = lane + 32 * j;
+    const int vi = gl + stride * j;
     raw[j] = vi < nvec ? __ldg(xv + vi) : make_uint4(0, 0, 0, 0);
   }
-  float amax = 0.0f;
+}
+
+template <class T, int NV, int WPR>
+__global__ void __launch_bounds__(WPR == 1 ? 256 : 128) rowwise_int8_pipe_kernel(
+    const T* __restrict__ x, int64_t rows, int64_t K, int8_t* __restrict__ q,
+    float* __restrict__ scales) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int STRIDE = 32 * WPR;
+  __shared__ float red[2][WPR];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gl = (WPR == 1) ? lane : static_cast<int>(threadIdx.x);  // lane within the row group
+  const int64_t groups_per_cta = (WPR == 1) ? (blockDim.x >> 5) : 1;
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * groups_per_cta + (WPR == 1 ? warp : 0);
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * groups_per_cta;
+  const int nvec = static_cast<int>(K / V);
+  uint4 cur[NV], nxt[NV];
+  if (g0 < rows) load_row_vecs<T, NV>(x, g0, K, nvec, gl, STRIDE, cur);
+  int parity = 0;
+  for (int64_t row = g0; row < rows; row += gstride) {
+    const int64_t next = row + gstride;
+    if (next < rows) load_row_vecs<T, NV>(x, next, K, nvec, gl, STRIDE, nxt);
+    float amax = 0.0f;
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const T* e = reinterpret_cast<const T*>(&raw[j]);
+    for (int j = 0; j < NV; ++j) {
+      const T* e = reinterpret_cast<const T*>(&cur[j]);
 #pragma unroll
-    for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(to_f32(e[i])));
-  }
-  amax = warp_max(amax);
-  const float s = __fdiv_rn(amax, 127.0f);
-  const float inv = recip_or_zero(s);
-  int8_t* qr = q + row * K;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {  // warp-uniform: all lanes take part in the vote
-    const int vi = lane + 32 * j;
-    const T* e = reinterpret_cast<const T*>(&raw[j]);
-    float f[V];
-#pragma unroll
-    for (int i = 0; i < V; ++i) f[i] = to_f32(e[i]);
-    int8_t out[V];
-    quant_i8_exact_warp<V>(f, s, inv, out);
-    if (vi < nvec) {
-      if constexpr (V == 8)
-        *reinterpret_cast<uint2*>(qr + vi * V) = *reinterpret_cast<const uint2*>(out);
-      else
-        *reinterpret_cast<uint32_t*>(qr + vi * V) = *reinterpret_cast<const uint32_t*>(out);
+      for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(to_f32(e[i])));
     }
+    amax = warp_max(amax);
+    if constexpr (WPR > 1) {
+      if (lane == 0) red[parity][warp] = amax;
+      __syncthreads();
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) amax = fmaxf(amax, red[parity][w]);
+      parity ^= 1;
+    }
+    const float s = __fdiv_rn(amax, 127.0f);
+    const float inv = recip_or_zero(s);
+    int8_t* qr = q + row * K;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int vi = gl + STRIDE * j;
+      const T* e = reinterpret_cast<const T*>(&cur[j]);
+      float f[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) f[i] = to_f32(e[i]);
+      int8_t out[V];
+      quant_i8_exact_warp<V>(f, s, inv, out);
+      if (vi < nvec) {
+        if constexpr (V == 8)
+          *reinterpret_cast<uint2*>(qr + vi * V) = *reinterpret_cast<const uint2*>(out);
+        else
+          *reinterpret_cast<uint32_t*>(qr + vi * V) = *reinterpret_cast<const uint32_t*>(out);
+      }
+    }
+    if (gl == 0) scales[row] = s;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) cur[j] = nxt[j];
   }
-  if (lane == 0) scales[row] = s;
 }
 
 template <class T>
@@ -225,21 +252,32 @@ void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, i
     using T = decltype(tag);
     const bool vec = ((K * sizeof(T)) % 16 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(q) & 7) == 0);
-    const int64_t nv = (K / Vec16<T>::N + 31) / 32;
-    auto reg_launch = [&](auto nv_c) {
+    const int64_t nvec = K / Vec16<T>::N;
+    auto warp_launch = [&](auto nv_c) {  // one warp per row, 8 rows per CTA in flight
       constexpr int NV = decltype(nv_c)::value;
-      rowwise_int8_reg_kernel<T, NV><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K,
-                                                                 q, s);
+      auto kern = rowwise_int8_pipe_kernel<T, NV, 1>;
+      const int grid = persistent_grid(kern, 256, 0, (rows + 7) / 8);
+      kern<<<grid, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
     };
-    if (vec && nv <= 16) {
-      if (nv <= 1) reg_launch(std::integral_constant<int, 1>{});
-      else if (nv <= 2) reg_launch(std::integral_constant<int, 2>{});
-      else if (nv <= 3) reg_launch(std::integral_constant<int, 3>{});
-      else if (nv <= 4) reg_launch(std::integral_constant<int, 4>{});
-      else if (nv <= 6) reg_launch(std::integral_constant<int, 6>{});
-      else if (nv <= 8) reg_launch(std::integral_constant<int, 8>{});
-      else if (nv <= 12) reg_launch(std::integral_constant<int, 12>{});
-      else reg_launch(std::integral_constant<int, 16>{});
+    auto cta_launch = [&](auto nv_c) {  // four warps per row
+      constexpr int NV = decltype(nv_c)::value;
+      auto kern = rowwise_int8_pipe_kernel<T, NV, 4>;
+      const int grid = persistent_grid(kern, 128, 0, rows);
+      kern<<<grid, 128, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
+    };
+    if (vec && nvec <= 4 * 32) {
+      const int64_t nv = (nvec + 31) / 32;
+      if (nv <= 1) warp_launch(std::integral_constant<int, 1>{});
+      else if (nv <= 2) warp_launch(std::integral_constant<int, 2>{});
+      else if (nv <= 3) warp_launch(std::integral_constant<int, 3>{});
+      else warp_launch(std::integral_constant<int, 4>{});
+    } else if (vec && nvec <= 8 * 128) {
+      const int64_t nv = (nvec + 127) / 128;
+      if (nv <= 2) cta_launch(std::integral_constant<int, 2>{});
+      else if (nv <= 3) cta_launch(std::integral_constant<int, 3>{});
+      else if (nv <= 4) cta_launch(std::integral_constant<int, 4>{});
+      else if (nv <= 6) cta_launch(std::integral_constant<int, 6>{});
+      else cta_launch(std::integral_constant<int, 8>{});
     } else if (vec)
       rowwise_int8_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
     else
