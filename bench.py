@@ -150,6 +150,22 @@ def per_layer_ops():
     ]
 
 
+def step_work(layers: int) -> dict:
+    """Algorithmic work of one step per kernel class: int8/bf16 ops of the
+    GEMMs and attention (2 per multiply-add), bytes of the bandwidth kernels."""
+    B, S, H, F, Ms, nh = WL["B"], WL["S"], WL["H"], WL["F"], WL["Ms"], WL["nh"]
+    T, dh = B * S, WL["H"] // WL["nh"]
+    gemm = 2.0 * (T * 4 * H * H + Ms * 2 * H * H + 3 * T * H * H + T * F * H + T * H * F)
+    attn = 4.0 * B * nh * dh * (S * (S + 1) / 2 + S * Ms)
+    # LN: f16 row in, int8 of LN(x) and of x out (LN1) / int8 out (LN2) + scales
+    ln = (2 * T * H + 2 * T * H + 8 * T) + (2 * T * H + T * H + 4 * T)
+    quant = 2 * (3 * T * H + 4 * T) + (3 * T * F + 4 * T) + (3 * Ms * H + 4 * Ms)
+    return {"w8a8_tc_kernel": {"amount": gemm * layers, "unit": "flop"},
+            "attn_tc_kernel": {"amount": attn * layers, "unit": "flop"},
+            "ln_x2_kernel": {"amount": ln * layers, "unit": "byte"},
+            "rowwise_int8_kernel": {"amount": quant * layers, "unit": "byte"}}
+
+
 def probe_kernels(torch, ltm, reps: int = 10, timed: bool = True):
     """Times each kernel of one block standalone at the workload's shapes with
     CUDA events on the launching stream (L2 flushed and cleaned before every
@@ -374,55 +390,52 @@ def run_ours(args):
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = tokens / (float(e2e_ms.item()) * 1e-3)
 
-    probe = None
+    # per-kernel device time of one more (untimed) forward, measured inside the
+    # library with CUDA events on the launching stream
+    flush.fill_(0)
+    torch.cuda.synchronize()
+    with ltm.KernelTimer() as kt:
+        model.forward(tok, out)
+    kernels = {name: {"launches": n, "ms": round(ms, 4), "ms_per_launch": round(ms / n, 5)}
+               for name, (n, ms) in kt.result.items()}
     roofline = None
     pk, pk_src = peaks()
     if rank == 0 and not args.no_probe:
-        probe = probe_kernels(torch, ltm)
         i8 = int8_peak(torch)
-        L = args.layers
+        if i8:
+            kernels["int8_peak_tops_measured"] = round(i8, 1)
+        work = step_work(args.layers)
         by_kind = {}
-        for r in probe:
-            k = by_kind.setdefault(r["kind"], dict(ms=0.0, flops=0.0, bytes=0.0, launches=0))
-            k["ms"] += r["ms"] * r["launches_per_layer"] * L
-            k["flops"] += r["flops"] * r["launches_per_layer"] * L
-            k["bytes"] += r["bytes"] * r["launches_per_layer"] * L
-            k["launches"] += r["launches_per_layer"] * L
-        dom = max(by_kind, key=lambda k: by_kind[k]["ms"])
+        for name, (n, ms) in kt.result.items():
+            kind = name.split("/")[0]
+            k = by_kind.setdefault(kind, dict(ms=0.0, launches=0))
+            k["ms"] += ms
+            k["launches"] += n
+        dom = max((k for k in by_kind if k in work), key=lambda k: by_kind[k]["ms"])
         d = by_kind[dom]
-        kname = {"w8a8": "w8a8_tc_kernel", "attn": "flash_fwd_tc_kernel",
-                 "ln": "ln_x2_kernel", "quant": "rowwise_int8_kernel"}[dom]
         avg_ms = d["ms"] / d["launches"]
-        if dom in ("w8a8", "attn"):
-            achieved = d["flops"] / d["launches"] / (avg_ms * 1e-3) / 1e12
-            if dom == "w8a8":
+        per_launch = work[dom]["amount"] / d["launches"]
+        if work[dom]["unit"] == "flop":
+            achieved = per_launch / (avg_ms * 1e-3) / 1e12
+            if dom.startswith("w8a8"):
                 peak = i8 if i8 else 2.0 * pk["bf16_tflops"]
-                peak_src = ("int8 torch._int_mm 8192^3 measured in this run" if i8 else
+                peak_src = ("int8 cuBLASLt (torch._int_mm 8192^3) measured in this run" if i8 else
                             "2 x bf16_tflops " + pk_src + " (derived int8)")
             else:
                 peak = pk["bf16_tflops"]
                 peak_src = "bf16_tflops " + pk_src
             unit, bound = "TFLOP/s", "tensor"
         else:
-            achieved = d["bytes"] / d["launches"] / (avg_ms * 1e-3) / 1e9
+            achieved = per_launch / (avg_ms * 1e-3) / 1e9
             peak = pk["hbm_gbs"]
             peak_src = "hbm_gbs " + pk_src
             unit, bound = "GB/s", "hbm"
-        traffic = traffic_from_profiles(kname)
-        roofline = {"bound": bound, "kernel": kname, "achieved": round(achieved, 2),
+        roofline = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2),
                     "peak": round(peak, 2), "unit": unit, "frac": round(achieved / peak, 4),
-                    "traffic": traffic, "peak_source": peak_src, "launches_per_step": d["launches"],
-                    "avg_launch_ms": round(avg_ms, 5),
-                    "algorithmic_per_launch": (d["flops"] if bound == "tensor" else d["bytes"])
-                    / d["launches"]}
-        probe = {r["name"]: {"ms_per_launch": round(r["ms"], 5),
-                             "ms_per_step": round(r["ms"] * r["launches_per_layer"] * L, 4),
-                             "rate": (round(r["flops"] / (r["ms"] * 1e-3) / 1e12, 1)
-                                      if r["flops"] else
-                                      round(r["bytes"] / (r["ms"] * 1e-3) / 1e9, 1)),
-                             "rate_unit": "TFLOP/s" if r["flops"] else "GB/s"} for r in probe}
-        if i8:
-            probe["int8_peak_tops_measured"] = round(i8, 1)
+                    "traffic": traffic_from_profiles(dom), "peak_source": peak_src,
+                    "launches_per_step": d["launches"], "avg_launch_ms": round(avg_ms, 5),
+                    "algorithmic_per_launch": per_launch,
+                    "algorithmic_unit": work[dom]["unit"]}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -445,7 +458,7 @@ def run_ours(args):
             "clocks": clocks,
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "kernels": probe,
+            "kernels": kernels,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:

@@ -73,6 +73,14 @@ LTM_API ltm_status ltm_device_error(int* code_out);
 /* Number of kernels this library has launched in this process (all devices). */
 LTM_API ltm_status ltm_launch_count(uint64_t* count_out);
 
+/* In-library kernel timer.  Between begin and end, every kernel the library
+ * launches on `stream` is followed by a CUDA event; end synchronizes the
+ * stream and writes one line per kernel name, "name launches total_ms\n", in
+ * first-launch order (a kernel's time is measured from the previous mark, so
+ * launches on the stream should run back to back). */
+LTM_API ltm_status ltm_kernel_timer_begin(void* stream);
+LTM_API ltm_status ltm_kernel_timer_end(char* report, size_t capacity);
+
 /* ---------------------------------------------------------- quantization -- */
 /* Replaces Quantizer<T>::quantize with per_channel=true, symmetric=true,
  * channel_axis=0 (include/core/quantization/quantizer.cuh:183,

@@ -107,7 +107,7 @@ template <int D, bool CAUSAL>
 void launch_f32(const AttnParams& p, int B, cudaStream_t stream) {
   dim3 grid((p.Sq + 3) / 4, p.nh, B);
   flash_fwd_f32_kernel<D, CAUSAL><<<grid, 128, 0, stream>>>(p);
-  check_launch("flash_fwd_f32_kernel");
+  check_launch("flash_fwd_f32_kernel", stream);
 }
 
 }  // namespace

@@ -349,7 +349,7 @@ void launch_inst(const AttnParams& p, int B, cudaStream_t stream) {
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   dim3 grid((p.Sq + kQM - 1) / kQM, p.nh, B);
   kern<<<grid, 256, L::kBytes, stream>>>(tq, tk, tv, p, device_error_ptr());
-  check_launch("attn_tc_kernel");
+  check_launch(CAUSAL ? "attn_tc_kernel/causal" : "attn_tc_kernel/full", stream);
 }
 
 }  // namespace

@@ -72,7 +72,7 @@ void upload_f32_as(const float* host, int64_t n, ltm_dtype dt, void* dev, cudaSt
     f32_to_kernel<T><<<grid_for(n), 256, 0, stream>>>(static_cast<const float*>(tmp.ptr),
                                                       static_cast<T*>(dev), n);
   });
-  check_launch("f32_to_kernel");
+  check_launch("f32_to_kernel", stream);
   LTM_CUDA_TRY(cudaStreamSynchronize(stream));
 }
 
@@ -83,7 +83,7 @@ void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n
     add3_kernel<T><<<grid_for(n), 256, 0, stream>>>(static_cast<const T*>(a), static_cast<const T*>(b),
                                                     static_cast<const T*>(c), static_cast<T*>(y), n);
   });
-  check_launch("add3_kernel");
+  check_launch("add3_kernel", stream);
 }
 
 // ------------------------------------------------------------ quantized W --

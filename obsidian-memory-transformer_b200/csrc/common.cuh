@@ -75,10 +75,12 @@ ltm_status guarded(F&& f) {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-void note_launch();
+// Counts a launch and, while the kernel timer is on for `stream`, records an
+// event after it (the kernel's end; its start is the previous mark).
+void note_launch(const char* what, cudaStream_t stream);
 
-inline void check_launch(const char* what) {
-  note_launch();
+inline void check_launch(const char* what, cudaStream_t stream = nullptr) {
+  note_launch(what, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string(what) + ": " + cudaGetErrorString(e));

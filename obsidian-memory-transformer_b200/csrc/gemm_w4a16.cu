@@ -216,7 +216,7 @@ void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s
     constexpr int MODE = decltype(mode_c)::value;
     if constexpr (MODE != kEpiAccI32 && !std::is_same<OutT, float>::value) go(OutT{}, mode_c);
   });
-  check_launch("w4a16_tc_kernel");
+  check_launch("w4a16_tc_kernel", stream);
 }
 
 }  // namespace ltm_b200

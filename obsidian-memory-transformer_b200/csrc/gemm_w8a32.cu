@@ -139,7 +139,7 @@ void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_
                                         static_cast<int>(K), ep);
     }
   });
-  check_launch("w8a32_kernel");
+  check_launch("w8a32_kernel", stream);
 }
 
 }  // namespace ltm_b200

@@ -193,7 +193,10 @@ void launch_w8a8_inst(const int8_t* qa, const int8_t* qw, int M, int N, int K, c
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
   kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, M, N, K, ep, device_error_ptr());
-  check_launch("w8a8_tc_kernel");
+  static const char* const kNames[] = {"w8a8_tc_kernel/plain", "w8a8_tc_kernel/rope",
+                                      "w8a8_tc_kernel/resid", "w8a8_tc_kernel/gatemix",
+                                      "w8a8_tc_kernel/acc_i32"};
+  check_launch(kNames[MODE], stream);
 }
 
 }  // namespace

@@ -120,21 +120,21 @@ void launch_memory_store(void* memory, const void* keys, int64_t ldk, const void
       const int splits = static_cast<int>(std::min<int64_t>(64, (T + 63) / 64));
       dim3 g1((H + 31) / 32, splits);
       colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(queries), ldq, T, H, qsum);
-      check_launch("colsum_kernel");
+      check_launch("colsum_kernel", st);
       const size_t smem = static_cast<size_t>(Ms) * sizeof(float);
       auto kern = slot_weight_kernel<TT>;
       LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)));
       kern<<<nh, 256, smem, st>>>(qsum, 1.0f / static_cast<float>(T), static_cast<const TT*>(keys),
                                   ldk, Ms, dh, nh, rate, wslot);
-      check_launch("slot_weight_kernel");
+      check_launch("slot_weight_kernel", st);
       w = wslot;
     }
     const int64_t n = static_cast<int64_t>(Ms) * H;
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
     bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale, w,
                                                  rate, Ms, H);
-    check_launch("bank_update_kernel");
+    check_launch("bank_update_kernel", st);
   });
 }
 

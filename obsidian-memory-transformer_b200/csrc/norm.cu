@@ -376,7 +376,7 @@ void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float*
             xt, rt, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
     }
   });
-  check_launch("ln_x2_kernel");
+  check_launch("ln_x2_kernel", stream);
 }
 
 void launch_embed_gather(const void* table, ltm_dtype dt, int vocab, int H, const int32_t* tok,
@@ -388,7 +388,7 @@ void launch_embed_gather(const void* table, ltm_dtype dt, int vocab, int H, cons
     embed_gather_kernel<TT><<<static_cast<unsigned>((T + 7) / 8), 256, 0, stream>>>(
         static_cast<const TT*>(table), vocab, H, tok, T, static_cast<TT*>(out), device_error_ptr());
   });
-  check_launch("embed_gather_kernel");
+  check_launch("embed_gather_kernel", stream);
 }
 
 }  // namespace ltm_b200

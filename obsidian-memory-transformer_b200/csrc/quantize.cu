@@ -283,7 +283,7 @@ void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, i
     else
       rowwise_int8_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
   });
-  check_launch("rowwise_int8_kernel");
+  check_launch("rowwise_int8_kernel", stream);
 }
 
 }  // namespace ltm_b200
@@ -320,7 +320,7 @@ extern "C" ltm_status ltm_dequantize_int8_per_channel(const int8_t* q, const flo
       dequant_int8_kernel<T><<<elementwise_grid(N * K), 256, 0, as_stream(stream)>>>(
           q, s, N, K, static_cast<T*>(out));
     });
-    check_launch("dequant_int8_kernel");
+    check_launch("dequant_int8_kernel", as_stream(stream));
   });
 }
 
@@ -342,7 +342,7 @@ extern "C" ltm_status ltm_quantize_int4_grouped(const void* w, ltm_dtype w_dtype
       int4_group_quant_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
           static_cast<const T*>(w), N, K, packed, s, zp);
     });
-    check_launch("int4_group_quant_kernel");
+    check_launch("int4_group_quant_kernel", as_stream(stream));
   });
 }
 
@@ -361,6 +361,6 @@ extern "C" ltm_status ltm_dequantize_int4_grouped(const uint8_t* packed, const f
       int4_dequant_kernel<T><<<elementwise_grid(N * K / 2), 256, 0, as_stream(stream)>>>(
           packed, s, zp, N, K, group_size, static_cast<T*>(out));
     });
-    check_launch("int4_dequant_kernel");
+    check_launch("int4_dequant_kernel", as_stream(stream));
   });
 }

@@ -1,8 +1,12 @@
 // runtime.cu -- error strings, device error word, device properties and the
 // TMA descriptor encoder (driver entry point resolved through the runtime, so
 // the library needs no link-time dependency on libcuda).
+#include <algorithm>
 #include <atomic>
+#include <cstdio>
+#include <map>
 #include <mutex>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -32,7 +36,41 @@ thread_local std::string t_last_error;
 std::atomic<uint64_t> g_launches{0};
 }  // namespace
 
-void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+// Kernel timer: while on, every launch on the timed stream is followed by an
+// event; a kernel's duration is the time between its event and the previous
+// one (launches on one stream run back to back).
+struct KernelTimer {
+  std::mutex mu;
+  std::atomic<bool> on{false};
+  cudaStream_t stream = nullptr;
+  int device = -1;
+  cudaEvent_t start = nullptr;
+  std::vector<std::pair<std::string, cudaEvent_t>> marks;
+  std::vector<cudaEvent_t> pool;
+  cudaEvent_t get() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+KernelTimer& timer() {
+  static KernelTimer t;
+  return t;
+}
+
+void note_launch(const char* what, cudaStream_t stream) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  KernelTimer& t = timer();
+  if (!t.on.load(std::memory_order_relaxed) || stream != t.stream) return;
+  std::lock_guard<std::mutex> lk(t.mu);
+  cudaEvent_t e = t.get();
+  if (e && cudaEventRecord(e, stream) == cudaSuccess) t.marks.emplace_back(what, e);
+}
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 void clear_error() { t_last_error.clear(); }
@@ -120,5 +158,49 @@ extern "C" ltm_status ltm_launch_count(uint64_t* count_out) {
   return guarded([&] {
     LTM_REQUIRE(count_out != nullptr, "count_out is NULL");
     *count_out = g_launches.load(std::memory_order_relaxed);
+  });
+}
+
+extern "C" ltm_status ltm_kernel_timer_begin(void* stream) {
+  return guarded([&] {
+    KernelTimer& t = timer();
+    std::lock_guard<std::mutex> lk(t.mu);
+    LTM_REQUIRE(!t.on.load(), "kernel timer already running");
+    for (auto& m : t.marks) t.pool.push_back(m.second);
+    t.marks.clear();
+    if (!t.start) LTM_CUDA_TRY(cudaEventCreate(&t.start));
+    t.stream = as_stream(stream);
+    LTM_CUDA_TRY(cudaEventRecord(t.start, t.stream));
+    t.on.store(true);
+  });
+}
+
+extern "C" ltm_status ltm_kernel_timer_end(char* report, size_t capacity) {
+  return guarded([&] {
+    KernelTimer& t = timer();
+    std::lock_guard<std::mutex> lk(t.mu);
+    LTM_REQUIRE(t.on.load(), "kernel timer not running");
+    t.on.store(false);
+    LTM_CUDA_TRY(cudaStreamSynchronize(t.stream));
+    std::map<std::string, std::pair<int, double>> agg;
+    std::vector<std::string> order;
+    cudaEvent_t prev = t.start;
+    for (auto& m : t.marks) {
+      float ms = 0.0f;
+      LTM_CUDA_TRY(cudaEventElapsedTime(&ms, prev, m.second));
+      if (!agg.count(m.first)) order.push_back(m.first);
+      agg[m.first].first += 1;
+      agg[m.first].second += ms;
+      prev = m.second;
+    }
+    std::string out;
+    for (const auto& name : order) {
+      char line[256];
+      std::snprintf(line, sizeof(line), "%s %d %.6f\n", name.c_str(), agg[name].first,
+                    agg[name].second);
+      out += line;
+    }
+    LTM_REQUIRE(report && capacity > out.size(), "report buffer too small");
+    std::memcpy(report, out.c_str(), out.size() + 1);
   });
 }

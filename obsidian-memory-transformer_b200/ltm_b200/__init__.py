@@ -73,6 +73,8 @@ def _declare(L):
         "ltm_last_error_string": ([], C.c_char_p),
         "ltm_device_error": ([C.POINTER(C.c_int)], ci),
         "ltm_launch_count": ([C.POINTER(C.c_uint64)], ci),
+        "ltm_kernel_timer_begin": ([vp], ci),
+        "ltm_kernel_timer_end": ([C.c_char_p, C.c_size_t], ci),
         "ltm_quantize_int8_per_channel": ([vp, ci, i64, i64, vp, vp, vp], ci),
         "ltm_dequantize_int8_per_channel": ([vp, vp, i64, i64, vp, ci, vp], ci),
         "ltm_quantize_act_int8_per_token": ([vp, ci, i64, i64, vp, vp, vp], ci),
@@ -141,6 +143,27 @@ def launch_count() -> int:
     n = C.c_uint64(0)
     _check(lib().ltm_launch_count(C.byref(n)))
     return n.value
+
+
+class KernelTimer:
+    """Per-kernel device times of everything the library launches on a stream
+    inside the `with` block: {name: (launches, total_ms)}."""
+
+    def __init__(self, stream=None):
+        self.stream = stream
+        self.result = {}
+
+    def __enter__(self):
+        _check(lib().ltm_kernel_timer_begin(_stream(self.stream)))
+        return self
+
+    def __exit__(self, *exc):
+        buf = C.create_string_buffer(1 << 16)
+        _check(lib().ltm_kernel_timer_end(buf, len(buf)))
+        for line in buf.value.decode().splitlines():
+            name, n, ms = line.split()
+            self.result[name] = (int(n), float(ms))
+        return False
 
 
 # ---------------------------------------------------------------- torch glue --
