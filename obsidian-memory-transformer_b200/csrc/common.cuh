@@ -3,6 +3,8 @@
 // (mbarrier, TMA, tcgen05) used by the tensor-core kernels.
 #pragma once
 
+#include <type_traits>
+
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -272,6 +274,33 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, ui
       : "memory");
 }
 
+// Tiled TMA store of one box from shared memory (bulk-group completion).
+// The box's smem writes must be made visible to the async proxy first
+// (fence_proxy_async_smem by the writing threads, then a warp/CTA sync).
+__device__ __forceinline__ void tma_store_2d(const void* desc, const void* smem_src, int32_t x,
+                                             int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(desc)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N committed bulk groups of this thread still read smem.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until every committed bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // --------------------------------------------------------- PTX: tcgen05 --
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -340,6 +369,21 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.wait::ld that also names the destination registers of the load it
+// completes, so no use of them can be scheduled above the wait (used when the
+// next load is issued before the current registers are consumed).
+__device__ __forceinline__ void tmem_wait_ld_tie(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 // Shared-memory matrix descriptor of a K-major operand tile stored with the
 // 128-byte swizzle (rows of 128 bytes, 8-row groups 1024 bytes apart), the
 // layout a SWIZZLE_128B TMA box of 128-byte rows produces.  Fields: start
@@ -391,6 +435,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b
 }
 
 // -------------------------------------------------------- TMA descriptors --
+template <class T>
+constexpr CUtensorMapDataType tma_dtype_of() {
+  if constexpr (std::is_same<T, __half>::value) return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  else if constexpr (std::is_same<T, __nv_bfloat16>::value) return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  else if constexpr (std::is_same<T, float>::value) return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  else if constexpr (std::is_same<T, int32_t>::value) return CU_TENSOR_MAP_DATA_TYPE_INT32;
+  else return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+}
+
 // 2-D tiled tensor map over a row-major [rows, cols] matrix of `elem_bytes`
 // elements (128-byte swizzle unless given); box = box_cols x box_rows.
 void make_tma_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,

@@ -301,3 +301,261 @@ void dispatch_epilogue(int mode, ltm_dtype out_dt, F&& f) {
 }
 
 }  // namespace ltm_b200
+
+namespace ltm_b200 {
+
+// ---------------------------------------------------------------------------
+// Pipelined tensor-core epilogue with TMA stores.
+//
+// One epilogue warp owns 32 tile rows (its TMEM lane quarter) x CW columns of
+// an accumulator tile and walks them in 32-column chunks:
+//   * the per-column dequant scale and bias of the warp's CW columns and the
+//     per-row activation scale are fetched one tile ahead into registers and
+//     published to a per-warp shared-memory vector at the tile start (read
+//     back as broadcast 16-byte loads);
+//   * the TMEM load of chunk c+1 and the global operands of chunk c+1 (RoPE
+//     table row, residual / gate-mix tensors) are in flight while chunk c is
+//     computed;
+//   * results are packed into a 32-row x 128-byte box in shared memory with
+//     the 128-byte swizzle (conflict-free row writes) and written by one TMA
+//     store per box; two boxes per warp alternate, so packing the next box
+//     overlaps the previous store.
+// The TMEM accumulator is released (on_tmem_free) as soon as the last chunk
+// has been read, before its math.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kEpiBoxBytes = 32 * 128;
+
+template <int MODE, class OutT>
+struct EpiChunkAux {
+  static constexpr int kVec = 32 * static_cast<int>(sizeof(OutT)) / 16;  // uint4 per 32 values
+  static constexpr int kTensors = MODE == kEpiResid ? 1 : (MODE == kEpiGateMix ? 3 : 0);
+  // Residual loads go one chunk ahead in a second register set; the RoPE row
+  // and the three gate-mix tensors use one set, refilled for the next chunk as
+  // soon as the current chunk's math has consumed it.
+  static constexpr bool kAhead = MODE == kEpiResid;
+  // fp32 gate-mix reads its three tensors straight from global memory at use
+  // (96 staged registers would spill).
+  static constexpr bool kDirect = MODE == kEpiGateMix && sizeof(OutT) == 4;
+  uint4 t[(kTensors > 0 && !kDirect) ? kTensors : 1][kVec];
+  float4 rope[MODE == kEpiRope ? 8 : 1];
+  const OutT* src_row[kDirect ? 3 : 1];
+  bool direct_ok;
+
+  // Issues the loads chunk (m, n) needs.  Rows >= M and chunks >= N load
+  // nothing (their results are never stored).
+  __device__ __forceinline__ void load(const Epilogue& ep, int64_t m, int64_t n, int pos, bool row_ok,
+                                       bool col_ok) {
+    if constexpr (MODE == kEpiRope) {
+      if (row_ok && n < ep.rope_cols) {
+        const int d0 = static_cast<int>(static_cast<uint32_t>(n) % static_cast<uint32_t>(ep.head_dim));
+        const float4* tab = reinterpret_cast<const float4*>(
+            ep.rope + static_cast<int64_t>(pos) * (ep.head_dim >> 1) + (d0 >> 1));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) rope[j] = __ldg(tab + j);
+      }
+    } else if constexpr (kDirect) {
+      direct_ok = row_ok && col_ok;
+      const void* src[3] = {ep.aux0, ep.aux1, ep.aux2};
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+        src_row[a] = direct_ok ? static_cast<const OutT*>(src[a]) + m * ep.ld_aux + n : nullptr;
+    } else if constexpr (kTensors > 0) {
+      if (row_ok && col_ok) {
+        const void* src[3] = {ep.aux0, ep.aux1, ep.aux2};
+#pragma unroll
+        for (int a = 0; a < kTensors; ++a) {
+          const uint4* p = reinterpret_cast<const uint4*>(static_cast<const OutT*>(src[a]) +
+                                                          m * ep.ld_aux + n);
+#pragma unroll
+          for (int j = 0; j < kVec; ++j) t[a][j] = __ldg(p + j);
+        }
+      }
+    }
+  }
+
+  // Element i (0..31) of tensor a of the chunk, as fp32.
+  __device__ __forceinline__ float at(int a, int i) const {
+    if constexpr (kDirect) {
+      return direct_ok ? to_f32(__ldg(src_row[a] + i)) : 0.0f;
+    } else {
+      constexpr int PER = 16 / sizeof(OutT);
+      return to_f32(reinterpret_cast<const OutT*>(&t[a][i / PER])[i % PER]);
+    }
+  }
+};
+
+template <int MODE, class OutT, int CW, bool ACC_INT>
+struct TmaTileEpilogue {
+  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
+  static constexpr int NCH = CW / 32;
+  static constexpr int BOXC = 128 / static_cast<int>(sizeof(StoreT));  // columns per box
+  static constexpr int CPB = BOXC / 32;                                  // chunks per box
+  static constexpr int UPC = 32 * static_cast<int>(sizeof(StoreT)) / 16;  // 16-byte units per chunk row
+  static constexpr bool kMath = MODE != kEpiAccI32;
+  static_assert(CW % BOXC == 0, "warp columns must be whole boxes");
+  // shared-memory bytes of the per-warp column vectors (scale + bias)
+  static constexpr uint32_t kColBytes = 2 * CW * 4;
+
+  float rs_next = 1.0f;
+  float cs_next[NCH], bs_next[NCH];
+  int sb = 0;  // staging box to fill next
+
+  // Fetches the row scale of row m and the scale/bias of columns nw + 32c + lane.
+  __device__ __forceinline__ void prefetch(const Epilogue& ep, int64_t m, int64_t nw, int M, int N,
+                                           int lane) {
+    if constexpr (kMath) {
+      rs_next = (ep.row_scale && m < M) ? __ldg(ep.row_scale + m) : 1.0f;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int64_t n = nw + c * 32 + lane;
+        cs_next[c] = (ep.col_scale && n < N) ? __ldg(ep.col_scale + n) : 1.0f;
+        bs_next[c] = (ep.bias && n < N) ? __ldg(ep.bias + n) : 0.0f;
+      }
+    }
+  }
+
+  // Epilogue of one tile.  tacc: TMEM address of (lane quarter, first column);
+  // m: this lane's row; row0: first row of the warp's 32 rows; nw: first
+  // column; cvec: per-warp column vectors (kColBytes); stg: two staging boxes
+  // (1024-byte aligned).  Returns after the last box store has been issued.
+  template <class OnTmemFree>
+  __device__ __forceinline__ void run(const Epilogue& ep, const CUtensorMap* tmo, uint32_t tacc,
+                                      int64_t m, int row0, int nw, int M, int N, float* cvec,
+                                      uint8_t* stg, int lane, OnTmemFree&& on_tmem_free) {
+    const float rs = rs_next;
+    if constexpr (kMath) {
+      __syncwarp();  // previous tile's reads of cvec are done
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        cvec[c * 32 + lane] = cs_next[c];
+        cvec[CW + c * 32 + lane] = bs_next[c];
+      }
+      __syncwarp();
+    }
+    const bool row_ok = m < M;
+    int pos = 0;
+    if constexpr (MODE == kEpiRope)
+      pos = static_cast<int>(static_cast<uint32_t>(m) % static_cast<uint32_t>(ep.seq_len));
+
+    using Aux = EpiChunkAux<MODE, OutT>;
+    constexpr int kAuxSets = Aux::kAhead ? 2 : 1;
+    uint32_t acc[2][32];
+    Aux aux[kAuxSets];
+    tmem_ld_32x32b_x32(tacc, acc[0]);
+    aux[0].load(ep, m, nw, pos, row_ok, nw < N);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int cur = c & 1;
+      const int ax = Aux::kAhead ? cur : 0;
+      const int64_t n = nw + c * 32;
+      tmem_wait_ld_tie(acc[cur]);
+      if (c + 1 < NCH) {
+        tmem_ld_32x32b_x32(tacc + (c + 1) * 32, acc[cur ^ 1]);
+        if constexpr (Aux::kAhead) aux[cur ^ 1].load(ep, m, n + 32, pos, row_ok, n + 32 < N);
+      } else {
+        tc_fence_before();
+        __syncwarp();
+        on_tmem_free();
+      }
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if constexpr (!kMath) v[i] = __int_as_float(static_cast<int>(acc[cur][i]));
+        else if constexpr (ACC_INT) v[i] = static_cast<float>(static_cast<int>(acc[cur][i]));
+        else v[i] = __uint_as_float(acc[cur][i]);
+      }
+      if constexpr (kMath) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= rs;
+        const float4* cs4 = reinterpret_cast<const float4*>(cvec + c * 32);
+        const float4* bs4 = reinterpret_cast<const float4*>(cvec + CW + c * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 s = cs4[j];
+          v[4 * j] *= s.x; v[4 * j + 1] *= s.y; v[4 * j + 2] *= s.z; v[4 * j + 3] *= s.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 s = bs4[j];
+          v[4 * j] += s.x; v[4 * j + 1] += s.y; v[4 * j + 2] += s.z; v[4 * j + 3] += s.w;
+        }
+        if (ep.act == LTM_EPI_GELU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+        } else if (ep.act == LTM_EPI_SIGMOID) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = sigmoid_f(v[i]);
+        }
+        if constexpr (MODE == kEpiRope) {
+          if (n < ep.rope_cols) {
+            const float* rp = reinterpret_cast<const float*>(aux[ax].rope);
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float cs = rp[i], sn = rp[i + 1];
+              const float a = v[i], b = v[i + 1];
+              v[i] = a * cs - b * sn;
+              v[i + 1] = a * sn + b * cs;
+            }
+          }
+        } else if constexpr (MODE == kEpiResid) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += aux[ax].at(0, i);
+        } else if constexpr (MODE == kEpiGateMix) {
+          // y = (s + g*mem) + (1-g)*x with g = v; g*x feeds the memory write
+          float gx[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float g = v[i], xv = aux[ax].at(2, i);
+            const float sm = aux[ax].at(0, i) + g * aux[ax].at(1, i);
+            gx[i] = row_ok ? g * xv : 0.0f;
+            v[i] = sm + (1.0f - g) * xv;
+          }
+          if (ep.colsum) {
+            const float csum = warp_colsum32(gx);
+            if (n < N) atomicAdd(ep.colsum + n + lane, csum);
+          }
+        }
+      }
+      if constexpr (!Aux::kAhead) {
+        if (c + 1 < NCH) aux[0].load(ep, m, n + 32, pos, row_ok, n + 32 < N);
+      }
+      // pack into the staging box (128-byte swizzle: 16-byte unit u of row r
+      // at unit u ^ (r & 7))
+      const int cb = c % CPB;
+      if (cb == 0) {
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+      }
+      uint8_t* box = stg + sb * kEpiBoxBytes + lane * 128;
+      constexpr int EPU = 16 / static_cast<int>(sizeof(StoreT));
+#pragma unroll
+      for (int u = 0; u < UPC; ++u) {
+        uint4 raw;
+        if constexpr (!kMath) {
+          raw.x = __float_as_uint(v[u * 4 + 0]);
+          raw.y = __float_as_uint(v[u * 4 + 1]);
+          raw.z = __float_as_uint(v[u * 4 + 2]);
+          raw.w = __float_as_uint(v[u * 4 + 3]);
+        } else {
+          StoreT* e = reinterpret_cast<StoreT*>(&raw);
+#pragma unroll
+          for (int i = 0; i < EPU; ++i) e[i] = from_f32<StoreT>(v[u * EPU + i]);
+        }
+        const int unit = (cb * UPC + u) ^ (lane & 7);
+        *reinterpret_cast<uint4*>(box + unit * 16) = raw;
+      }
+      if (cb == CPB - 1) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int x = nw + (c - cb) * 32;
+        if (lane == 0 && row0 < M && x < N) {  // boxes wholly outside the output are skipped
+          tma_store_2d(tmo, stg + sb * kEpiBoxBytes, x, row0);
+          bulk_commit_group();
+        }
+        sb ^= 1;
+      }
+    }
+  }
+};
+
+}  // namespace ltm_b200

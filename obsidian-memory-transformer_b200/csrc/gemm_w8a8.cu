@@ -34,23 +34,25 @@ constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle row
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 
-template <int BN, int STAGES, class StoreT>
+template <int BN, int STAGES>
 struct W8A8Smem {
   static constexpr uint32_t kA = kBM * kBK;
   static constexpr uint32_t kB = BN * kBK;
-  static constexpr uint32_t kStage = kA + kB;
+  static constexpr uint32_t kStage = kA + kB;  // multiple of 1024
   static constexpr uint32_t kStgOff = STAGES * kStage;
-  static constexpr uint32_t kStgWarp = 32 * epi_stage_row_bytes<StoreT>();
-  static constexpr uint32_t kBarOff = kStgOff + kEpiWarps * kStgWarp;
+  static constexpr uint32_t kStgWarp = 2 * kEpiBoxBytes;  // two TMA-store boxes per warp
+  static constexpr uint32_t kColOff = kStgOff + kEpiWarps * kStgWarp;
+  static constexpr uint32_t kColWarp = 2 * (BN / 2) * 4;  // scale + bias of the warp's columns
+  static constexpr uint32_t kBarOff = kColOff + kEpiWarps * kColWarp;
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
 };
 
 template <int BN, int STAGES, int MODE, class OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, Epilogue ep, int* err) {
-  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
-  using L = W8A8Smem<BN, STAGES, StoreT>;
+                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, Epilogue ep,
+                   int* err) {
+  using L = W8A8Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -82,6 +84,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) tmem_alloc(tslot, 2 * BN);
   tc_fence_before();
@@ -151,24 +154,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..9: TMEM lane quarter q = warp % 4, column half
-    // (warp - 2) / 4 of the tile.
+    // Epilogue warps 2..9: TMEM lane quarter q = warp % 4 (tile rows
+    // 32q..32q+31), column half (warp - 2) / 4 of the tile.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
+    float* cvec = reinterpret_cast<float*>(smem + L::kColOff + (warp - 2) * L::kColWarp);
+    TmaTileEpilogue<MODE, OutT, BN / 2, true> epi;
+    auto rows_of = [&](int t) { return (t / num_n) * kBM + q * 32; };
+    auto cols_of = [&](int t) { return (t % num_n) * BN + half * (BN / 2); };
+    if (static_cast<int>(blockIdx.x) < tiles)
+      epi.prefetch(ep, rows_of(blockIdx.x) + lane, cols_of(blockIdx.x), M, N, lane);
     int lt = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
       const int b = lt & 1;
       const uint32_t use = static_cast<uint32_t>(lt >> 1);
+      const int row0 = rows_of(t), nw = cols_of(t);
       if (!mbar_wait_bounded(accf + b, use & 1, abort_flag, err, kErrWaitAccum)) break;
       tc_fence_after();
-      const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN + half * (BN / 2);
-      tc_tile_epilogue_passes<MODE, OutT, BN / 2, true>(ep, tmem + b * BN + half * (BN / 2), q, lane,
-                                                        m0, n0, M, N, stg);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce + b);
+      // publish this tile's column vectors, then fetch the next tile's
+      epi.run(ep, &tmO, tmem + b * BN + half * (BN / 2) + (static_cast<uint32_t>(q * 32) << 16),
+              row0 + lane, row0, nw, M, N, cvec, stg, lane,
+              [&] {
+                if (lane == 0) mbar_arrive(acce + b);
+                const int tn = t + static_cast<int>(gridDim.x);
+                if (tn < tiles) epi.prefetch(ep, rows_of(tn) + lane, cols_of(tn), M, N, lane);
+              });
     }
+    if (lane == 0) bulk_wait_group_all();
   }
 
   tc_fence_before();
@@ -183,16 +196,18 @@ template <int BN, int STAGES, int MODE, class OutT>
 void launch_w8a8_inst(const int8_t* qa, const int8_t* qw, int M, int N, int K, const Epilogue& ep,
                       cudaStream_t stream) {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
-  using L = W8A8Smem<BN, STAGES, StoreT>;
+  using L = W8A8Smem<BN, STAGES>;
   static_assert(L::kBytes <= 232448, "shared memory budget exceeded");
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
   make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, BN);
+  constexpr int ob = static_cast<int>(sizeof(StoreT));
+  make_tma_2d(&to, ep.out, tma_dtype_of<StoreT>(), ob, M, N, ep.ldo, 128 / ob, 32);
   auto kern = w8a8_tc_kernel<BN, STAGES, MODE, OutT>;
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
-  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, M, N, K, ep, device_error_ptr());
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, ep, device_error_ptr());
   static const char* const kNames[] = {"w8a8_tc_kernel/plain", "w8a8_tc_kernel/rope",
                                       "w8a8_tc_kernel/resid", "w8a8_tc_kernel/gatemix",
                                       "w8a8_tc_kernel/acc_i32"};
