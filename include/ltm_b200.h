@@ -294,6 +294,35 @@ LTM_API ltm_status ltm_block_forward(ltm_block* blk, const void* x, void* y, con
 LTM_API ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stream);
 LTM_API ltm_status ltm_block_destroy(ltm_block* blk);
 
+/* ------------------------------------------------------ tensor parallel -- */
+/* No counterpart in the reference (single GPU only).  A communicator of
+ * nranks GPUs (NCCL, loaded at run time from libnccl.so.2) for the
+ * tensor-parallel block: rank 0 creates a 128-byte unique id, the caller
+ * distributes it to every rank over its own channel, each rank creates its
+ * communicator on its device. */
+typedef struct ltm_comm ltm_comm;
+#define LTM_COMM_ID_BYTES 128
+LTM_API ltm_status ltm_comm_unique_id(void* id_out /* LTM_COMM_ID_BYTES */);
+LTM_API ltm_status ltm_comm_create(const void* id, int nranks, int rank, int device, ltm_comm** out);
+/* In-place allowed (send == recv); op_max != 0: maximum, else sum. */
+LTM_API ltm_status ltm_comm_allreduce(ltm_comm* comm, const void* send, void* recv, size_t count,
+                              ltm_dtype dtype, int op_max, void* stream);
+LTM_API ltm_status ltm_comm_destroy(ltm_comm* comm);
+
+/* Tensor-parallel block on the communicator's device (rank r of n): Q/K/V/
+ * Q_m, K_M/V_M and W1 are split by heads / FFN columns, W_o, W_om and W2 by
+ * their input columns (partial sums joined by one allreduce each), the gate
+ * and LayerNorms are replicated, the bank is replicated and updated
+ * identically on every rank.  ltm_block_load_weights takes the FULL host
+ * weights on every rank and keeps this rank's shard; per-channel weight
+ * scales and per-token activation scales are those of the unsplit matrices
+ * (global row maxima), so the int8 codes equal the single-GPU block's.
+ * ltm_block_forward's x and y are the full [B,S,H] on every rank.  Needs
+ * num_heads and ffn_dim divisible by n.  The communicator must outlive the
+ * block. */
+LTM_API ltm_status ltm_block_create_tp(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
+                               ltm_comm* comm, ltm_block** out);
+
 /* ----------------------------------------------------------------- model -- */
 /* Multi-layer model (token embedding gather + n_layers Titan blocks), the
  * forward of TitanModel (python_bindings/ltm/model.py:159-215) without the

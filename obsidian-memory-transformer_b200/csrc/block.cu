@@ -117,6 +117,48 @@ void QLinear::load(const ltm_quant_config& q, const float* w_host, const float* 
   LTM_CUDA_TRY(cudaStreamSynchronize(stream));
 }
 
+// Loads the columns [c0, c0 + nc) of a host [n, k] weight: the full matrix is
+// quantized (per-output-channel scales, or group-128 int4 along K) and the
+// codes / group parameters of the column range are kept, so the shard holds
+// exactly the codes and scales of the unsplit weight (row-parallel
+// tensor-parallel layers).  c0 and nc are multiples of 128 for W4A16.
+void QLinear::load_cols(const ltm_quant_config& q, const float* w_host, const float* b_host,
+                        int64_t n, int64_t k, int64_t c0, int64_t nc, cudaStream_t stream) {
+  QLinear full;
+  full.load(q, w_host, b_host, n, k, stream);
+  N = n;
+  K = nc;
+  scheme = q.scheme;
+  if (scheme == LTM_SCHEME_W4A16) {
+    LTM_REQUIRE(c0 % 128 == 0 && nc % 128 == 0, "int4 column shard must align to 128");
+    q4.ensure(N * nc / 2);
+    s4.ensure(N * (nc / 128) * sizeof(float));
+    z4.ensure(N * (nc / 128));
+    LTM_CUDA_TRY(cudaMemcpy2DAsync(q4.ptr, nc / 2, full.q4.as<uint8_t>() + c0 / 2, k / 2, nc / 2, N,
+                                   cudaMemcpyDeviceToDevice, stream));
+    LTM_CUDA_TRY(cudaMemcpy2DAsync(s4.ptr, (nc / 128) * sizeof(float),
+                                   full.s4.as<float>() + c0 / 128, (k / 128) * sizeof(float),
+                                   (nc / 128) * sizeof(float), N, cudaMemcpyDeviceToDevice, stream));
+    LTM_CUDA_TRY(cudaMemcpy2DAsync(z4.ptr, nc / 128, full.z4.as<uint8_t>() + c0 / 128, k / 128,
+                                   nc / 128, N, cudaMemcpyDeviceToDevice, stream));
+  } else {
+    q8.ensure(N * nc);
+    s8.ensure(N * sizeof(float));
+    LTM_CUDA_TRY(cudaMemcpy2DAsync(q8.ptr, nc, full.q8.as<int8_t>() + c0, k, nc, N,
+                                   cudaMemcpyDeviceToDevice, stream));
+    LTM_CUDA_TRY(cudaMemcpyAsync(s8.ptr, full.s8.ptr, N * sizeof(float), cudaMemcpyDeviceToDevice,
+                                 stream));
+  }
+  if (b_host) {
+    bias.ensure(N * sizeof(float));
+    LTM_CUDA_TRY(cudaMemcpyAsync(bias.ptr, full.bias.ptr, N * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, stream));
+  } else {
+    bias.release();
+  }
+  LTM_CUDA_TRY(cudaStreamSynchronize(stream));
+}
+
 // Runs y = epilogue(a W^T) for the block's scheme.  a_act: activation in the
 // act dtype (W8A32 / W4A16); aq/as: its per-token int8 codes (W8A8).
 void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode,
@@ -148,6 +190,11 @@ struct ltm_block {
   ltm_quant_config q{};
   int device = 0;
   int H = 0, F = 0, nh = 0, dh = 0, Ms = 0;
+  // tensor parallelism: this rank's heads (nhl), their width Hl = nhl * dh
+  // and FFN columns Fl; tp = 1 is the single-GPU block
+  ltm_comm* comm = nullptr;
+  int tp = 1, tpr = 0;
+  int nhl = 0, Hl = 0, Fl = 0;
   ltm_dtype dt = LTM_DTYPE_F16;
   bool loaded = false;
   QLinear qkvm, kvm, o, om, g, w1, w2;
@@ -157,8 +204,8 @@ struct ltm_block {
   int rope_S = 0;
   // workspace
   int64_t ws_T = 0;
-  DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, sp, mp, y, zq, zs, z,
-      u, uq, us;
+  DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, spm, y, zq, zs, z,
+      u, uq, us, amax;
   MemoryWriteState mw;
 
   size_t act_bytes() const { return dtype_size(dt); }
@@ -188,26 +235,39 @@ struct ltm_block {
       hs.ensure(T * 4);
       xq.ensure(T * H);
       xs.ensure(T * 4);
-      osq.ensure(T * H);
+      osq.ensure(T * Hl);
       oss.ensure(T * 4);
-      omq.ensure(T * H);
+      omq.ensure(T * Hl);
       oms.ensure(T * 4);
       zq.ensure(T * H);
       zs.ensure(T * 4);
-      uq.ensure(T * F);
+      uq.ensure(T * Fl);
       us.ensure(T * 4);
+      if (tp > 1) amax.ensure(2 * T * 4);
     } else {
       h.ensure(T * H * a);
       z.ensure(T * H * a);
     }
-    qkv.ensure(T * 4 * H * a);
-    os.ensure(T * H * a);
-    om_.ensure(T * H * a);
-    sp.ensure(T * H * a);
-    mp.ensure(T * H * a);
+    qkv.ensure(T * 4 * Hl * a);
+    os.ensure(T * Hl * a);
+    om_.ensure(T * Hl * a);
+    spm.ensure(2 * T * H * a);  // s | m, one allreduce under tensor parallelism
     y.ensure(T * H * a);
-    u.ensure(T * F * a);
+    u.ensure(T * Fl * a);
     ws_T = T;
+  }
+
+  // Per-token int8 of rows whose columns are split over the ranks (global row
+  // maxima through an allreduce-max); the plain quantizer when tp == 1.
+  void quant_rows(const void* src, int64_t T, int64_t K, int8_t* qd, float* sd, float* amx,
+                  cudaStream_t st) {
+    if (tp == 1) {
+      launch_rowwise_int8(src, dt, T, K, qd, sd, st);
+      return;
+    }
+    launch_row_absmax(src, dt, T, K, amx, st);
+    comm_allreduce(comm, amx, amx, T, LTM_DTYPE_F32, true, st);
+    launch_rowwise_int8_amax(src, dt, T, K, amx, qd, sd, st);
   }
 
   void forward(const void* x, void* out, int B, int S, cudaStream_t st) {
@@ -231,16 +291,16 @@ struct ltm_block {
     {
       Epilogue ep;
       ep.out = kvmb.ptr;
-      ep.ldo = 2 * H;
+      ep.ldo = 2 * Hl;
       kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st);
     }
     // 3. fused Q | K | V | Qm projection with RoPE on Q, K
     {
       Epilogue ep;
       ep.out = qkv.ptr;
-      ep.ldo = 4 * H;
+      ep.ldo = 4 * Hl;
       ep.rope = rope.as<float2>();
-      ep.rope_cols = cfg.use_rotary ? 2 * H : 0;
+      ep.rope_cols = cfg.use_rotary ? 2 * Hl : 0;
       ep.seq_len = S;
       ep.head_dim = dh;
       qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
@@ -251,55 +311,60 @@ struct ltm_block {
       const size_t a = act_bytes();
       AttnParams p{};
       p.q = qkv.ptr;
-      p.k = static_cast<const char*>(qkv.ptr) + H * a;
-      p.v = static_cast<const char*>(qkv.ptr) + 2 * H * a;
+      p.k = static_cast<const char*>(qkv.ptr) + Hl * a;
+      p.v = static_cast<const char*>(qkv.ptr) + 2 * Hl * a;
       p.o = os.ptr;
-      p.ldq = p.ldk = p.ldv = 4 * H;
-      p.ldo = H;
+      p.ldq = p.ldk = p.ldv = 4 * Hl;
+      p.ldo = Hl;
       p.q_batch_rows = S;
       p.kv_batch_rows = S;
       p.Sq = S;
       p.Skv = S;
-      p.nh = nh;
+      p.nh = nhl;
       p.causal_offset = 0;
       launch_attention(p, B, dh, true, dt, st);
       AttnParams pm = p;
-      pm.q = static_cast<const char*>(qkv.ptr) + 3 * H * a;
+      pm.q = static_cast<const char*>(qkv.ptr) + 3 * Hl * a;
       pm.k = kvmb.ptr;
-      pm.v = static_cast<const char*>(kvmb.ptr) + H * a;
+      pm.v = static_cast<const char*>(kvmb.ptr) + Hl * a;
       pm.o = om_.ptr;
-      pm.ldk = pm.ldv = 2 * H;
+      pm.ldk = pm.ldv = 2 * Hl;
       pm.kv_batch_rows = 0;
       pm.Skv = Ms;
       launch_attention(pm, B, dh, false, dt, st);
     }
     // 5. output projections
     if (w8a8) {
-      launch_rowwise_int8(os.ptr, dt, T, H, osq.as<int8_t>(), oss.as<float>(), st);
-      launch_rowwise_int8(om_.ptr, dt, T, H, omq.as<int8_t>(), oms.as<float>(), st);
+      quant_rows(os.ptr, T, Hl, osq.as<int8_t>(), oss.as<float>(), amax.as<float>(), st);
+      quant_rows(om_.ptr, T, Hl, omq.as<int8_t>(), oms.as<float>(),
+                 tp > 1 ? amax.as<float>() + T : nullptr, st);
     }
+    void* sp = spm.ptr;
+    void* mp = static_cast<char*>(spm.ptr) + T * H * act_bytes();
     {
       Epilogue ep;
-      ep.out = sp.ptr;
+      ep.out = sp;
       ep.ldo = H;
       o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st);
-      ep.out = mp.ptr;
+      ep.out = mp;
       om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st);
     }
+    // row-parallel partial sums of s and m (the biases were added by rank 0)
+    if (tp > 1) comm_allreduce(comm, spm.ptr, spm.ptr, 2 * T * H, dt, false, st);
     // 6. gated memory integration
     if (cfg.use_memory_gating) {
       Epilogue ep;
       ep.act = LTM_EPI_SIGMOID;
       ep.out = y.ptr;
       ep.ldo = H;
-      ep.aux0 = sp.ptr;
-      ep.aux1 = mp.ptr;
+      ep.aux0 = sp;
+      ep.aux1 = mp;
       ep.aux2 = x;
       ep.ld_aux = H;
       if (q.memory_write) mw.prepare_gate_epilogue(ep, H, st);
       g.run(x, xq.as<int8_t>(), xs.as<float>(), T, kEpiGateMix, dt, ep, st);
     } else {
-      launch_add3(sp.ptr, mp.ptr, x, y.ptr, T * H, dt, st);
+      launch_add3(sp, mp, x, y.ptr, T * H, dt, st);
     }
     // 7. FFN with residual
     if (w8a8) {
@@ -314,23 +379,28 @@ struct ltm_block {
       Epilogue ep;
       ep.act = LTM_EPI_GELU;
       ep.out = u.ptr;
-      ep.ldo = F;
+      ep.ldo = Fl;
       w1.run(zin, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st);
     }
-    if (w8a8) launch_rowwise_int8(u.ptr, dt, T, F, uq.as<int8_t>(), us.as<float>(), st);
+    if (w8a8) quant_rows(u.ptr, T, Fl, uq.as<int8_t>(), us.as<float>(), amax.as<float>(), st);
     {
+      // out = y + W2 u + b2; under tensor parallelism rank 0 adds y and b2 to
+      // its partial product and the allreduce sums the ranks' partials
       Epilogue ep;
       ep.out = out;
       ep.ldo = H;
       ep.aux0 = y.ptr;
       ep.ld_aux = H;
-      w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, kEpiResid, dt, ep, st);
+      w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, tpr == 0 ? kEpiResid : kEpiPlain, dt, ep,
+             st);
     }
+    if (tp > 1) comm_allreduce(comm, out, out, T * H, dt, false, st);
     // 8. memory write after the read
     if (q.memory_write && cfg.use_memory_gating) {
       const size_t a = act_bytes();
-      mw.update_bank(memory.ptr, kvmb.ptr, static_cast<const char*>(qkv.ptr) + 3 * H * a, 4 * H, T,
-                     H, nh, dh, Ms, cfg.memory_update_rate, q.use_attention_scores != 0, dt, st);
+      mw.update_bank(memory.ptr, kvmb.ptr, 2 * Hl, static_cast<const char*>(qkv.ptr) + 3 * Hl * a,
+                     4 * Hl, T, H, nhl, nh, dh, Ms, cfg.memory_update_rate,
+                     q.use_attention_scores != 0, dt, comm, st);
     }
   }
 };
@@ -371,9 +441,21 @@ std::vector<float> cat_rows(const float* a, int64_t na, const float* b, int64_t 
   return r;
 }
 
+// Rows [r0, r0 + nr) of each of the `parts` consecutive [n_part, k] blocks of
+// a host matrix, concatenated ([parts * nr, k]); k = 1 for a bias.
+std::vector<float> take_rows(const float* w, int parts, int64_t n_part, int64_t r0, int64_t nr,
+                             int64_t k) {
+  std::vector<float> r(static_cast<size_t>(parts * nr * k));
+  for (int p = 0; p < parts; ++p)
+    std::memcpy(r.data() + p * nr * k, w + (p * n_part + r0) * k, sizeof(float) * nr * k);
+  return r;
+}
+
 void load_block(ltm_block* b, const ltm_block_weights* w, cudaStream_t st) {
-  const int H = b->H, F = b->F;
+  const int H = b->H, F = b->F, Hl = b->Hl, Fl = b->Fl;
+  const int64_t hr0 = static_cast<int64_t>(b->tpr) * Hl, fr0 = static_cast<int64_t>(b->tpr) * Fl;
   const bool ub = b->cfg.use_bias != 0;
+  const bool lead = b->tpr == 0;  // adds the biases of the row-parallel layers
   LTM_REQUIRE(w && w->w_qkv && w->w_o && w->w_qm && w->w_km && w->w_vm && w->w_om && w->w_g &&
                   w->w_1 && w->w_2 && w->memory,
               "missing weight");
@@ -383,19 +465,33 @@ void load_block(ltm_block* b, const ltm_block_weights* w, cudaStream_t st) {
                 "missing bias");
   if (b->cfg.use_layer_norm)
     LTM_REQUIRE(w->ln1_g && w->ln1_b && w->ln2_g && w->ln2_b, "missing LayerNorm parameters");
-  auto wq = cat_rows(w->w_qkv, 3 * H, w->w_qm, H, H);
+  // Q | K | V | Qm rows of this rank's heads
+  auto wq = cat_rows(take_rows(w->w_qkv, 3, H, hr0, Hl, H).data(), 3 * Hl,
+                     take_rows(w->w_qm, 1, H, hr0, Hl, H).data(), Hl, H);
   std::vector<float> bq;
-  if (ub) bq = cat_rows(w->b_qkv, 3 * H, w->b_qm, H, 1);
-  b->qkvm.load(b->q, wq.data(), ub ? bq.data() : nullptr, 4 * H, H, st);
-  auto wk = cat_rows(w->w_km, H, w->w_vm, H, H);
+  if (ub)
+    bq = cat_rows(take_rows(w->b_qkv, 3, H, hr0, Hl, 1).data(), 3 * Hl,
+                  take_rows(w->b_qm, 1, H, hr0, Hl, 1).data(), Hl, 1);
+  b->qkvm.load(b->q, wq.data(), ub ? bq.data() : nullptr, 4 * Hl, H, st);
+  // K_M | V_M rows of this rank's heads
+  auto wk = cat_rows(take_rows(w->w_km, 1, H, hr0, Hl, H).data(), Hl,
+                     take_rows(w->w_vm, 1, H, hr0, Hl, H).data(), Hl, H);
   std::vector<float> bk;
-  if (ub) bk = cat_rows(w->b_km, H, w->b_vm, H, 1);
-  b->kvm.load(b->q, wk.data(), ub ? bk.data() : nullptr, 2 * H, H, st);
-  b->o.load(b->q, w->w_o, ub ? w->b_o : nullptr, H, H, st);
-  b->om.load(b->q, w->w_om, ub ? w->b_om : nullptr, H, H, st);
+  if (ub)
+    bk = cat_rows(take_rows(w->b_km, 1, H, hr0, Hl, 1).data(), Hl,
+                  take_rows(w->b_vm, 1, H, hr0, Hl, 1).data(), Hl, 1);
+  b->kvm.load(b->q, wk.data(), ub ? bk.data() : nullptr, 2 * Hl, H, st);
+  if (b->tp == 1) {
+    b->o.load(b->q, w->w_o, ub ? w->b_o : nullptr, H, H, st);
+    b->om.load(b->q, w->w_om, ub ? w->b_om : nullptr, H, H, st);
+    b->w2.load(b->q, w->w_2, ub ? w->b_2 : nullptr, H, F, st);
+  } else {  // row-parallel: input columns of this rank's heads / FFN columns
+    b->o.load_cols(b->q, w->w_o, (ub && lead) ? w->b_o : nullptr, H, H, hr0, Hl, st);
+    b->om.load_cols(b->q, w->w_om, (ub && lead) ? w->b_om : nullptr, H, H, hr0, Hl, st);
+    b->w2.load_cols(b->q, w->w_2, (ub && lead) ? w->b_2 : nullptr, H, F, fr0, Fl, st);
+  }
   b->g.load(b->q, w->w_g, ub ? w->b_g : nullptr, H, H, st);
-  b->w1.load(b->q, w->w_1, ub ? w->b_1 : nullptr, F, H, st);
-  b->w2.load(b->q, w->w_2, ub ? w->b_2 : nullptr, H, F, st);
+  b->w1.load(b->q, w->w_1 + fr0 * H, ub ? w->b_1 + fr0 : nullptr, Fl, H, st);
   if (b->cfg.use_layer_norm) {
     for (auto pr : {std::make_pair(&b->ln1_g, w->ln1_g), std::make_pair(&b->ln1_b, w->ln1_b),
                     std::make_pair(&b->ln2_g, w->ln2_g), std::make_pair(&b->ln2_b, w->ln2_b)}) {
@@ -405,7 +501,7 @@ void load_block(ltm_block* b, const ltm_block_weights* w, cudaStream_t st) {
   }
   b->memory.ensure(static_cast<size_t>(b->Ms) * H * dtype_size(b->dt));
   upload_f32_as(w->memory, static_cast<int64_t>(b->Ms) * H, b->dt, b->memory.ptr, st);
-  b->kvmb.ensure(static_cast<size_t>(b->Ms) * 2 * H * dtype_size(b->dt));
+  b->kvmb.ensure(static_cast<size_t>(b->Ms) * 2 * Hl * dtype_size(b->dt));
   if (b->q.scheme == LTM_SCHEME_W8A8) {
     b->mq.ensure(static_cast<size_t>(b->Ms) * H);
     b->ms.ensure(static_cast<size_t>(b->Ms) * sizeof(float));
@@ -445,6 +541,9 @@ ltm_block* make_block(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
   b->dh = cfg->head_dim;
   b->Ms = cfg->memory_slots;
   b->dt = qcfg->act_dtype;
+  b->nhl = b->nh;
+  b->Hl = b->H;
+  b->Fl = b->F;
   return b.release();
 }
 
@@ -480,6 +579,32 @@ extern "C" ltm_status ltm_block_create(const ltm_block_config* cfg, const ltm_qu
   return guarded([&] {
     LTM_REQUIRE(out, "out is NULL");
     *out = make_block(cfg, qcfg, device);
+  });
+}
+
+extern "C" ltm_status ltm_block_create_tp(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
+                                          ltm_comm* comm, ltm_block** out) {
+  return guarded([&] {
+    LTM_REQUIRE(out && comm, "NULL argument");
+    LTM_REQUIRE(cfg && qcfg, "NULL config");
+    const int n = comm->nranks;
+    LTM_REQUIRE(n >= 1, "communicator without ranks");
+    LTM_REQUIRE(cfg->num_heads % n == 0, "num_heads must be divisible by the tensor-parallel size");
+    LTM_REQUIRE(cfg->ffn_dim % n == 0, "ffn_dim must be divisible by the tensor-parallel size");
+    const int Hl = cfg->hidden_dim / n, Fl = cfg->ffn_dim / n;
+    LTM_REQUIRE(Hl % 32 == 0 && Fl % 32 == 0,
+                "per-rank head and FFN widths must be multiples of 32");
+    if (qcfg->scheme == LTM_SCHEME_W4A16)
+      LTM_REQUIRE(Hl % 128 == 0 && Fl % 128 == 0,
+                  "W4A16 needs per-rank head and FFN widths that are multiples of 128");
+    std::unique_ptr<ltm_block> b(make_block(cfg, qcfg, comm->device));
+    b->comm = comm;
+    b->tp = n;
+    b->tpr = comm->rank;
+    b->nhl = b->nh / n;
+    b->Hl = Hl;
+    b->Fl = Fl;
+    *out = b.release();
   });
 }
 

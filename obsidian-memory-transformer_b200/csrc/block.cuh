@@ -5,7 +5,18 @@
 #include "common.cuh"
 #include "epilogue.cuh"
 
+// Tensor-parallel communicator (comm.cu): an NCCL communicator of `nranks`
+// GPUs; this process is `rank`, on `device`.
+struct ltm_comm {
+  void* handle = nullptr;
+  int nranks = 1, rank = 0, device = 0;
+};
+
 namespace ltm_b200 {
+
+// In-stream allreduce (sum, or max) over the communicator; send == recv allowed.
+void comm_allreduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dtype dt,
+                    bool max_op, cudaStream_t st);
 
 // Owning device allocation (grow-only).
 struct DevBuf {
@@ -30,6 +41,10 @@ struct QLinear {
   DevBuf q8, s8, q4, s4, z4, bias;
   void load(const ltm_quant_config& q, const float* w_host, const float* b_host, int64_t n,
             int64_t k, cudaStream_t stream);
+  // Input columns [c0, c0 + nc) of a host [n, k] weight with the unsplit
+  // weight's scales (row-parallel tensor-parallel layers).
+  void load_cols(const ltm_quant_config& q, const float* w_host, const float* b_host, int64_t n,
+                 int64_t k, int64_t c0, int64_t nc, cudaStream_t stream);
   void run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode, ltm_dtype dt,
            Epilogue ep, cudaStream_t stream) const;
 };
@@ -54,10 +69,21 @@ struct AttnParams {
 struct MemoryWriteState {
   DevBuf colsum, qsum, wslot;
   void prepare_gate_epilogue(Epilogue& ep, int H, cudaStream_t st);
-  void update_bank(void* memory, const void* kvm, const void* qm, int64_t ldq, int64_t T, int H,
-                   int nh, int dh, int Ms, float rate, bool use_scores, ltm_dtype dt,
-                   cudaStream_t st);
+  // kvm: K_M [Ms, heads*dh] with row stride ldk; qm: memory queries [T,
+  // heads*dh] with row stride ldq (this rank's `heads` of nh_total; comm
+  // sums the slot weights over the ranks when given).
+  void update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm, int64_t ldq,
+                   int64_t T, int H, int heads, int nh_total, int dh, int Ms, float rate,
+                   bool use_scores, ltm_dtype dt, ltm_comm* comm, cudaStream_t st);
 };
+
+// Slot weights of `heads` heads (rate / nh_total per head, summed into wslot;
+// qsum [heads*dh] and wslot [Ms] are cleared here) and the bank EMA.
+void launch_slot_weights(const void* keys, int64_t ldk, const void* queries, int64_t ldq,
+                         int64_t T, int Ms, int heads, int dh, int nh_total, float rate,
+                         ltm_dtype dt, float* qsum, float* wslot, cudaStream_t st);
+void launch_bank_update(void* memory, const float* state, float state_scale, const float* wslot,
+                        float rate, int Ms, int H, ltm_dtype dt, cudaStream_t st);
 
 // Memory-bank store: slot weights from the mean of the query rows against the
 // keys (use_scores) and the EMA of every slot towards state * state_scale.
@@ -72,6 +98,12 @@ void validate_memory_store(const void* memory, const void* keys, int64_t ldk, co
 
 void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, int8_t* q, float* s,
                          cudaStream_t stream);
+// Tensor-parallel per-token quantization: local row maxima, then codes with
+// s = amax / 127 from the (allreduced) maxima.
+void launch_row_absmax(const void* x, ltm_dtype dt, int64_t rows, int64_t K, float* amax,
+                       cudaStream_t stream);
+void launch_rowwise_int8_amax(const void* x, ltm_dtype dt, int64_t rows, int64_t K,
+                              const float* amax, int8_t* q, float* s, cudaStream_t stream);
 void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
                  ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream);
 void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,

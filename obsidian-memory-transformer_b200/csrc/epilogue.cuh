@@ -316,14 +316,13 @@ namespace ltm_b200 {
 //   * the TMEM load of chunk c+1 and the global operands of chunk c+1 (RoPE
 //     table row, residual / gate-mix tensors) are in flight while chunk c is
 //     computed;
-//   * results are packed into a 32-row x 128-byte box in shared memory with
-//     the 128-byte swizzle (conflict-free row writes) and written by one TMA
-//     store per box; two boxes per warp alternate, so packing the next box
-//     overlaps the previous store.
+//   * results are packed into 32-row boxes of 128 or 64 bytes per row in
+//     shared memory with the matching TMA swizzle (conflict-free row writes)
+//     and written by one TMA store per box; two box slots per warp alternate,
+//     so packing the next box overlaps the previous store.
 // The TMEM accumulator is released (on_tmem_free) as soon as the last chunk
 // has been read, before its math.
 // ---------------------------------------------------------------------------
-constexpr uint32_t kEpiBoxBytes = 32 * 128;
 
 template <int MODE, class OutT>
 struct EpiChunkAux {
@@ -384,21 +383,32 @@ struct EpiChunkAux {
   }
 };
 
-template <int MODE, class OutT, int CW, bool ACC_INT>
+// BOXB: bytes per row of one staged box, 128 (128-byte swizzle, 4 KiB boxes)
+// or 64 (64-byte swizzle, 2 KiB boxes); the output tensor map's box is
+// BOXB / sizeof(store type) columns x 32 rows with the same swizzle.
+template <int MODE, class OutT, int CW, bool ACC_INT, int BOXB = 128>
 struct TmaTileEpilogue {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
   static constexpr int NCH = CW / 32;
-  static constexpr int BOXC = 128 / static_cast<int>(sizeof(StoreT));  // columns per box
-  static constexpr int CPB = BOXC / 32;                                  // chunks per box
+  static constexpr int BOXC = BOXB / static_cast<int>(sizeof(StoreT));  // columns per box
   static constexpr int UPC = 32 * static_cast<int>(sizeof(StoreT)) / 16;  // 16-byte units per chunk row
+  static constexpr int UPB = BOXB / 16;                                   // 16-byte units per box row
+  static constexpr uint32_t kBoxBytes = 32 * BOXB;
+  // Staged boxes per tile; two slots per warp.  When both boxes of a tile fit
+  // (kBatched), the warp packs the whole tile, fences once and issues both
+  // stores, and waits for the previous tile's stores to leave shared memory
+  // only at the next tile start.  Otherwise the slots alternate box by box.
+  static constexpr int kBoxesPerTile = CW * static_cast<int>(sizeof(StoreT)) / BOXB;
+  static constexpr bool kBatched = kBoxesPerTile <= 2;
+  static_assert(kBatched || kBoxesPerTile % 2 == 0, "slot parity must restart at each tile");
   static constexpr bool kMath = MODE != kEpiAccI32;
+  static_assert(BOXB == 128 || BOXB == 64, "box rows are 64 or 128 bytes");
   static_assert(CW % BOXC == 0, "warp columns must be whole boxes");
   // shared-memory bytes of the per-warp column vectors (scale + bias)
   static constexpr uint32_t kColBytes = 2 * CW * 4;
 
   float rs_next = 1.0f;
   float cs_next[NCH], bs_next[NCH];
-  int sb = 0;  // staging box to fill next
 
   // Fetches the row scale of row m and the scale/bias of columns nw + 32c + lane.
   __device__ __forceinline__ void prefetch(const Epilogue& ep, int64_t m, int64_t nw, int M, int N,
@@ -423,6 +433,9 @@ struct TmaTileEpilogue {
                                       int64_t m, int row0, int nw, int M, int N, float* cvec,
                                       uint8_t* stg, int lane, OnTmemFree&& on_tmem_free) {
     const float rs = rs_next;
+    if constexpr (kBatched) {
+      if (lane == 0) bulk_wait_group_read<0>();  // previous tile's boxes have left the slots
+    }
     if constexpr (kMath) {
       __syncwarp();  // previous tile's reads of cvec are done
 #pragma unroll
@@ -519,40 +532,48 @@ struct TmaTileEpilogue {
       if constexpr (!Aux::kAhead) {
         if (c + 1 < NCH) aux[0].load(ep, m, n + 32, pos, row_ok, n + 32 < N);
       }
-      // pack into the staging box (128-byte swizzle: 16-byte unit u of row r
-      // at unit u ^ (r & 7))
-      const int cb = c % CPB;
-      if (cb == 0) {
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-      }
-      uint8_t* box = stg + sb * kEpiBoxBytes + lane * 128;
+      // Pack into staging boxes.  Unit k of this chunk is unit g = c*UPC + k
+      // of the warp's row, i.e. unit g % UPB of box g / UPB.  Swizzle (as the
+      // TMA applies it): 128-byte rows, unit u of row r at u ^ (r & 7);
+      // 64-byte rows, unit u of row r at u ^ ((r >> 1) & 3).
       constexpr int EPU = 16 / static_cast<int>(sizeof(StoreT));
 #pragma unroll
-      for (int u = 0; u < UPC; ++u) {
+      for (int k = 0; k < UPC; ++k) {
+        const int g = c * UPC + k;
+        const int ub = g % UPB;
+        const int sb = (g / UPB) & 1;  // slot of this box (compile-time)
+        if (!kBatched && ub == 0) {
+          if (lane == 0) bulk_wait_group_read<1>();  // the store that last read slot sb is done
+          __syncwarp();
+        }
         uint4 raw;
         if constexpr (!kMath) {
-          raw.x = __float_as_uint(v[u * 4 + 0]);
-          raw.y = __float_as_uint(v[u * 4 + 1]);
-          raw.z = __float_as_uint(v[u * 4 + 2]);
-          raw.w = __float_as_uint(v[u * 4 + 3]);
+          raw.x = __float_as_uint(v[k * 4 + 0]);
+          raw.y = __float_as_uint(v[k * 4 + 1]);
+          raw.z = __float_as_uint(v[k * 4 + 2]);
+          raw.w = __float_as_uint(v[k * 4 + 3]);
         } else {
           StoreT* e = reinterpret_cast<StoreT*>(&raw);
 #pragma unroll
-          for (int i = 0; i < EPU; ++i) e[i] = from_f32<StoreT>(v[u * EPU + i]);
+          for (int i = 0; i < EPU; ++i) e[i] = from_f32<StoreT>(v[k * EPU + i]);
         }
-        const int unit = (cb * UPC + u) ^ (lane & 7);
-        *reinterpret_cast<uint4*>(box + unit * 16) = raw;
-      }
-      if (cb == CPB - 1) {
-        fence_proxy_async_smem();
-        __syncwarp();
-        const int x = nw + (c - cb) * 32;
-        if (lane == 0 && row0 < M && x < N) {  // boxes wholly outside the output are skipped
-          tma_store_2d(tmo, stg + sb * kEpiBoxBytes, x, row0);
-          bulk_commit_group();
+        const int unit = BOXB == 128 ? (ub ^ (lane & 7)) : (ub ^ ((lane >> 1) & 3));
+        *reinterpret_cast<uint4*>(stg + sb * kBoxBytes + lane * BOXB + unit * 16) = raw;
+        const bool last_box_unit = kBatched ? (g == NCH * UPC - 1) : (ub == UPB - 1);
+        if (last_box_unit) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            constexpr int kFirst = kBatched ? 0 : -1;
+#pragma unroll
+            for (int bi = (kBatched ? kFirst : g / UPB); bi <= g / UPB; ++bi) {
+              const int x = nw + bi * BOXC;
+              if (row0 < M && x < N)  // boxes wholly outside the output are skipped
+                tma_store_2d(tmo, stg + (bi & 1) * kBoxBytes, x, row0);
+            }
+            bulk_commit_group();
+          }
         }
-        sb ^= 1;
       }
     }
   }

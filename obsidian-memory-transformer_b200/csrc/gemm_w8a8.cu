@@ -40,7 +40,7 @@ struct W8A8Smem {
   static constexpr uint32_t kB = BN * kBK;
   static constexpr uint32_t kStage = kA + kB;  // multiple of 1024
   static constexpr uint32_t kStgOff = STAGES * kStage;
-  static constexpr uint32_t kStgWarp = 2 * kEpiBoxBytes;  // two TMA-store boxes per warp
+  static constexpr uint32_t kStgWarp = 2 * 32 * 128;  // two 4 KiB TMA-store boxes per warp
   static constexpr uint32_t kColOff = kStgOff + kEpiWarps * kStgWarp;
   static constexpr uint32_t kColWarp = 2 * (BN / 2) * 4;  // scale + bias of the warp's columns
   static constexpr uint32_t kBarOff = kColOff + kEpiWarps * kColWarp;
@@ -192,6 +192,212 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2).  The pair computes a
+// 256 x 256 tile: per stage each CTA loads its own 128 rows of qa and 128 of
+// the tile's 256 rows of qw (32 KiB; 4 stages beside the epilogue staging)
+// and keeps its 128 x 256 int32 accumulator in its own TMEM.  The
+// even-rank CTA issues the MMAs (M = 256); both CTAs' stage bytes complete on
+// its full barriers, and its commits arrive on the stage / accumulator
+// barriers of both CTAs.  Both CTAs' epilogue warps release an accumulator on
+// the even CTA's barrier.  Per SM this halves the weight bytes per stage, so
+// more of the L2 round trip is covered by queued MMA work.
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 4;
+constexpr int kPairBN = 256;
+constexpr int kPairAccBufs = 2;  // TMEM accumulators per CTA (kPairAccBufs x 256 columns)
+
+struct W8A8PairSmem {
+  static constexpr uint32_t kA = kBM * kBK;            // this CTA's 128 rows of qa
+  static constexpr uint32_t kB = (kPairBN / 2) * kBK;  // this CTA's 128 rows of qw
+  static constexpr uint32_t kStage = kA + kB;          // multiple of 1024
+  static constexpr uint32_t kStgOff = kPairStages * kStage;
+  static constexpr uint32_t kStgWarp = 2 * 32 * 128;  // two 4 KiB TMA-store boxes per warp
+  static constexpr uint32_t kColOff = kStgOff + kEpiWarps * kStgWarp;
+  static constexpr uint32_t kColWarp = 2 * (kPairBN / 2) * 4;
+  static constexpr uint32_t kBarOff = kColOff + kEpiWarps * kColWarp;
+  static constexpr uint32_t kBytes = kBarOff + 256 + 1024;
+};
+
+template <int MODE, class OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    w8a8_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO, int M, int N, int K, Epilogue ep,
+                        int* err) {
+  using L = W8A8PairSmem;
+  constexpr int BN = kPairBN;
+  constexpr int STAGES = kPairStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;  // [2] accumulator ready (both CTAs)
+  uint64_t* acce = accf + 2;        // [2] accumulator drained (even CTA: both CTAs' warps)
+  uint64_t* drain = acce + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int npairs = static_cast<int>(gridDim.x >> 1);
+  const int num_n = (N + BN - 1) / BN;
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * num_n;
+  const int nkb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 2 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
+  }
+  if (warp == 1) tmem_alloc_pair(tslot, kPairAccBufs * BN);
+  tc_fence_before();
+  cluster_sync();  // barriers initialised pair-wide before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(full, 0);  // the even CTA's full[0]
+      int it = 0;
+      for (int t = pair; t < tiles && !*abort_flag; t += npairs) {
+        const int m0 = (t / num_n) * (2 * kBM) + static_cast<int>(rank) * kBM;
+        const int n0 = (t % num_n) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_bounded(empty + s, ph ^ 1, abort_flag, err, kErrWaitEmpty)) break;
+          uint8_t* a_dst = smem + s * L::kStage;
+          if (leader) mbar_arrive_expect_tx(full + s, 2 * L::kStage);
+          const uint32_t fb = full0 + static_cast<uint32_t>(s) * 8u;
+          tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, m0);
+          tma_load_2d_pair(a_dst + L::kA, &tmB, fb, kb * kBK, n0);
+          ++it;
+        }
+      }
+      if (*abort_flag && leader) {
+        // Drain the pair's copies still in flight before the CTAs unwind.
+        volatile int never = 0;
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+          mbar_wait_bounded(full + (j % STAGES), (j / STAGES) & 1, &never, err, kErrWaitOther);
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(2 * kBM, BN);
+      int it = 0, lt = 0;
+      for (int t = pair; t < tiles && !*abort_flag; t += npairs, ++lt) {
+        const int b = lt % kPairAccBufs;
+        const uint32_t use = static_cast<uint32_t>(lt / kPairAccBufs);
+        if (!mbar_wait_bounded(acce + b, (use & 1) ^ 1, abort_flag, err, kErrWaitAccum)) break;
+        tc_fence_after();
+        const uint32_t tacc = tmem + b * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait_bounded(full + s, ph, abort_flag, err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::kStage);
+          const uint32_t b_addr = a_addr + L::kA;
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k) {
+            tc_mma_i8_pair(tacc, make_desc_kmajor_sw128(a_addr + k * 32),
+                           make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+          }
+          tc_commit_pair_mc(empty + s, 0x3);
+          ++it;
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(accf + b, 0x3);
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        tc_commit_pair_mc(drain, 0x1);
+        mbar_wait_bounded(drain, 0, &never, err, kErrWaitOther);
+      }
+    }
+  } else {
+    // Epilogue warps 2..9 of each CTA: TMEM lane quarter q = warp % 4 (this
+    // CTA's tile rows 32q..32q+31), column half (warp - 2) / 4.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
+    float* cvec = reinterpret_cast<float*>(smem + L::kColOff + (warp - 2) * L::kColWarp);
+    const uint32_t acce0 = mapa_shared(acce, 0);  // the even CTA's acce[0]
+    TmaTileEpilogue<MODE, OutT, BN / 2, true, 128> epi;
+    auto rows_of = [&](int t) {
+      return (t / num_n) * (2 * kBM) + static_cast<int>(rank) * kBM + q * 32;
+    };
+    auto cols_of = [&](int t) { return (t % num_n) * BN + half * (BN / 2); };
+    if (pair < tiles) epi.prefetch(ep, rows_of(pair) + lane, cols_of(pair), M, N, lane);
+    int lt = 0;
+    for (int t = pair; t < tiles; t += npairs, ++lt) {
+      const int b = lt % kPairAccBufs;
+      const uint32_t use = static_cast<uint32_t>(lt / kPairAccBufs);
+      const int row0 = rows_of(t), nw = cols_of(t);
+      if (!mbar_wait_bounded(accf + b, use & 1, abort_flag, err, kErrWaitAccum)) break;
+      tc_fence_after();
+      epi.run(ep, &tmO, tmem + b * BN + half * (BN / 2) + (static_cast<uint32_t>(q * 32) << 16),
+              row0 + lane, row0, nw, M, N, cvec, stg, lane,
+              [&] {
+                if (lane == 0) mbar_arrive_cluster(acce0 + static_cast<uint32_t>(b) * 8u);
+                const int tn = t + npairs;
+                if (tn < tiles) epi.prefetch(ep, rows_of(tn) + lane, cols_of(tn), M, N, lane);
+              });
+    }
+    if (lane == 0) bulk_wait_group_all();
+  }
+
+  tc_fence_before();
+  cluster_sync();  // the pair's MMAs, copies and remote arrives are finished
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kPairAccBufs * BN);
+  }
+}
+
+template <int MODE, class OutT>
+void launch_w8a8_pair(const int8_t* qa, const int8_t* qw, int M, int N, int K, const Epilogue& ep,
+                      cudaStream_t stream) {
+  using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
+  using L = W8A8PairSmem;
+  static_assert(L::kBytes <= 232448, "shared memory budget exceeded");
+  CUtensorMap ta, tb, to;
+  make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
+  make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, kPairBN / 2);
+  constexpr int ob = static_cast<int>(sizeof(StoreT));
+  make_tma_2d(&to, ep.out, tma_dtype_of<StoreT>(), ob, M, N, ep.ldo, 128 / ob, 32);
+  auto kern = w8a8_tc_pair_kernel<MODE, OutT>;
+  LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kPairBN - 1) / kPairBN);
+  const int pairs_max = device_sm_count() / 2;
+  const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, ep, device_error_ptr());
+  static const char* const kNames[] = {"w8a8_tc_kernel/plain", "w8a8_tc_kernel/rope",
+                                      "w8a8_tc_kernel/resid", "w8a8_tc_kernel/gatemix",
+                                      "w8a8_tc_kernel/acc_i32"};
+  check_launch(kNames[MODE], stream);
+}
+
 template <int BN, int STAGES, int MODE, class OutT>
 void launch_w8a8_inst(const int8_t* qa, const int8_t* qw, int M, int N, int K, const Epilogue& ep,
                       cudaStream_t stream) {
@@ -239,7 +445,9 @@ void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64
   dispatch_epilogue(mode, out_dt, [&](auto mode_c, auto out_tag) {
     constexpr int MODE = decltype(mode_c)::value;
     using OutT = decltype(out_tag);
-    if (N % 256 == 0)
+    if (N % 256 == 0 && M >= 2 * kBM)
+      launch_w8a8_pair<MODE, OutT>(qa, qw, m, n, k, ep, stream);
+    else if (N % 256 == 0)
       launch_w8a8_inst<256, 3, MODE, OutT>(qa, qw, m, n, k, ep, stream);
     else
       launch_w8a8_inst<128, 4, MODE, OutT>(qa, qw, m, n, k, ep, stream);

@@ -41,11 +41,13 @@ __global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ x, in
   }
 }
 
-// One CTA per head: slot softmax of the mean memory query against K_M.
+// One CTA per head: slot softmax of the mean memory query against K_M, added
+// into wslot with weight rate / nh_total (the mean over all heads; a
+// tensor-parallel rank adds its own heads and the ranks sum wslot).
 template <class T>
 __global__ void __launch_bounds__(256) slot_weight_kernel(const float* __restrict__ qsum,
                                                           float inv_T, const T* __restrict__ kvm,
-                                                          int64_t ldk, int Ms, int dh, int nh,
+                                                          int64_t ldk, int Ms, int dh, int nh_total,
                                                           float rate, float* __restrict__ wslot) {
   extern __shared__ float sc[];  // [Ms] scores, then reduction scratch
   __shared__ float red[32];
@@ -77,7 +79,7 @@ __global__ void __launch_bounds__(256) slot_weight_kernel(const float* __restric
   __syncthreads();
   sum = 0.0f;
   for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) sum += red[i];
-  const float f = rate / (sum * static_cast<float>(nh));
+  const float f = rate / (sum * static_cast<float>(nh_total));
   for (int s = threadIdx.x; s < Ms; s += blockDim.x) atomicAdd(wslot + s, sc[s] * f);
 }
 
@@ -105,37 +107,48 @@ void MemoryWriteState::prepare_gate_epilogue(Epilogue& ep, int H, cudaStream_t s
   ep.colsum = colsum.as<float>();
 }
 
+void launch_slot_weights(const void* keys, int64_t ldk, const void* queries, int64_t ldq,
+                         int64_t T, int Ms, int heads, int dh, int nh_total, float rate,
+                         ltm_dtype dt, float* qsum, float* wslot, cudaStream_t st) {
+  const int Hq = heads * dh;
+  dispatch_dtype(dt, [&](auto tag) {
+    using TT = decltype(tag);
+    LTM_CUDA_TRY(cudaMemsetAsync(qsum, 0, Hq * sizeof(float), st));
+    LTM_CUDA_TRY(cudaMemsetAsync(wslot, 0, Ms * sizeof(float), st));
+    const int splits = static_cast<int>(std::min<int64_t>(64, (T + 63) / 64));
+    dim3 g1((Hq + 31) / 32, splits);
+    colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(queries), ldq, T, Hq, qsum);
+    check_launch("colsum_kernel", st);
+    const size_t smem = static_cast<size_t>(Ms) * sizeof(float);
+    auto kern = slot_weight_kernel<TT>;
+    LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+    kern<<<heads, 256, smem, st>>>(qsum, 1.0f / static_cast<float>(T), static_cast<const TT*>(keys),
+                                   ldk, Ms, dh, nh_total, rate, wslot);
+    check_launch("slot_weight_kernel", st);
+  });
+}
+
+void launch_bank_update(void* memory, const float* state, float state_scale, const float* wslot,
+                        float rate, int Ms, int H, ltm_dtype dt, cudaStream_t st) {
+  dispatch_dtype(dt, [&](auto tag) {
+    using TT = decltype(tag);
+    const int64_t n = static_cast<int64_t>(Ms) * H;
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
+    bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale,
+                                                 wslot, rate, Ms, H);
+    check_launch("bank_update_kernel", st);
+  });
+}
+
 void launch_memory_store(void* memory, const void* keys, int64_t ldk, const void* queries,
                          int64_t ldq, int64_t T, const float* state, float state_scale, int Ms,
                          int H, int nh, float rate, bool use_scores, ltm_dtype dt, float* qsum,
                          float* wslot, cudaStream_t st) {
   if (Ms == 0 || H == 0) return;
-  const int dh = H / nh;
-  dispatch_dtype(dt, [&](auto tag) {
-    using TT = decltype(tag);
-    const float* w = nullptr;
-    if (use_scores) {
-      LTM_CUDA_TRY(cudaMemsetAsync(qsum, 0, H * sizeof(float), st));
-      LTM_CUDA_TRY(cudaMemsetAsync(wslot, 0, Ms * sizeof(float), st));
-      const int splits = static_cast<int>(std::min<int64_t>(64, (T + 63) / 64));
-      dim3 g1((H + 31) / 32, splits);
-      colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(queries), ldq, T, H, qsum);
-      check_launch("colsum_kernel", st);
-      const size_t smem = static_cast<size_t>(Ms) * sizeof(float);
-      auto kern = slot_weight_kernel<TT>;
-      LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)));
-      kern<<<nh, 256, smem, st>>>(qsum, 1.0f / static_cast<float>(T), static_cast<const TT*>(keys),
-                                  ldk, Ms, dh, nh, rate, wslot);
-      check_launch("slot_weight_kernel", st);
-      w = wslot;
-    }
-    const int64_t n = static_cast<int64_t>(Ms) * H;
-    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
-    bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale, w,
-                                                 rate, Ms, H);
-    check_launch("bank_update_kernel", st);
-  });
+  if (use_scores)
+    launch_slot_weights(keys, ldk, queries, ldq, T, Ms, nh, H / nh, nh, rate, dt, qsum, wslot, st);
+  launch_bank_update(memory, state, state_scale, use_scores ? wslot : nullptr, rate, Ms, H, dt, st);
 }
 
 void validate_memory_store(const void* memory, const void* keys, int64_t ldk, const void* queries,
@@ -153,19 +166,23 @@ void validate_memory_store(const void* memory, const void* keys, int64_t ldk, co
   }
 }
 
-void MemoryWriteState::update_bank(void* memory, const void* kvm, const void* qm, int64_t ldq,
-                                   int64_t T, int H, int nh, int dh, int Ms, float rate,
-                                   bool use_scores, ltm_dtype dt, cudaStream_t st) {
-  (void)dh;
-  if (T == 0) return;
+void MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm,
+                                   int64_t ldq, int64_t T, int H, int heads, int nh_total, int dh,
+                                   int Ms, float rate, bool use_scores, ltm_dtype dt,
+                                   ltm_comm* comm, cudaStream_t st) {
+  if (T == 0 || Ms == 0) return;
+  const int Hq = heads * dh;
   if (use_scores) {
-    qsum.ensure(H * sizeof(float));
+    qsum.ensure(Hq * sizeof(float));
     wslot.ensure(Ms * sizeof(float));
+    validate_memory_store(memory, kvm, ldk, qm, ldq, T, colsum.as<float>(), Ms, Hq, heads, true);
+    launch_slot_weights(kvm, ldk, qm, ldq, T, Ms, heads, dh, nh_total, rate, dt, qsum.as<float>(),
+                        wslot.as<float>(), st);
+    if (comm && comm->nranks > 1)  // every rank adds its heads' share of the head mean
+      comm_allreduce(comm, wslot.ptr, wslot.ptr, Ms, LTM_DTYPE_F32, false, st);
   }
-  validate_memory_store(memory, kvm, 2 * H, qm, ldq, T, colsum.as<float>(), Ms, H, nh, use_scores);
-  launch_memory_store(memory, kvm, 2 * H, qm, ldq, T, colsum.as<float>(),
-                      1.0f / static_cast<float>(T), Ms, H, nh, rate, use_scores, dt,
-                      qsum.as<float>(), wslot.as<float>(), st);
+  launch_bank_update(memory, colsum.as<float>(), 1.0f / static_cast<float>(T),
+                     use_scores ? wslot.as<float>() : nullptr, rate, Ms, H, dt, st);
 }
 
 namespace {

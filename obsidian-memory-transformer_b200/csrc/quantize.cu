@@ -286,6 +286,68 @@ void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, i
   check_launch("rowwise_int8_kernel", stream);
 }
 
+namespace {
+
+// Split form of the per-token quantizer for a row whose columns are spread
+// over tensor-parallel ranks: row_absmax_kernel gives this rank's row maxima,
+// the ranks combine them with an allreduce-max, and rowwise_int8_amax_kernel
+// quantizes the local columns with s = global max / 127 -- the codes and
+// scales the unsplit row would get.  One warp per row.
+template <class T>
+__global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x, int64_t rows,
+                                                         int64_t K, float* __restrict__ amax) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * K;
+  float m = 0.0f;
+  for (int64_t j = lane; j < K; j += 32) m = fmaxf(m, fabsf(to_f32(xr[j])));
+  m = warp_max(m);
+  if (lane == 0) amax[row] = m;
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) rowwise_int8_amax_kernel(const T* __restrict__ x,
+                                                                int64_t rows, int64_t K,
+                                                                const float* __restrict__ amax,
+                                                                int8_t* __restrict__ q,
+                                                                float* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * K;
+  int8_t* qr = q + row * K;
+  const float s = __fdiv_rn(amax[row], 127.0f);
+  const float inv = recip_or_zero(s);
+  for (int64_t j = lane; j < K; j += 32) qr[j] = quant_i8_exact(to_f32(xr[j]), s, inv);
+  if (lane == 0) scales[row] = s;
+}
+
+}  // namespace
+
+void launch_row_absmax(const void* x, ltm_dtype dt, int64_t rows, int64_t K, float* amax,
+                       cudaStream_t stream) {
+  if (rows == 0) return;
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+    row_absmax_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, amax);
+  });
+  check_launch("row_absmax_kernel", stream);
+}
+
+void launch_rowwise_int8_amax(const void* x, ltm_dtype dt, int64_t rows, int64_t K,
+                              const float* amax, int8_t* q, float* s, cudaStream_t stream) {
+  if (rows == 0) return;
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+    rowwise_int8_amax_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K,
+                                                            amax, q, s);
+  });
+  check_launch("rowwise_int8_amax_kernel", stream);
+}
+
 }  // namespace ltm_b200
 
 using namespace ltm_b200;

@@ -103,6 +103,12 @@ def _declare(L):
         "ltm_model_load_layer": ([vp, ci, C.POINTER(BlockWeightsC)], ci),
         "ltm_model_forward": ([vp, vp, vp, ci, ci, vp], ci),
         "ltm_model_destroy": ([vp], ci),
+        "ltm_comm_unique_id": ([vp], ci),
+        "ltm_comm_create": ([vp, ci, ci, ci, C.POINTER(vp)], ci),
+        "ltm_comm_allreduce": ([vp, vp, vp, C.c_size_t, ci, ci, vp], ci),
+        "ltm_comm_destroy": ([vp], ci),
+        "ltm_block_create_tp": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), vp,
+                                 C.POINTER(vp)], ci),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -421,16 +427,89 @@ def _weights_c(w: dict):
     return st, keep
 
 
-class TitanBlock:
-    """ltm::transformer::TitanBlock<T> over the C ABI (T = act dtype)."""
+COMM_ID_BYTES = 128
 
-    def __init__(self, config: TitanBlockConfig, quant: QuantConfig | None = None, device: int = 0):
+
+def comm_unique_id() -> bytes:
+    """A fresh communicator id (rank 0 makes it; every rank needs the same bytes)."""
+    buf = C.create_string_buffer(COMM_ID_BYTES)
+    _check(lib().ltm_comm_unique_id(buf))
+    return buf.raw
+
+
+def broadcast_comm_id(group=None) -> bytes:
+    """Group rank 0 makes a communicator id and every rank of the
+    torch.distributed group receives the same bytes (host-side exchange; works
+    over gloo)."""
+    import torch.distributed as dist
+    obj = [comm_unique_id() if dist.get_rank(group) == 0 else None]
+    src = dist.get_global_rank(group, 0) if group is not None else 0
+    dist.broadcast_object_list(obj, src=src, group=group)
+    uid = obj[0]
+    if not isinstance(uid, bytes) or len(uid) != COMM_ID_BYTES:
+        raise LtmError(ERR_COMM, "malformed communicator id")
+    return uid
+
+
+class Comm:
+    """Tensor-parallel communicator of `nranks` GPUs (ltm_comm_* over NCCL).
+
+    `uid` is the bytes of comm_unique_id() made on rank 0 and handed to every
+    rank by the caller (see `from_process_group`)."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device: int):
+        h = C.c_void_p()
+        _check(lib().ltm_comm_create(C.c_char_p(uid), nranks, rank, device, C.byref(h)))
+        self._h, self.nranks, self.rank, self.device = h, nranks, rank, device
+
+    @classmethod
+    def from_process_group(cls, device: int, group=None) -> "Comm":
+        """Creates the communicator of the torch.distributed group's ranks (any
+        backend; the id is broadcast from group rank 0 over it)."""
+        import torch.distributed as dist
+        uid = broadcast_comm_id(group)
+        return cls(uid, dist.get_world_size(group), dist.get_rank(group), device)
+
+    def allreduce(self, x, op_max: bool = False, stream=None):
+        """In-place sum (or max) of a CUDA tensor over the ranks."""
+        _need_cuda(x)
+        _check(lib().ltm_comm_allreduce(self._h, _ptr(x), _ptr(x), x.numel(), dtype_code(x.dtype),
+                                        int(op_max),
+                                        _stream(stream)))
+        return x
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _check(lib().ltm_comm_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+class TitanBlock:
+    """ltm::transformer::TitanBlock<T> over the C ABI (T = act dtype).
+
+    With `comm` the block is the comm.rank-th tensor-parallel shard (on
+    comm.device): load_weights still takes the full weights, forward the full
+    [B,S,H] input and returns the full output on every rank."""
+
+    def __init__(self, config: TitanBlockConfig, quant: QuantConfig | None = None, device: int = 0,
+                 comm: Comm | None = None):
         self.config = config
         self.quant = quant or QuantConfig()
-        self.device = device
+        self.device = comm.device if comm is not None else device
+        self._comm = comm  # kept alive for the block's lifetime
         h = C.c_void_p()
-        _check(lib().ltm_block_create(C.byref(config.to_c()), C.byref(self.quant.to_c()), device,
-                                      C.byref(h)))
+        if comm is None:
+            _check(lib().ltm_block_create(C.byref(config.to_c()), C.byref(self.quant.to_c()),
+                                          device, C.byref(h)))
+        else:
+            _check(lib().ltm_block_create_tp(C.byref(config.to_c()), C.byref(self.quant.to_c()),
+                                             comm._h, C.byref(h)))
         self._h = h
 
     def load_weights(self, w: dict) -> None:

@@ -7,8 +7,11 @@ from _util import as_f32, assert_close, torch_dtype
 
 pytestmark = pytest.mark.gpu
 
+# N % 256 == 0 with M >= 256 runs the CTA-pair kernel (256 x 256 tiles): ragged
+# M, a single pair tile, several tiles per pair, the minimum K
 ACC_SHAPES = [(128, 128, 128), (1, 32, 16), (200, 96, 48), (256, 384, 768), (513, 2304, 768),
-              (64, 768, 3072), (130, 160, 1040)]
+              (64, 768, 3072), (130, 160, 1040), (256, 256, 16), (2048, 3072, 768),
+              (4100, 512, 1024), (300, 768, 3072)]
 
 
 def _rand_i8(shape, seed):

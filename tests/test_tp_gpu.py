@@ -1,0 +1,116 @@
+"""Tensor-parallel Titan block on 2 GPUs (one process per GPU, NCCL through the
+library's communicator) against the TB-v1 oracle and the single-GPU block:
+every rank returns the same full output, the memory bank after the write is
+the same on every rank, and both match the oracle within the dtype tolerance.
+Skipped on a machine with fewer than two GPUs."""
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from _util import as_f32, assert_close, orc_dtype, to_device
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+TOL = {"f16": (2e-2, 1e-2), "bf16": (2e-2, 1e-2)}
+
+
+def _case(scheme, dt, memory_write):
+    H, nh, F, Ms, B, S = 512, 8, 1024, 128, 2, 96
+    return dict(H=H, nh=nh, F=F, Ms=Ms, B=B, S=S, scheme=scheme, dt=dt,
+                memory_write=memory_write, seed=11)
+
+
+def _build(ltm, c, comm=None):
+    sch = {"w8a8": ltm.SCHEME_W8A8, "w4a16": ltm.SCHEME_W4A16}[c["scheme"]]
+    dtc = {"f16": ltm.DTYPE_F16, "bf16": ltm.DTYPE_BF16}[c["dt"]]
+    cfg = ltm.TitanBlockConfig(hidden_dim=c["H"], ffn_dim=c["F"], num_heads=c["nh"],
+                               head_dim=c["H"] // c["nh"], memory_slots=c["Ms"])
+    q = ltm.QuantConfig(scheme=sch, act_dtype=dtc, memory_write=c["memory_write"])
+    return cfg, q, sch
+
+
+def _worker(rank, n, uid, c, out):
+    sys.path[:0] = [str(ROOT), str(ROOT / "obsidian-memory-transformer_b200")]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import ltm_b200 as ltm
+    from ltm_b200 import synthetic
+    try:
+        torch.cuda.set_device(rank)
+        comm = ltm.Comm(uid, n, rank, rank)
+        cfg, q, _ = _build(ltm, c, comm)
+        blk = ltm.TitanBlock(cfg, q, comm=comm)
+        blk.load_weights(synthetic.block_weights(c["H"], c["F"], c["Ms"], c["seed"]))
+        x = synthetic.activations(c["B"] * c["S"], c["H"], c["seed"] + 1)
+        xd = to_device(x, c["dt"]).reshape(c["B"], c["S"], c["H"])
+        y1 = blk(xd)
+        y2 = blk(xd)  # reads the bank the first forward wrote (when enabled)
+        torch.cuda.synchronize()
+        out.put((rank, as_f32(y1), as_f32(y2), as_f32(blk.memory()), ltm.device_error()))
+        blk.close()
+        comm.close()
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        out.put((rank, repr(e), None, None, -1))
+
+
+def _run_tp(c, n=2):
+    import torch.multiprocessing as mp
+    import ltm_b200 as ltm
+    uid = ltm.comm_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, n, uid, c, q)) for r in range(n)]
+    for p in procs:
+        p.start()
+    try:
+        res = {}
+        for _ in procs:
+            r, y1, y2, mem, derr = q.get(timeout=600)
+            assert not isinstance(y1, str), f"rank {r}: {y1}"
+            assert derr == 0
+            res[r] = (y1, y2, mem)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+@pytest.mark.parametrize("scheme,dt,memory_write",
+                         [("w8a8", "f16", True), ("w8a8", "bf16", False), ("w4a16", "bf16", True)])
+def test_tp2_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_write):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from ltm_b200 import synthetic
+    c = _case(scheme, dt, memory_write)
+    res = _run_tp(c)
+    y1, y2, mem = res[0]
+    for r in res:  # the allreduce gives every rank the same result
+        assert np.array_equal(res[r][0], y1) and np.array_equal(res[r][1], y2)
+        assert np.array_equal(res[r][2], mem)
+    # single-GPU block and the oracle on the same inputs
+    cfg, qc, sch = _build(ltm, c)
+    w = synthetic.block_weights(c["H"], c["F"], c["Ms"], c["seed"])
+    blk = ltm.TitanBlock(cfg, qc)
+    blk.load_weights(w)
+    B, S, H = c["B"], c["S"], c["H"]
+    xd = to_device(synthetic.activations(B * S, H, c["seed"] + 1), dt).reshape(B, S, H)
+    s1 = as_f32(blk(xd))
+    ocfg = dict(H=H, F=c["F"], nh=c["nh"], dh=H // c["nh"], Ms=c["Ms"], scheme=sch,
+                dtype=orc_dtype(dt), memory_write=int(memory_write), use_attention_scores=1,
+                update_rate=cfg.memory_update_rate, use_rotary=1, use_bias=1, use_layer_norm=1,
+                use_memory_gating=1)
+    ref, mem_ref = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S)
+    assert_close(y1.reshape(ref.shape), ref, *TOL[dt], what=f"tp2 {scheme} {dt} vs oracle")
+    assert_close(y1, s1, *TOL[dt], what="tp2 vs single GPU")
+    if memory_write:
+        assert_close(mem, mem_ref, 2e-3, 1e-2, what="tp2 bank after write")
+        ref2, _ = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S, memory=mem_ref)
+        assert_close(y2.reshape(ref2.shape), ref2, *TOL[dt], what="tp2 second forward")
+    blk.close()
