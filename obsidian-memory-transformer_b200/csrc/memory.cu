@@ -181,7 +181,15 @@ void MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, c
     if (comm && comm->nranks > 1)  // every rank adds its heads' share of the head mean
       comm_allreduce(comm, wslot.ptr, wslot.ptr, Ms, LTM_DTYPE_F32, false, st);
   }
-  launch_bank_update(memory, colsum.as<float>(), 1.0f / static_cast<float>(T),
+  float state_scale = 1.0f / static_cast<float>(T);
+  if (comm && comm->nranks > 1) {
+    // Every rank accumulated the same column sums (replicated gate), in its
+    // own atomic order; their mean makes the state, and so the bank, identical
+    // on all ranks.
+    comm_allreduce(comm, colsum.ptr, colsum.ptr, H, LTM_DTYPE_F32, false, st);
+    state_scale /= static_cast<float>(comm->nranks);
+  }
+  launch_bank_update(memory, colsum.as<float>(), state_scale,
                      use_scores ? wslot.as<float>() : nullptr, rate, Ms, H, dt, st);
 }
 
