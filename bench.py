@@ -48,7 +48,11 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
-    ap.add_argument("--layers", type=int, default=WL["layers"], help=argparse.SUPPRESS)
+    ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--config", choices=["prefill", "tp"], default="prefill",
+                    help="prefill: the 12-layer W8A8 prefill (default; N>1 = data-parallel "
+                         "replicas); tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel "
+                         "over the N GPUs")
     ap.add_argument("--ncu-case", action="store_true",
                     help="launch each kernel of one block once at the workload's shapes (for ncu)")
     return ap.parse_args()
@@ -164,6 +168,64 @@ def step_work(layers: int) -> dict:
             "attn_tc_kernel": {"amount": attn * layers, "unit": "flop"},
             "ln_x2_kernel": {"amount": ln * layers, "unit": "byte"},
             "rowwise_int8_kernel": {"amount": quant * layers, "unit": "byte"}}
+
+
+# Tensor-parallel prefill: hidden 8192, 64 heads (head_dim 128), FFN 28672,
+# 8192 memory slots, batch 16 x seq 4096, 8 layers, W8A8 + bf16 activations.
+TP_WL = dict(layers=8, B=16, S=4096, H=8192, nh=64, F=28672, Ms=8192)
+TP_WORKLOAD_NAME = ("8-layer Titan prefill, tensor-parallel, W8A8 INT8 linears + bf16 activations, "
+                    "hidden 8192, 64 heads (head_dim 128), FFN 28672, 8192 memory slots, "
+                    "batch 16, seq 4096")
+
+
+def step_work_tp(layers: int, tp: int) -> dict:
+    """Algorithmic ops of one tensor-parallel step on one rank (its head /
+    FFN shards; the gate projection is replicated)."""
+    B, S, H, F, Ms, nh = (TP_WL[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
+    T, dh, Hl, Fl, nhl = B * S, H // nh, H // tp, F // tp, nh // tp
+    gemm = 2.0 * (T * 4 * Hl * H + Ms * 2 * Hl * H + 2 * T * H * Hl + T * H * H + T * Fl * H
+                  + T * H * Fl)
+    attn = 4.0 * B * nhl * dh * (S * (S + 1) / 2 + S * Ms)
+    return {"w8a8_tc_kernel": {"amount": gemm * layers, "unit": "flop"},
+            "attn_tc_kernel": {"amount": attn * layers, "unit": "flop"}}
+
+
+def roofline_of(result: dict, work: dict, torch) -> tuple:
+    """Roofline entry of the dominant kernel class of one timed step (kernel
+    timer result) and the measured int8 peak."""
+    pk, pk_src = peaks()
+    i8 = int8_peak(torch)
+    by_kind = {}
+    for name, (n, ms) in result.items():
+        kind = name.split("/")[0]
+        k = by_kind.setdefault(kind, dict(ms=0.0, launches=0))
+        k["ms"] += ms
+        k["launches"] += n
+    dom = max((k for k in by_kind if k in work), key=lambda k: by_kind[k]["ms"])
+    d = by_kind[dom]
+    avg_ms = d["ms"] / d["launches"]
+    per_launch = work[dom]["amount"] / d["launches"]
+    if work[dom]["unit"] == "flop":
+        achieved = per_launch / (avg_ms * 1e-3) / 1e12
+        if dom.startswith("w8a8"):
+            peak = i8 if i8 else 2.0 * pk["bf16_tflops"]
+            peak_src = ("int8 cuBLASLt (torch._int_mm 8192^3) measured in this run" if i8 else
+                        "2 x bf16_tflops " + pk_src + " (derived int8)")
+        else:
+            peak = pk["bf16_tflops"]
+            peak_src = "bf16_tflops " + pk_src
+        unit, bound = "TFLOP/s", "tensor"
+    else:
+        achieved = per_launch / (avg_ms * 1e-3) / 1e9
+        peak = pk["hbm_gbs"]
+        peak_src = "hbm_gbs " + pk_src
+        unit, bound = "GB/s", "hbm"
+    roof = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2),
+            "peak": round(peak, 2), "unit": unit, "frac": round(achieved / peak, 4),
+            "traffic": traffic_from_profiles(dom), "peak_source": peak_src,
+            "launches_per_step": d["launches"], "avg_launch_ms": round(avg_ms, 5),
+            "algorithmic_per_launch": per_launch, "algorithmic_unit": work[dom]["unit"]}
+    return roof, i8
 
 
 def probe_kernels(torch, ltm, reps: int = 10, timed: bool = True):
@@ -311,6 +373,141 @@ def cpu_baseline(threads_hint=None):
                       f"{dt:.1f} s; tokens/s scaled to {WL['layers']} layers"}
 
 
+def run_tp(args):
+    """The tensor-parallel prefill: one block per rank (its head / FFN shard of
+    one random-init block, built from the same seeded full weights on every
+    rank) applied at each of the layers; the input hidden states are the full
+    [B,S,H] on every rank.  Strong scaling: the job is fixed, N GPUs share it."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import ltm_b200 as ltm
+    from ltm_b200 import synthetic
+    ws, rank, local = dist_env()
+    assert ws == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {ws}"
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    L = args.layers or TP_WL["layers"]
+    B, S, H, F, Ms, nh = (TP_WL[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
+    comm = (ltm.Comm.from_process_group(local) if ws > 1 else
+            ltm.Comm(ltm.comm_unique_id(), 1, 0, local))
+    cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
+                               memory_slots=Ms)
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W8A8, act_dtype=ltm.DTYPE_BF16)
+    blk = ltm.TitanBlock(cfg, q, comm=comm)
+    w = synthetic.block_weights(H, F, Ms, 1000)
+    blk.load_weights(w)
+    del w
+    gen = torch.Generator(device=dev).manual_seed(7)
+    x = (torch.randn((B, S, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    bufs = (torch.empty_like(x), torch.empty_like(x))
+    stream = torch.cuda.current_stream()
+
+    def forward_all(inp):
+        a = inp
+        for i in range(L):
+            o = bufs[i % 2]
+            blk.forward(a, out=o)
+            a = o
+        return a
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    args.warmup = max(args.warmup, 3)
+    for _ in range(args.warmup):
+        forward_all(x)
+    torch.cuda.synchronize()
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(cvd.split(",")[local] if cvd else local)
+    launches0 = ltm.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    evs = []
+    for _ in range(args.steps):
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record(stream)
+        forward_all(x)
+        e_.record(stream)
+        evs.append((s_, e_))
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    launches = ltm.launch_count() - launches0
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    value = B * S * args.steps / (total_ms * 1e-3)
+
+    # end to end: pinned H2D of the input hidden states, the layers, D2H of
+    # each sequence's last hidden state
+    x_host = x.cpu().pin_memory()
+    last_host = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+    barrier()
+    e2e_evs = []
+    for _ in range(args.steps):
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record(stream)
+        x.copy_(x_host, non_blocking=True)
+        y = forward_all(x)
+        last_host.copy_(y[:, -1, :], non_blocking=True)
+        e_.record(stream)
+        e2e_evs.append((s_, e_))
+    torch.cuda.synchronize()
+    barrier()
+    e2e_t = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_evs)], dtype=torch.float64,
+                         device=dev)
+    if ws > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = B * S * args.steps / (float(e2e_t.item()) * 1e-3)
+
+    torch.cuda.synchronize()
+    with ltm.KernelTimer() as kt:
+        forward_all(x)
+    kernels = {name: {"launches": n, "ms": round(ms, 4), "ms_per_launch": round(ms / n, 5)}
+               for name, (n, ms) in kt.result.items()}
+    comm_ms = sum(ms for name, (n, ms) in kt.result.items() if name.startswith("nccl"))
+    all_ms = sum(ms for name, (n, ms) in kt.result.items())
+    roofline = None
+    if rank == 0 and not args.no_probe:
+        roofline, i8 = roofline_of(kt.result, step_work_tp(L, ws), torch)
+        if i8:
+            kernels["int8_peak_tops_measured"] = round(i8, 1)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (hidden states N(0,0.02^2), weights N(0,0.02), random init)",
+            "config": {"workload": TP_WORKLOAD_NAME, "layers": L, "global_batch": B,
+                       "seq_len": S, "act_dtype": "bf16", "parallelism": f"tp{ws}",
+                       "tokens_per_s_per_gpu": round(value / ws, 1),
+                       "comm_fraction_of_rank0_step": round(comm_ms / all_ms, 4) if all_ms else None,
+                       "weights": "one random-init block's shard applied at every layer",
+                       "l2": "inputs (1 GiB per activation tensor) larger than L2"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(x_host.numel() * 2),
+                    "d2h_bytes_per_step": int(last_host.numel() * 2)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "roofline": roofline,
+            "cpu_baseline": None,
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    blk.close()
+    comm.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -399,43 +596,10 @@ def run_ours(args):
     kernels = {name: {"launches": n, "ms": round(ms, 4), "ms_per_launch": round(ms / n, 5)}
                for name, (n, ms) in kt.result.items()}
     roofline = None
-    pk, pk_src = peaks()
     if rank == 0 and not args.no_probe:
-        i8 = int8_peak(torch)
+        roofline, i8 = roofline_of(kt.result, step_work(args.layers), torch)
         if i8:
             kernels["int8_peak_tops_measured"] = round(i8, 1)
-        work = step_work(args.layers)
-        by_kind = {}
-        for name, (n, ms) in kt.result.items():
-            kind = name.split("/")[0]
-            k = by_kind.setdefault(kind, dict(ms=0.0, launches=0))
-            k["ms"] += ms
-            k["launches"] += n
-        dom = max((k for k in by_kind if k in work), key=lambda k: by_kind[k]["ms"])
-        d = by_kind[dom]
-        avg_ms = d["ms"] / d["launches"]
-        per_launch = work[dom]["amount"] / d["launches"]
-        if work[dom]["unit"] == "flop":
-            achieved = per_launch / (avg_ms * 1e-3) / 1e12
-            if dom.startswith("w8a8"):
-                peak = i8 if i8 else 2.0 * pk["bf16_tflops"]
-                peak_src = ("int8 cuBLASLt (torch._int_mm 8192^3) measured in this run" if i8 else
-                            "2 x bf16_tflops " + pk_src + " (derived int8)")
-            else:
-                peak = pk["bf16_tflops"]
-                peak_src = "bf16_tflops " + pk_src
-            unit, bound = "TFLOP/s", "tensor"
-        else:
-            achieved = per_launch / (avg_ms * 1e-3) / 1e9
-            peak = pk["hbm_gbs"]
-            peak_src = "hbm_gbs " + pk_src
-            unit, bound = "GB/s", "hbm"
-        roofline = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2),
-                    "peak": round(peak, 2), "unit": unit, "frac": round(achieved / peak, 4),
-                    "traffic": traffic_from_profiles(dom), "peak_source": peak_src,
-                    "launches_per_step": d["launches"], "avg_launch_ms": round(avg_ms, 5),
-                    "algorithmic_per_launch": per_launch,
-                    "algorithmic_unit": work[dom]["unit"]}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -509,6 +673,9 @@ def run_reference(args):
 
 def main():
     args = parse()
+    # NCCL's own log (e.g. its version line) goes to stderr: stdout carries
+    # exactly one JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.ncu_case:
         import torch
         import ltm_b200 as ltm
@@ -517,7 +684,11 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "tp":
+        run_tp(args)
     else:
+        if args.layers is None:
+            args.layers = WL["layers"]
         run_ours(args)
 
 

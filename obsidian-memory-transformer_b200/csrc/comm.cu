@@ -79,6 +79,7 @@ void comm_allreduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm
   nccl_check(nccl().all_reduce(send, recv, count, nccl_type(dt), max_op ? ncclMax : ncclSum,
                                static_cast<ncclComm_t>(c->handle), st),
              "ncclAllReduce");
+  note_launch(max_op ? "nccl_allreduce/max" : "nccl_allreduce/sum", st);  // timer entry of its own
 }
 
 }  // namespace ltm_b200

@@ -517,12 +517,13 @@ class TitanBlock:
         _check(lib().ltm_block_load_weights(self._h, C.byref(st)))
         del keep
 
-    def forward(self, x, attention_mask=None, stream=None):
-        """x: CUDA tensor [B,S,H] in the act dtype -> y of the same shape."""
+    def forward(self, x, attention_mask=None, stream=None, out=None):
+        """x: CUDA tensor [B,S,H] in the act dtype -> y of the same shape
+        (written into `out` when given; it must not alias x)."""
         torch = _torch()
-        _need_cuda(x)
+        _need_cuda(x, out)
         B, S, H = x.shape
-        y = torch.empty_like(x)
+        y = torch.empty_like(x) if out is None else out
         _check(lib().ltm_block_forward(self._h, _ptr(x), _ptr(y), _ptr(attention_mask), B, S,
                                        _stream(stream)))
         return y
