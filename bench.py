@@ -500,7 +500,7 @@ def run_tp(args):
             "cpu_baseline": None,
             "kernels": kernels,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     blk.close()
     comm.close()
     if ws > 1:
@@ -624,7 +624,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "kernels": kernels,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -668,19 +668,30 @@ def run_reference(args):
         "note": "the reference's CUDA sources do not compile; this arm times the CPU "
                 "restatement of its algorithm (oracle/) on all host cores",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_FD = 1
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the process's original stdout."""
+    os.write(_JSON_FD, (json.dumps(line) + "\n").encode())
 
 
 def main():
+    global _JSON_FD
     args = parse()
-    # NCCL's own log (e.g. its version line) goes to stderr: stdout carries
-    # exactly one JSON line
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    # stdout carries exactly one JSON line: everything else written to file
+    # descriptor 1 (libraries' banners, e.g. NCCL's version line) goes to stderr
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.ncu_case:
         import torch
         import ltm_b200 as ltm
         probe_kernels(torch, ltm, timed=False)
-        print(json.dumps({"ncu_case": "done", "device_error": ltm.device_error()}))
+        emit({"ncu_case": "done", "device_error": ltm.device_error()})
         return
     if args.impl == "reference":
         run_reference(args)

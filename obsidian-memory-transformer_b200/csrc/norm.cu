@@ -169,7 +169,44 @@ __device__ __forceinline__ float warp_max_f(float v) {
 // vectors l, l+32, ... (NV of them).  Same arithmetic as ln_x2_kernel; all
 // reductions are warp shuffles.  Persistent grid (8 warps per CTA, grid-stride
 // over rows) with the next row prefetched.  SAME: residual == x.
-template <class T, int NV, bool SAME>
+// Row reductions of ln_x2_warp_kernel: a warp-shuffle tree, then (WPR = 8:
+// the CTA's eight warps share the row) the eight warp results in order
+// through a double-buffered shared array, one barrier per reduction.
+template <int WPR>
+struct RowReduce {
+  float* red;  // [2][WPR]
+  int par = 0;
+  __device__ __forceinline__ float sum(float v) {
+    v = warp_sum_f(v);
+    if constexpr (WPR == 1) {
+      return v;
+    } else {
+      if ((threadIdx.x & 31) == 0) red[par * WPR + (threadIdx.x >> 5)] = v;
+      __syncthreads();
+      float t = 0.0f;
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) t += red[par * WPR + w];
+      par ^= 1;
+      return t;
+    }
+  }
+  __device__ __forceinline__ float max(float v) {
+    v = warp_max_f(v);
+    if constexpr (WPR == 1) {
+      return v;
+    } else {
+      if ((threadIdx.x & 31) == 0) red[par * WPR + (threadIdx.x >> 5)] = v;
+      __syncthreads();
+      float t = 0.0f;
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) t = fmaxf(t, red[par * WPR + w]);
+      par ^= 1;
+      return t;
+    }
+  }
+};
+
+template <class T, int NV, bool SAME, int WPR = 1>
 __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x,
                                                          const T* __restrict__ res, int64_t rows,
                                                          int H, const float* __restrict__ gamma,
@@ -179,9 +216,15 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
                                                          int8_t* __restrict__ xq,
                                                          float* __restrict__ xs, int do_norm) {
   constexpr int V = 16 / sizeof(T);
-  const int lane = threadIdx.x & 31;
-  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  const int64_t gstride = static_cast<int64_t>(gridDim.x) * 8;
+  constexpr int GROUPS = 8 / WPR;    // row groups per 256-thread CTA
+  constexpr int STRIDE = 32 * WPR;   // vectors between a lane's consecutive vectors
+  static_assert(WPR == 1 || WPR == 8, "one warp or the whole CTA per row");
+  __shared__ float red_s[2 * WPR];
+  RowReduce<WPR> rr_{red_s};
+  // lane: this thread's index within its row group
+  const int lane = (WPR == 1) ? static_cast<int>(threadIdx.x & 31) : static_cast<int>(threadIdx.x);
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * GROUPS + (WPR == 1 ? (threadIdx.x >> 5) : 0);
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * GROUPS;
   const int nvec = H / V;
   // persistent: the next row's loads are in flight while this row is processed
   constexpr int NR = SAME ? 1 : NV;
@@ -189,7 +232,7 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
   auto load = [&](int64_t rr, uint4 (&ax)[NV], uint4 (&ar)[NR]) {
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int vi = lane + 32 * j;
+      const int vi = lane + STRIDE * j;
       ax[j] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(x + rr * H) + vi) : make_uint4(0, 0, 0, 0);
       if constexpr (!SAME)
         ar[j] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(res + rr * H) + vi)
@@ -222,12 +265,12 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
     for (int j = 0; j < NV; ++j)
 #pragma unroll
       for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[j][i]));
-    am = warp_max_f(am);
+    am = rr_.max(am);
     const float s = __fdiv_rn(am, 127.0f);
     const float inv = recip_or_zero(s);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int vi = lane + 32 * j;
+      const int vi = lane + STRIDE * j;
       store_q_warp<V>(xq + row * H + vi * V, xv[j], s, inv, vi < nvec);
     }
     if (lane == 0) xs[row] = s;
@@ -238,11 +281,11 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
     for (int j = 0; j < NV; ++j)
 #pragma unroll
       for (int i = 0; i < V; ++i) sum += lnin(j, i);
-    const float mean = warp_sum_f(sum) / static_cast<float>(H);
+    const float mean = rr_.sum(sum) / static_cast<float>(H);
     float sq = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      if (lane + 32 * j < nvec) {
+      if (lane + STRIDE * j < nvec) {
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           const float d = lnin(j, i) - mean;
@@ -250,11 +293,11 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
         }
       }
     }
-    const float var = warp_sum_f(sq) / static_cast<float>(H);
+    const float var = rr_.sum(sq) / static_cast<float>(H);
     const float rstd = rsqrtf(var + 1e-5f);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int vi = lane + 32 * j;
+      const int vi = lane + STRIDE * j;
       const int c0 = vi < nvec ? vi * V : 0;
       float gv[V], bv[V];
 #pragma unroll
@@ -276,7 +319,7 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
   if (y) {
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int vi = lane + 32 * j;
+      const int vi = lane + STRIDE * j;
       if (vi < nvec) {
         uint4 raw;
         T* e = reinterpret_cast<T*>(&raw);
@@ -289,7 +332,7 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
   if (yq) {
 #pragma unroll
     for (int j = 0; j < NV; ++j)
-      if (lane + 32 * j >= nvec)
+      if (lane + STRIDE * j >= nvec)
 #pragma unroll
         for (int i = 0; i < V; ++i) xv[j][i] = 0.0f;
     float am = 0.0f;
@@ -297,12 +340,12 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
     for (int j = 0; j < NV; ++j)
 #pragma unroll
       for (int i = 0; i < V; ++i) am = fmaxf(am, fabsf(xv[j][i]));
-    am = warp_max_f(am);
+    am = rr_.max(am);
     const float s = __fdiv_rn(am, 127.0f);
     const float inv = recip_or_zero(s);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int vi = lane + 32 * j;
+      const int vi = lane + STRIDE * j;
       store_q_warp<V>(yq + row * H + vi * V, xv[j], s, inv, vi < nvec);
     }
     if (lane == 0) ys[row] = s;
@@ -342,8 +385,8 @@ void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float*
   if (rows == 0) return;
   const int V = static_cast<int>(16 / dtype_size(dt));
   LTM_REQUIRE(H % V == 0, "hidden size must be a multiple of 16 bytes");
-  const int threads = ((H / V + 31) / 32) * 32;
-  LTM_REQUIRE(threads <= 1024, "hidden size too large for the row-resident LayerNorm");
+  const int threads = ((H / V + 31) / 32) * 32;  // fallback: one thread per vector
+  LTM_REQUIRE(H / V <= 2048, "hidden size too large for the row-resident LayerNorm");
   LTM_REQUIRE(!do_norm || ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0,
               "LayerNorm gamma / beta must be 16-byte aligned");
   const int nv = (H / V + 31) / 32;  // 16-byte vectors per lane, warp-per-row layout
@@ -352,28 +395,44 @@ void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float*
     const T* xt = static_cast<const T*>(x);
     const T* rt = static_cast<const T*>(residual ? residual : x);
     const int64_t want_blocks = (rows + 7) / 8;
-    auto warp_launch = [&](auto nv_c) {
+    auto warp_launch = [&](auto nv_c, auto wpr_c) {
       constexpr int NV = decltype(nv_c)::value;
+      constexpr int WPR = decltype(wpr_c)::value;
+      const int64_t want = WPR == 1 ? want_blocks : rows;
       if (rt == xt) {
-        auto kern = ln_x2_warp_kernel<T, NV, true>;
-        kern<<<persistent_grid(kern, 256, 0, want_blocks), 256, 0, stream>>>(
+        auto kern = ln_x2_warp_kernel<T, NV, true, WPR>;
+        kern<<<persistent_grid(kern, 256, 0, want), 256, 0, stream>>>(
             xt, rt, rows, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
       } else {
-        auto kern = ln_x2_warp_kernel<T, NV, false>;
-        kern<<<persistent_grid(kern, 256, 0, want_blocks), 256, 0, stream>>>(
+        auto kern = ln_x2_warp_kernel<T, NV, false, WPR>;
+        kern<<<persistent_grid(kern, 256, 0, want), 256, 0, stream>>>(
             xt, rt, rows, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
       }
     };
-    switch (nv) {
-      case 1: warp_launch(std::integral_constant<int, 1>{}); break;
-      case 2: warp_launch(std::integral_constant<int, 2>{}); break;
-      case 3: warp_launch(std::integral_constant<int, 3>{}); break;
-      case 4: warp_launch(std::integral_constant<int, 4>{}); break;
-      case 5: case 6: warp_launch(std::integral_constant<int, 6>{}); break;
-      case 7: case 8: warp_launch(std::integral_constant<int, 8>{}); break;
-      default:
-        ln_x2_kernel<T, 32><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
-            xt, rt, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
+    using W1 = std::integral_constant<int, 1>;
+    using W8 = std::integral_constant<int, 8>;
+    const int nv8 = (H / V + 255) / 256;  // 16-byte vectors per thread, CTA-per-row layout
+    if (nv <= 8) {
+      switch (nv) {
+        case 1: warp_launch(std::integral_constant<int, 1>{}, W1{}); break;
+        case 2: warp_launch(std::integral_constant<int, 2>{}, W1{}); break;
+        case 3: warp_launch(std::integral_constant<int, 3>{}, W1{}); break;
+        case 4: warp_launch(std::integral_constant<int, 4>{}, W1{}); break;
+        case 5: case 6: warp_launch(std::integral_constant<int, 6>{}, W1{}); break;
+        default: warp_launch(std::integral_constant<int, 8>{}, W1{}); break;
+      }
+    } else if (nv8 <= 8) {  // a 256-thread CTA per row (hidden up to 2048 vectors)
+      switch (nv8) {
+        case 2: warp_launch(std::integral_constant<int, 2>{}, W8{}); break;
+        case 3: warp_launch(std::integral_constant<int, 3>{}, W8{}); break;
+        case 4: warp_launch(std::integral_constant<int, 4>{}, W8{}); break;
+        case 5: case 6: warp_launch(std::integral_constant<int, 6>{}, W8{}); break;
+        default: warp_launch(std::integral_constant<int, 8>{}, W8{}); break;
+      }
+    } else {
+      LTM_REQUIRE(threads <= 1024, "hidden size too large for the row-resident LayerNorm");
+      ln_x2_kernel<T, 32><<<static_cast<unsigned>(rows), threads, 0, stream>>>(
+          xt, rt, H, gamma, beta, static_cast<T*>(y), yq, ys, xq, xs, do_norm ? 1 : 0);
     }
   });
   check_launch("ln_x2_kernel", stream);

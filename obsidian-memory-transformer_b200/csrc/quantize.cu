@@ -293,7 +293,7 @@ namespace {
 // the ranks combine them with an allreduce-max, and rowwise_int8_amax_kernel
 // quantizes the local columns with s = global max / 127 -- the codes and
 // scales the unsplit row would get.  One warp per row.
-template <class T>
+template <class T, bool VEC>
 __global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x, int64_t rows,
                                                          int64_t K, float* __restrict__ amax) {
   const int lane = threadIdx.x & 31;
@@ -301,12 +301,23 @@ __global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x
   if (row >= rows) return;
   const T* xr = x + row * K;
   float m = 0.0f;
-  for (int64_t j = lane; j < K; j += 32) m = fmaxf(m, fabsf(to_f32(xr[j])));
+  if constexpr (VEC) {
+    constexpr int V = Vec16<T>::N;
+    const uint4* xv = reinterpret_cast<const uint4*>(xr);
+    for (int64_t j = lane; j < K / V; j += 32) {
+      const uint4 raw = __ldg(xv + j);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < V; ++i) m = fmaxf(m, fabsf(to_f32(e[i])));
+    }
+  } else {
+    for (int64_t j = lane; j < K; j += 32) m = fmaxf(m, fabsf(to_f32(xr[j])));
+  }
   m = warp_max(m);
   if (lane == 0) amax[row] = m;
 }
 
-template <class T>
+template <class T, bool VEC>
 __global__ void __launch_bounds__(256) rowwise_int8_amax_kernel(const T* __restrict__ x,
                                                                 int64_t rows, int64_t K,
                                                                 const float* __restrict__ amax,
@@ -319,7 +330,23 @@ __global__ void __launch_bounds__(256) rowwise_int8_amax_kernel(const T* __restr
   int8_t* qr = q + row * K;
   const float s = __fdiv_rn(amax[row], 127.0f);
   const float inv = recip_or_zero(s);
-  for (int64_t j = lane; j < K; j += 32) qr[j] = quant_i8_exact(to_f32(xr[j]), s, inv);
+  if constexpr (VEC) {
+    constexpr int V = Vec16<T>::N;
+    const uint4* xv = reinterpret_cast<const uint4*>(xr);
+    for (int64_t j = lane; j < K / V; j += 32) {
+      const uint4 raw = __ldg(xv + j);
+      const T* e = reinterpret_cast<const T*>(&raw);
+      int8_t out[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) out[i] = quant_i8_exact(to_f32(e[i]), s, inv);
+      if constexpr (V == 8)
+        *reinterpret_cast<uint2*>(qr + j * V) = *reinterpret_cast<const uint2*>(out);
+      else
+        *reinterpret_cast<uint32_t*>(qr + j * V) = *reinterpret_cast<const uint32_t*>(out);
+    }
+  } else {
+    for (int64_t j = lane; j < K; j += 32) qr[j] = quant_i8_exact(to_f32(xr[j]), s, inv);
+  }
   if (lane == 0) scales[row] = s;
 }
 
@@ -331,7 +358,11 @@ void launch_row_absmax(const void* x, ltm_dtype dt, int64_t rows, int64_t K, flo
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
-    row_absmax_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, amax);
+    const bool vec = (K * sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (vec)
+      row_absmax_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, amax);
+    else
+      row_absmax_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, amax);
   });
   check_launch("row_absmax_kernel", stream);
 }
@@ -342,8 +373,14 @@ void launch_rowwise_int8_amax(const void* x, ltm_dtype dt, int64_t rows, int64_t
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
-    rowwise_int8_amax_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows, K,
-                                                            amax, q, s);
+    const bool vec = (K * sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(q) & 7) == 0;
+    if (vec)
+      rowwise_int8_amax_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x), rows,
+                                                                    K, amax, q, s);
+    else
+      rowwise_int8_amax_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(x),
+                                                                     rows, K, amax, q, s);
   });
   check_launch("rowwise_int8_amax_kernel", stream);
 }

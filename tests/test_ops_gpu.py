@@ -11,7 +11,7 @@ TOL = {"f32": (1e-4, 1e-4), "f16": (2e-2, 1e-2), "bf16": (2e-2, 1e-2)}
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
-@pytest.mark.parametrize("H", [64, 768, 4096])
+@pytest.mark.parametrize("H", [64, 768, 4096, 8192])  # 4096 / 8192: a CTA per row
 def test_layernorm_x2(ltm, orc, dt, H):
     import torch
     rng = np.random.default_rng(H)

@@ -8,7 +8,10 @@ from _util import DT_NAMES, as_f32, orc_dtype, to_device
 
 pytestmark = pytest.mark.gpu
 
-INT8_SHAPES = [(1, 16), (3, 8), (37, 100), (64, 768), (300, 3072), (5, 28672), (2, 1)]
+# widths cover the warp-per-row (<= 128 vectors), 4-warp (<= 1024 vectors) and
+# streaming row quantizers
+INT8_SHAPES = [(1, 16), (3, 8), (37, 100), (64, 768), (300, 3072), (64, 4096), (33, 8192),
+               (5, 28672), (2, 1)]
 
 
 def _weights(shape, seed, special=True):
