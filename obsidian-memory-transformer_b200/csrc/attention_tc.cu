@@ -3,21 +3,25 @@
 //
 //   o[t, h*D:(h+1)*D] = softmax_j( q_t . k_j / sqrt(D) ) v_j
 //
-// One CTA owns 128 queries of one (batch, head) and walks 128-key tiles:
+// One CTA owns 128 queries of one (batch, head) and walks 64-key tiles:
 //   warp 0     TMA: the Q tile once, K tiles into a 2-stage ring
-//   warp 2     TMA: V tiles (single buffer, reloaded once P.V has consumed it)
-//   warp 1     TMEM allocator + MMA issuer:
-//                S  = Q K^T      kind::f16, M=128 N=128 K=D, Q and K K-major
-//                PV = P V        kind::f16, M=128 N=D K=128, P K-major (smem),
-//                                V MN-major (the [keys x D] tile as loaded)
-//   warps 4-7  softmax (thread = query row = TMEM lane): two passes over its S
-//              row in TMEM (raw row max, then p = 2^(s*scale - max*scale) on
-//              FFMA + MUFU.EX2 and the row sum), P written as
-//              16-bit into the 128-byte-swizzled K-major smem tile, the
-//              previous tile's PV folded into the register accumulator O with
-//              the online-softmax correction; O / l stored at the end.
-// TMEM: S at columns [0,128), PV at [128, 128+D) (256 columns allocated), so
-// two CTAs share an SM for D = 64.  Every mbarrier wait is bounded.
+//   warp 2     TMA: V tiles into a 2-stage ring
+//   warp 1     TMEM allocator + MMA issuer, in the order S(0), S(1), PV(0),
+//              S(2), PV(1), ... so that the tensor core computes the scores of
+//              tile j+1 while tile j is in the softmax:
+//                S[j%2] = Q K^T  kind::f16, M=128 N=64 K=D (Q, K K-major)
+//                O     += P V    kind::f16, M=128 N=D K=64 (P K-major in
+//                                smem, V MN-major as loaded)
+//   warps 4-7  softmax (thread = query row = TMEM lane): one TMEM read of its
+//              S row into registers (the S buffer is released right after),
+//              the row max, p = 2^(s*scale - m_ref*scale) on FFMA + MUFU.EX2
+//              and the row sum, P written as 16-bit into the 128-byte-swizzled
+//              K-major smem tile.  O accumulates in TMEM across tiles; m_ref is
+//              the row's reference max, raised -- with O and the sum rescaled in
+//              place -- only when the running max exceeds it by more than 2^8
+//              (so p <= 256; the final O / l is the same for any reference).
+// TMEM: S0 [0,64), S1 [64,128), O [128, 128+D) of 256 columns, so two CTAs
+// share an SM.  Every mbarrier wait is bounded.
 //
 // Replaces chunkAttentionKernel (src/core/attention/flash_attention.cu:188-268,
 // scale 1/sqrt(head_dim) :241) and the memory-attention score / softmax / PV
@@ -31,28 +35,33 @@ namespace ltm_b200 {
 namespace {
 
 constexpr int kQM = 128;   // queries per CTA
-constexpr int kKN = 128;   // keys per tile
-constexpr uint32_t kChunk = 128 * 128;  // one [128 rows x 128 bytes] swizzled chunk
+constexpr int kKN = 64;    // keys per tile
+constexpr uint32_t kChunk = 128 * 128;   // one [128 rows x 128 bytes] swizzled chunk (Q, P)
+constexpr uint32_t kKChunk = kKN * 128;  // one [64 rows x 128 bytes] swizzled chunk (K, V)
+constexpr float kRescaleLog2 = 8.0f;    // lazy-rescale threshold (log2 units)
 
 template <int D>
 struct AttnSmem {
   static constexpr int DC = D / 64;                 // 128-byte chunks per row
+  // V tiles in flight: two for D = 64; one for D = 128, which keeps the CTA
+  // under half of the SM's shared memory so that two CTAs share an SM
+  static constexpr int VST = D <= 64 ? 2 : 1;
   static constexpr uint32_t kQ = DC * kChunk;
-  static constexpr uint32_t kK = DC * kChunk;
-  static constexpr uint32_t kV = DC * kChunk;
-  static constexpr uint32_t kP = 2 * kChunk;        // 128 x 128 16-bit
+  static constexpr uint32_t kK = DC * kKChunk;
+  static constexpr uint32_t kV = DC * kKChunk;
+  static constexpr uint32_t kP = kChunk;            // 128 queries x 64 keys, 16-bit
   static constexpr uint32_t kOffK = kQ;
   static constexpr uint32_t kOffV = kOffK + 2 * kK;
-  static constexpr uint32_t kOffP = kOffV + kV;
+  static constexpr uint32_t kOffP = kOffV + VST * kV;
   static constexpr uint32_t kOffBar = kOffP + kP;
   static constexpr uint32_t kBytes = kOffBar + 256 + 1024;
 };
 
 enum AttnBar : int {
-  kBarQFull = 0, kBarKFull0, kBarKFull1, kBarKEmpty0, kBarKEmpty1, kBarVFull, kBarVEmpty,
-  kBarSFull, kBarSFree, kBarPFull, kBarPVFull, kBarDrain, kNumBars
+  kBarQFull = 0, kBarKFull0, kBarKFull1, kBarKEmpty0, kBarKEmpty1, kBarVFull0, kBarVFull1,
+  kBarVEmpty0, kBarVEmpty1, kBarSFull0, kBarSFull1, kBarSFree0, kBarSFree1, kBarPFull,
+  kBarPVDone, kBarDrain, kNumBars
 };
-
 
 // Two floats rounded to a packed pair of 16-bit values (one paired convert).
 template <class T>
@@ -67,7 +76,7 @@ __device__ __forceinline__ uint32_t pack2_16(float lo, float hi) {
 }
 
 template <class T, int D, bool CAUSAL>
-__global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
+__global__ void __launch_bounds__(256, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, AttnParams p, int* err) {
   using L = AttnSmem<D>;
@@ -94,8 +103,10 @@ __global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
   const int ntiles = kv_end > 0 ? (kv_end + kKN - 1) / kKN : 0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBars; ++i)
-      mbar_init(bar + i, (i == kBarSFree || i == kBarPFull) ? 4 : 1);
+    for (int i = 0; i < kNumBars; ++i) {
+      const bool per_warp = i == kBarSFree0 || i == kBarSFree1 || i == kBarPFull;
+      mbar_init(bar + i, per_warp ? 4 : 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -107,7 +118,7 @@ __global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tS = tmem, tPV = tmem + 128;
+  const uint32_t tO = tmem + 2 * kKN;
 
   if (warp == 0) {
     if (lane == 0 && ntiles > 0) {
@@ -122,7 +133,7 @@ __global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
           break;
         mbar_arrive_expect_tx(bar + kBarKFull0 + s, L::kK);
         for (int c = 0; c < DC; ++c)
-          tma_load_2d(sK + s * L::kK + c * kChunk, &tmK, bar + kBarKFull0 + s, h * D + c * 64,
+          tma_load_2d(sK + s * L::kK + c * kKChunk, &tmK, bar + kBarKFull0 + s, h * D + c * 64,
                       krow0 + j * kKN);
         ++issued;
       }
@@ -137,15 +148,22 @@ __global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
     if (lane == 0 && ntiles > 0) {
       int issued = 0;
       for (int j = 0; j < ntiles; ++j) {
-        if (!mbar_wait_bounded(bar + kBarVEmpty, (j & 1) ^ 1, abort_flag, err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(bar + kBarVFull, L::kV);
+        const int s = j % L::VST;
+        const uint32_t use = static_cast<uint32_t>(j / L::VST);
+        if (!mbar_wait_bounded(bar + kBarVEmpty0 + s, (use & 1) ^ 1, abort_flag, err,
+                               kErrWaitEmpty))
+          break;
+        mbar_arrive_expect_tx(bar + kBarVFull0 + s, L::kV);
         for (int c = 0; c < DC; ++c)
-          tma_load_2d(sV + c * kChunk, &tmV, bar + kBarVFull, h * D + c * 64, krow0 + j * kKN);
+          tma_load_2d(sV + s * L::kV + c * kKChunk, &tmV, bar + kBarVFull0 + s, h * D + c * 64,
+                      krow0 + j * kKN);
         ++issued;
       }
-      if (*abort_flag && issued > 0) {
+      if (*abort_flag) {
         volatile int never = 0;
-        mbar_wait_bounded(bar + kBarVFull, (issued - 1) & 1, &never, err, kErrWaitOther);
+        for (int j = (issued > L::VST ? issued - L::VST : 0); j < issued; ++j)
+          mbar_wait_bounded(bar + kBarVFull0 + (j % L::VST), (j / L::VST) & 1, &never, err,
+                            kErrWaitOther);
       }
     }
   } else if (warp == 1) {
@@ -153,44 +171,49 @@ __global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
       constexpr bool kBF = std::is_same<T, __nv_bfloat16>::value;
       constexpr uint32_t idS = idesc_f16(kQM, kKN, kBF);
       constexpr uint32_t idPV = idesc_f16(kQM, D, kBF, /*b_mn_major=*/true);
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP), aV = smem_u32(sV);
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait_bounded(bar + kBarPFull, i & 1, abort_flag, err, kErrWaitFull)) return false;
-        if (!mbar_wait_bounded(bar + kBarVFull, i & 1, abort_flag, err, kErrWaitFull)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int t = 0; t < kKN / 16; ++t)
-          tc_mma_f16(tPV, make_desc_kmajor_sw128(aP + (t >> 2) * kChunk + (t & 3) * 32),
-                     make_desc_mnmajor_sw128(aV + t * 2048, kChunk), idPV, t != 0);
-        tc_commit(bar + kBarPVFull);
-        tc_commit(bar + kBarVEmpty);
-        return true;
-      };
-      bool ok = mbar_wait_bounded(bar + kBarQFull, 0, abort_flag, err, kErrWaitFull);
-      for (int j = 0; ok && j < ntiles; ++j) {
+      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      // S(j) = Q K(j)^T into S buffer j % 2 (the softmax has released it)
+      auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait_bounded(bar + kBarKFull0 + s, (j >> 1) & 1, abort_flag, err, kErrWaitFull)) {
-          ok = false;
-          break;
-        }
-        if (j > 0 && !mbar_wait_bounded(bar + kBarSFree, (j - 1) & 1, abort_flag, err, kErrWaitOther)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait_bounded(bar + kBarKFull0 + s, (j >> 1) & 1, abort_flag, err, kErrWaitFull))
+          return false;
+        if (j >= 2 && !mbar_wait_bounded(bar + kBarSFree0 + s, ((j - 2) >> 1) & 1, abort_flag, err,
+                                         kErrWaitOther))
+          return false;
         tc_fence_after();
         const uint32_t aK = smem_u32(sK + s * L::kK);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
-          tc_mma_f16(tS, make_desc_kmajor_sw128(aQ + (k >> 2) * kChunk + (k & 3) * 32),
-                     make_desc_kmajor_sw128(aK + (k >> 2) * kChunk + (k & 3) * 32), idS, k != 0);
-        tc_commit(bar + kBarSFull);
+          tc_mma_f16(tmem + s * kKN, make_desc_kmajor_sw128(aQ + (k >> 2) * kChunk + (k & 3) * 32),
+                     make_desc_kmajor_sw128(aK + (k >> 2) * kKChunk + (k & 3) * 32), idS, k != 0);
+        tc_commit(bar + kBarSFull0 + s);
         tc_commit(bar + kBarKEmpty0 + s);
-        if (j > 0 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
-        }
+        return true;
+      };
+      // O (+)= P(i) V(i) once the softmax has written P(i) (and rescaled O)
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % L::VST;
+        if (!mbar_wait_bounded(bar + kBarPFull, i & 1, abort_flag, err, kErrWaitFull)) return false;
+        if (!mbar_wait_bounded(bar + kBarVFull0 + s, (i / L::VST) & 1, abort_flag, err,
+                               kErrWaitFull))
+          return false;
+        tc_fence_after();
+        const uint32_t aV = smem_u32(sV + s * L::kV);
+#pragma unroll
+        for (int t = 0; t < kKN / 16; ++t)
+          tc_mma_f16(tO, make_desc_kmajor_sw128(aP + t * 32),
+                     make_desc_mnmajor_sw128(aV + t * 2048, kKChunk), idPV, (i | t) != 0);
+        tc_commit(bar + kBarPVDone);
+        tc_commit(bar + kBarVEmpty0 + s);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(bar + kBarQFull, 0, abort_flag, err, kErrWaitFull);
+      if (ok) ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        ok = issue_pv(j);
+        if (ok && j + 2 < ntiles) ok = issue_s(j + 2);
       }
-      if (ok) issue_pv(ntiles - 1);
       if (*abort_flag) {
         volatile int never = 0;
         tc_commit(bar + kBarDrain);
@@ -203,123 +226,145 @@ __global__ void __launch_bounds__(256, (D <= 64 ? 2 : 1))
     const int r = q4 * 32 + lane;
     const int qi = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.0f;
-    float m = -INFINITY, l = 0.0f, corr_prev = 0.0f;
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY, l = 0.0f;
+    // waits whose outcome is the same for the whole warp (the TMEM accesses
+    // that follow are warp-collective)
+    auto wait_warp = [&](int bi, uint32_t parity, int code) -> bool {
+      const bool r = mbar_wait_bounded(bar + bi, parity, abort_flag, err, code);
+      return __all_sync(0xffffffffu, r);
+    };
     bool ok = true;  // with no key tile at all the output is written as zeros
     for (int j = 0; ok && j < ntiles; ++j) {
-      if (!mbar_wait_bounded(bar + kBarSFull, j & 1, abort_flag, err, kErrWaitAccum)) {
+      const int sb = j & 1;
+      if (!wait_warp(kBarSFull0 + sb, (j >> 1) & 1, kErrWaitAccum)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      constexpr int NC = kKN / 32;
+      uint32_t sr[NC][32];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_ld_32x32b_x32(tmem + sb * kKN + lane_off + c * 32, sr[c]);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_wait_ld_tie(sr[c]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar + kBarSFree0 + sb);  // S buffer may be overwritten
       const int k0 = j * kKN;
       const bool need_mask = (k0 + kKN > p.Skv) || (CAUSAL && k0 + kKN - 1 > q0 + p.causal_offset);
-      const int kmax = CAUSAL ? min(p.Skv - 1, qi + p.causal_offset) : p.Skv - 1;  // last visible key
-      // pass 1: row max of the raw scores (the positive scale commutes with max)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kKN / 32; ++c) {
-        uint32_t sr[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, sr);
-        tmem_wait_ld();
-        if (!need_mask) {
+      if (need_mask) {
+        const int kmax = CAUSAL ? min(p.Skv - 1, qi + p.causal_offset) : p.Skv - 1;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-        } else {
-          const int kb = k0 + c * 32;
+        for (int c = 0; c < NC; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            mx = fmaxf(mx, kb + i <= kmax ? __uint_as_float(sr[i]) : -INFINITY);
-        }
+            if (k0 + c * 32 + i > kmax) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, mx);  // raw-score units
-      const float msc = (m_new == -INFINITY) ? 0.0f : m_new * p.scale_log2;
-      const float corr = ex2_approx(fmaf(m, p.scale_log2, -msc));  // m = -inf -> 0
-      // fold the previous tile's P.V (relative to the previous max)
-      if (j > 0) {
-        if (!mbar_wait_bounded(bar + kBarPVFull, (j - 1) & 1, abort_flag, err, kErrWaitAccum)) {
+      // row max: eight independent partial maxima (short dependency chains)
+      float pm[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(sr[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      // raise the reference max (and rescale O, l) only past the threshold
+      const bool raise = (m_ref == -INFINITY) ? (mx > -INFINITY)
+                                              : ((mx - m_ref) * sl2 > kRescaleLog2);
+      bool pv_waited = false;
+      if (j > 0 && __any_sync(0xffffffffu, raise)) {
+        const float m_new = fmaxf(m_ref, mx);
+        const float f = (m_ref == -INFINITY) ? 0.0f : ex2_approx((m_ref - m_new) * sl2);
+        if (!wait_warp(kBarPVDone, (j - 1) & 1, kErrWaitAccum)) {
           ok = false;
           break;
         }
+        pv_waited = true;
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t pv[32];
-          tmem_ld_32x32b_x32(tPV + lane_off + c * 32, pv);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr_prev, __uint_as_float(pv[i]));
-        }
-      }
-      // pass 2: P = 2^(s * scale - max * scale) as 16-bit into the swizzled K-major tile
-      float rs = 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < kKN / 32; ++c) {
-        uint32_t sr[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, sr);
-        tmem_wait_ld();
-        float pv[32];
-        if (!need_mask) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pv[i] = ex2_approx(fmaf(__uint_as_float(sr[i]), p.scale_log2, -msc));
-        } else {
-          const int kb = k0 + c * 32;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            pv[i] = kb + i <= kmax ? ex2_approx(fmaf(__uint_as_float(sr[i]), p.scale_log2, -msc)) : 0.0f;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) rs += pv[i];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {  // 4 x 16-byte chunks = 32 keys
-          const int cc = c * 4 + u;      // 16-byte chunk index within the 256-byte row
-          uint4 w;
-          w.x = pack2_16<T>(pv[8 * u + 0], pv[8 * u + 1]);
-          w.y = pack2_16<T>(pv[8 * u + 2], pv[8 * u + 3]);
-          w.z = pack2_16<T>(pv[8 * u + 4], pv[8 * u + 5]);
-          w.w = pack2_16<T>(pv[8 * u + 6], pv[8 * u + 7]);
-          *reinterpret_cast<uint4*>(sP + (cc >> 3) * kChunk + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) = w;
-        }
-      }
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar + kBarSFree);
-        mbar_arrive(bar + kBarPFull);
-      }
-      l = l * corr + rs;
-      m = m_new;
-      corr_prev = corr;
-    }
-    if (ok && ntiles > 0) {
-      ok = mbar_wait_bounded(bar + kBarPVFull, (ntiles - 1) & 1, abort_flag, err, kErrWaitAccum);
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t pv[32];
-          tmem_ld_32x32b_x32(tPV + lane_off + c * 32, pv);
-          tmem_wait_ld();
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(tO + lane_off + c * 32, ov);
+          tmem_wait_ld_tie(ov);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr_prev, __uint_as_float(pv[i]));
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * f);
+          tmem_st_32x32b_x32(tO + lane_off + c * 32, ov);
+        }
+        tmem_wait_st();
+        l *= f;
+        m_ref = m_new;
+      } else if (j == 0) {
+        m_ref = mx;
+      }
+      const float msc = (m_ref == -INFINITY) ? 0.0f : m_ref * sl2;
+      // P = 2^(s*scale - m_ref*scale), the row sum, and P as 16-bit pairs
+      float ps[8];  // eight independent partial row sums
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ps[u] = 0.0f;
+      uint32_t pk[NC * 16];
+#pragma unroll
+      for (int c = 0; c < NC; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float a = ex2_approx(fmaf(__uint_as_float(sr[c][i]), sl2, -msc));
+          const float bb = ex2_approx(fmaf(__uint_as_float(sr[c][i + 1]), sl2, -msc));
+          ps[(i >> 1) & 7] += a + bb;
+          pk[c * 16 + i / 2] = pack2_16<T>(a, bb);
+        }
+      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      // the single P buffer is free once P(j-1).V(j-1) has completed
+      if (j > 0 && !pv_waited && !wait_warp(kBarPVDone, (j - 1) & 1, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int cc = 0; cc < NC * 4; ++cc) {  // 16-byte unit cc of the row's 128 bytes
+        uint4 w;
+        w.x = pk[cc * 4 + 0];
+        w.y = pk[cc * 4 + 1];
+        w.z = pk[cc * 4 + 2];
+        w.w = pk[cc * 4 + 3];
+        *reinterpret_cast<uint4*>(sP + r * 128 + ((cc ^ (r & 7)) << 4)) = w;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar + kBarPFull);
+    }
+    if (ok && ntiles > 0) ok = wait_warp(kBarPVDone, (ntiles - 1) & 1, kErrWaitAccum);
+    const bool aborted = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
+    // The TMEM reads are warp-collective (.sync.aligned): the whole warp takes
+    // this branch (ok, ntiles and the abort flag are the same for its lanes)
+    // and only the global stores depend on the lane's row.
+    if (ok && ntiles > 0 && !aborted) {
+      tc_fence_after();
+      const bool store = qi < p.Sq;
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      T* og = static_cast<T*>(p.o) + (b * p.q_batch_rows + (store ? qi : 0)) * p.ldo + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(tO + lane_off + c * 32, ov);
+        tmem_wait_ld_tie(ov);
+        if (store) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = pack2_16<T>(__uint_as_float(ov[8 * u + 0]) * inv, __uint_as_float(ov[8 * u + 1]) * inv);
+            w.y = pack2_16<T>(__uint_as_float(ov[8 * u + 2]) * inv, __uint_as_float(ov[8 * u + 3]) * inv);
+            w.z = pack2_16<T>(__uint_as_float(ov[8 * u + 4]) * inv, __uint_as_float(ov[8 * u + 5]) * inv);
+            w.w = pack2_16<T>(__uint_as_float(ov[8 * u + 6]) * inv, __uint_as_float(ov[8 * u + 7]) * inv);
+            *reinterpret_cast<uint4*>(og + c * 32 + 8 * u) = w;
+          }
         }
       }
-    }
-    if (ok && qi < p.Sq && !*abort_flag) {
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    } else if (ok && ntiles == 0 && qi < p.Sq) {
       T* og = static_cast<T*>(p.o) + (b * p.q_batch_rows + qi) * p.ldo + h * D;
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint4 w;
-        w.x = pack2_16<T>(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-        w.y = pack2_16<T>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-        w.z = pack2_16<T>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-        w.w = pack2_16<T>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-        *reinterpret_cast<uint4*>(og + 8 * c) = w;
-      }
+      for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(og + 8 * c) = make_uint4(0, 0, 0, 0);
     }
   }
 

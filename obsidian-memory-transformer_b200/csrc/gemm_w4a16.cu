@@ -166,7 +166,10 @@ __global__ void __launch_bounds__(192, 2)
     }
     // ---- epilogue: the pipeline stages are free once the accumulator is
     // complete, so stage 0 doubles as the output staging buffer
-    const bool ok = mbar_wait_bounded(accf, 0, abort_flag, err, kErrWaitAccum) && !*abort_flag;
+    // warp-uniform outcome: the epilogue's TMEM loads are warp-collective
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(accf, 0, abort_flag, err,
+                                                              kErrWaitAccum) &&
+                                                !*abort_flag);
     tc_fence_after();
     if (ok)
       tc_tile_epilogue_passes<MODE, T, kBN, false>(ep, tmem, q, lane, m0, n0, M, N,

@@ -170,7 +170,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = lt & 1;
       const uint32_t use = static_cast<uint32_t>(lt >> 1);
       const int row0 = rows_of(t), nw = cols_of(t);
-      if (!mbar_wait_bounded(accf + b, use & 1, abort_flag, err, kErrWaitAccum)) break;
+      // warp-uniform outcome: the epilogue's TMEM loads are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(accf + b, use & 1, abort_flag, err,
+                                                     kErrWaitAccum)))
+        break;
       tc_fence_after();
       // publish this tile's column vectors, then fetch the next tile's
       epi.run(ep, &tmO, tmem + b * BN + half * (BN / 2) + (static_cast<uint32_t>(q * 32) << 16),
@@ -354,7 +357,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int b = lt % kPairAccBufs;
       const uint32_t use = static_cast<uint32_t>(lt / kPairAccBufs);
       const int row0 = rows_of(t), nw = cols_of(t);
-      if (!mbar_wait_bounded(accf + b, use & 1, abort_flag, err, kErrWaitAccum)) break;
+      // warp-uniform outcome: the epilogue's TMEM loads are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(accf + b, use & 1, abort_flag, err,
+                                                     kErrWaitAccum)))
+        break;
       tc_fence_after();
       epi.run(ep, &tmO, tmem + b * BN + half * (BN / 2) + (static_cast<uint32_t>(q * 32) << 16),
               row0 + lane, row0, nw, M, N, cvec, stg, lane,
