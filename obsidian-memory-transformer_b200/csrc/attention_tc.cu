@@ -6,9 +6,10 @@
 // One CTA owns 128 queries of one (batch, head) and walks 64-key tiles:
 //   warp 0     TMA: the Q tile once, K tiles into a 2-stage ring
 //   warp 2     TMA: V tiles into a 2-stage ring
-//   warp 1     TMEM allocator + MMA issuer, in the order S(0), S(1), PV(0),
-//              S(2), PV(1), ... so that the tensor core computes the scores of
-//              tile j+1 while tile j is in the softmax:
+//   warp 1     TMEM allocator + MMA issuer, in the order S(0), S(1), S(2),
+//              PV(0), S(3), PV(1), ... (S(j+2) as soon as the softmax has read
+//              S(j)) so that the tensor core computes the scores of later tiles
+//              while tile j is in the softmax:
 //                S[j%2] = Q K^T  kind::f16, M=128 N=64 K=D (Q, K K-major)
 //                O     += P V    kind::f16, M=128 N=D K=64 (P K-major in
 //                                smem, V MN-major as loaded)
@@ -46,6 +47,9 @@ struct AttnSmem {
   // V tiles in flight: two for D = 64; one for D = 128, which keeps the CTA
   // under half of the SM's shared memory so that two CTAs share an SM
   static constexpr int VST = D <= 64 ? 2 : 1;
+  // P tiles: two for D = 64 (the softmax writes P(j+1) while P(j).V(j) runs),
+  // one for D = 128 (shared-memory budget of two CTAs per SM)
+  static constexpr int PST = D <= 64 ? 2 : 1;
   static constexpr uint32_t kQ = DC * kChunk;
   static constexpr uint32_t kK = DC * kKChunk;
   static constexpr uint32_t kV = DC * kKChunk;
@@ -53,14 +57,14 @@ struct AttnSmem {
   static constexpr uint32_t kOffK = kQ;
   static constexpr uint32_t kOffV = kOffK + 2 * kK;
   static constexpr uint32_t kOffP = kOffV + VST * kV;
-  static constexpr uint32_t kOffBar = kOffP + kP;
+  static constexpr uint32_t kOffBar = kOffP + PST * kP;
   static constexpr uint32_t kBytes = kOffBar + 256 + 1024;
 };
 
 enum AttnBar : int {
   kBarQFull = 0, kBarKFull0, kBarKFull1, kBarKEmpty0, kBarKEmpty1, kBarVFull0, kBarVFull1,
-  kBarVEmpty0, kBarVEmpty1, kBarSFull0, kBarSFull1, kBarSFree0, kBarSFree1, kBarPFull,
-  kBarPVDone, kBarDrain, kNumBars
+  kBarVEmpty0, kBarVEmpty1, kBarSFull0, kBarSFull1, kBarSFree0, kBarSFree1, kBarPFull0,
+  kBarPFull1, kBarPVDone0, kBarPVDone1, kBarDrain, kNumBars
 };
 
 // Two floats rounded to a packed pair of 16-bit values (one paired convert).
@@ -104,7 +108,8 @@ __global__ void __launch_bounds__(256, 2)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) {
-      const bool per_warp = i == kBarSFree0 || i == kBarSFree1 || i == kBarPFull;
+      const bool per_warp = i == kBarSFree0 || i == kBarSFree1 || i == kBarPFull0 ||
+                            i == kBarPFull1;
       mbar_init(bar + i, per_warp ? 4 : 1);
     }
     *abort_flag = 0;
@@ -193,26 +198,33 @@ __global__ void __launch_bounds__(256, 2)
       // O (+)= P(i) V(i) once the softmax has written P(i) (and rescaled O)
       auto issue_pv = [&](int i) -> bool {
         const int s = i % L::VST;
-        if (!mbar_wait_bounded(bar + kBarPFull, i & 1, abort_flag, err, kErrWaitFull)) return false;
+        const int pb = i % L::PST;
+        if (!mbar_wait_bounded(bar + kBarPFull0 + pb, (i / L::PST) & 1, abort_flag, err,
+                               kErrWaitFull))
+          return false;
         if (!mbar_wait_bounded(bar + kBarVFull0 + s, (i / L::VST) & 1, abort_flag, err,
                                kErrWaitFull))
           return false;
         tc_fence_after();
         const uint32_t aV = smem_u32(sV + s * L::kV);
+        const uint32_t aPb = aP + pb * L::kP;
 #pragma unroll
         for (int t = 0; t < kKN / 16; ++t)
-          tc_mma_f16(tO, make_desc_kmajor_sw128(aP + t * 32),
+          tc_mma_f16(tO, make_desc_kmajor_sw128(aPb + t * 32),
                      make_desc_mnmajor_sw128(aV + t * 2048, kKChunk), idPV, (i | t) != 0);
-        tc_commit(bar + kBarPVDone);
+        tc_commit(bar + kBarPVDone0 + pb);
         tc_commit(bar + kBarVEmpty0 + s);
         return true;
       };
       bool ok = mbar_wait_bounded(bar + kBarQFull, 0, abort_flag, err, kErrWaitFull);
       if (ok) ok = issue_s(0);
       if (ok && ntiles > 1) ok = issue_s(1);
+      // S(j+2) as soon as the softmax has read S(j) (early in its tile), then
+      // P(j).V(j) once it has written P(j): the scores of tile j+2 are computed
+      // during tile j's exponentials
       for (int j = 0; ok && j < ntiles; ++j) {
-        ok = issue_pv(j);
-        if (ok && j + 2 < ntiles) ok = issue_s(j + 2);
+        if (j + 2 < ntiles) ok = issue_s(j + 2);
+        if (ok) ok = issue_pv(j);
       }
       if (*abort_flag) {
         volatile int never = 0;
@@ -278,7 +290,8 @@ __global__ void __launch_bounds__(256, 2)
       if (j > 0 && __any_sync(0xffffffffu, raise)) {
         const float m_new = fmaxf(m_ref, mx);
         const float f = (m_ref == -INFINITY) ? 0.0f : ex2_approx((m_ref - m_new) * sl2);
-        if (!wait_warp(kBarPVDone, (j - 1) & 1, kErrWaitAccum)) {
+        // O is final up to P(j-1).V(j-1)
+        if (!wait_warp(kBarPVDone0 + (j - 1) % L::PST, ((j - 1) / L::PST) & 1, kErrWaitAccum)) {
           ok = false;
           break;
         }
@@ -315,11 +328,14 @@ __global__ void __launch_bounds__(256, 2)
           pk[c * 16 + i / 2] = pack2_16<T>(a, bb);
         }
       l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      // the single P buffer is free once P(j-1).V(j-1) has completed
-      if (j > 0 && !pv_waited && !wait_warp(kBarPVDone, (j - 1) & 1, kErrWaitAccum)) {
+      // P buffer j % PST is free once P(j-PST).V(j-PST) has completed
+      if (j >= L::PST && !pv_waited &&
+          !wait_warp(kBarPVDone0 + j % L::PST, ((j - L::PST) / L::PST) & 1, kErrWaitAccum)) {
         ok = false;
         break;
       }
+#pragma unroll
+      uint8_t* sPb = sP + (j % L::PST) * L::kP;
 #pragma unroll
       for (int cc = 0; cc < NC * 4; ++cc) {  // 16-byte unit cc of the row's 128 bytes
         uint4 w;
@@ -327,14 +343,16 @@ __global__ void __launch_bounds__(256, 2)
         w.y = pk[cc * 4 + 1];
         w.z = pk[cc * 4 + 2];
         w.w = pk[cc * 4 + 3];
-        *reinterpret_cast<uint4*>(sP + r * 128 + ((cc ^ (r & 7)) << 4)) = w;
+        *reinterpret_cast<uint4*>(sPb + r * 128 + ((cc ^ (r & 7)) << 4)) = w;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar + kBarPFull);
+      if (lane == 0) mbar_arrive(bar + kBarPFull0 + j % L::PST);
     }
-    if (ok && ntiles > 0) ok = wait_warp(kBarPVDone, (ntiles - 1) & 1, kErrWaitAccum);
+    if (ok && ntiles > 0)  // the last P.V (and, in order, every earlier one) has completed
+      ok = wait_warp(kBarPVDone0 + (ntiles - 1) % L::PST, ((ntiles - 1) / L::PST) & 1,
+                     kErrWaitAccum);
     const bool aborted = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
     // The TMEM reads are warp-collective (.sync.aligned): the whole warp takes
     // this branch (ok, ntiles and the abort flag are the same for its lanes)
