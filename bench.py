@@ -55,8 +55,10 @@ def parse():
                     help="prefill: the 12-layer W8A8 prefill (default; N>1 = data-parallel "
                          "replicas); tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel "
                          "over the N GPUs")
-    ap.add_argument("--ncu-case", action="store_true",
-                    help="launch each kernel of one block once at the workload's shapes (for ncu)")
+    ap.add_argument("--ncu-case", nargs="?", const="prefill", default=None,
+                    choices=["prefill", "tp"],
+                    help="launch each kernel of one block once at the workload's shapes (for ncu); "
+                         "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2")
     return ap.parse_args()
 
 
@@ -314,6 +316,35 @@ def probe_kernels(torch, ltm, reps: int = 10, timed: bool = True):
                         flops=flops, bytes=nbytes))
     del flush, clean
     return res
+
+
+def probe_tp_case(torch, ltm):
+    """One launch each of the tensor-parallel layer's kernels at a reduced
+    batch (2 x 4096 tokens, 8 heads of 128, 8192 memory slots; a W8A8 GEMM
+    with M = 8192, N = 8192, K = 8192): inputs larger than L2, a few GB on the
+    device."""
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    B, S, nh, D, Ms = 2, 4096, 8, 128, 8192
+    H = nh * D
+    qkv = torch.randn((B * S, 4 * H), generator=gen, device=dev).to(torch.bfloat16)
+    kv = torch.randn((Ms, 2 * H), generator=gen, device=dev).to(torch.bfloat16)
+    o = torch.empty((B * S, H), dtype=torch.bfloat16, device=dev)
+    ltm.attention(qkv[:, :H], qkv[:, H:2 * H], qkv[:, 2 * H:3 * H], B, S, S, nh, D, True, out=o)
+    ltm.attention(qkv[:, 3 * H:], kv[:, :H], kv[:, H:], B, S, Ms, nh, D, False, kv_shared=True,
+                  out=o)
+    M = N = K = 8192
+    qa = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=gen)
+    qw = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=gen)
+    sa = torch.rand(M, device=dev) * 1e-4
+    sw = torch.rand(N, device=dev) * 1e-4
+    bias = torch.zeros(N, device=dev)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ltm._check(ltm.lib().ltm_linear_w8a8(ltm._ptr(qa), ltm._ptr(sa), ltm._ptr(qw), ltm._ptr(sw),
+                                         ltm._ptr(bias), 0, ltm._ptr(y), ltm.DTYPE_BF16, M, N, K,
+                                         ltm._stream()))
+    torch.cuda.synchronize()
 
 
 def int8_peak(torch):
@@ -693,7 +724,10 @@ def main():
     if args.ncu_case:
         import torch
         import ltm_b200 as ltm
-        probe_kernels(torch, ltm, timed=False)
+        if args.ncu_case == "tp":
+            probe_tp_case(torch, ltm)
+        else:
+            probe_kernels(torch, ltm, timed=False)
         emit({"ncu_case": "done", "device_error": ltm.device_error()})
         return
     if args.impl == "reference":
