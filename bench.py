@@ -51,10 +51,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
-    ap.add_argument("--config", choices=["prefill", "tp"], default="prefill",
+    ap.add_argument("--config", choices=["prefill", "tp", "w4a16"], default="prefill",
                     help="prefill: the 12-layer W8A8 prefill (default; N>1 = data-parallel "
                          "replicas); tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel "
-                         "over the N GPUs")
+                         "over the N GPUs; w4a16: the 4-layer hidden-4096 W4A16 long-context "
+                         "prefill (tensor-parallel when N > 1)")
     ap.add_argument("--ncu-case", nargs="?", const="prefill", default=None,
                     choices=["prefill", "tp"],
                     help="launch each kernel of one block once at the workload's shapes (for ncu); "
@@ -182,15 +183,24 @@ TP_WORKLOAD_NAME = ("8-layer Titan prefill, tensor-parallel, W8A8 INT8 linears +
                     "batch 16, seq 4096")
 
 
-def step_work_tp(layers: int, tp: int) -> dict:
+# W4A16 long-context prefill: hidden 4096, 32 heads (head_dim 128), FFN 11008,
+# 4096 memory slots, batch 4 x seq 8192, 4 layers, INT4 group-128 weights,
+# bf16 activations.
+W4_WL = dict(layers=4, B=4, S=8192, H=4096, nh=32, F=11008, Ms=4096)
+W4_WORKLOAD_NAME = ("4-layer Titan long-context prefill, W4A16 INT4 group-128 weights + bf16 "
+                    "activations, hidden 4096, 32 heads (head_dim 128), FFN 11008, 4096 memory "
+                    "slots, batch 4, seq 8192")
+
+
+def step_work_tp(layers: int, tp: int, wl: dict = TP_WL, gemm_class: str = "w8a8_tc_kernel") -> dict:
     """Algorithmic ops of one tensor-parallel step on one rank (its head /
     FFN shards; the gate projection is replicated)."""
-    B, S, H, F, Ms, nh = (TP_WL[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
+    B, S, H, F, Ms, nh = (wl[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
     T, dh, Hl, Fl, nhl = B * S, H // nh, H // tp, F // tp, nh // tp
     gemm = 2.0 * (T * 4 * Hl * H + Ms * 2 * Hl * H + 2 * T * H * Hl + T * H * H + T * Fl * H
                   + T * H * Fl)
     attn = 4.0 * B * nhl * dh * (S * (S + 1) / 2 + S * Ms)
-    return {"w8a8_tc_kernel": {"amount": gemm * layers, "unit": "flop"},
+    return {gemm_class: {"amount": gemm * layers, "unit": "flop"},
             "attn_tc_kernel": {"amount": attn * layers, "unit": "flop"}}
 
 
@@ -211,7 +221,7 @@ def roofline_of(result: dict, work: dict, torch) -> tuple:
     per_launch = work[dom]["amount"] / d["launches"]
     if work[dom]["unit"] == "flop":
         achieved = per_launch / (avg_ms * 1e-3) / 1e12
-        if dom.startswith("w8a8"):
+        if dom.startswith("w8a8"):  # int8 tensor peak; the 16-bit classes use bf16
             peak = i8 if i8 else 2.0 * pk["bf16_tflops"]
             peak_src = ("int8 cuBLASLt (torch._int_mm 8192^3) measured in this run" if i8 else
                         "2 x bf16_tflops " + pk_src + " (derived int8)")
@@ -406,11 +416,12 @@ def cpu_baseline(threads_hint=None):
                       f"{dt:.1f} s; tokens/s scaled to {WL['layers']} layers"}
 
 
-def run_tp(args):
+def run_tp(args, wl: dict = TP_WL, w4a16: bool = False):
     """The tensor-parallel prefill: one block per rank (its head / FFN shard of
     one random-init block, built from the same seeded full weights on every
     rank) applied at each of the layers; the input hidden states are the full
-    [B,S,H] on every rank.  Strong scaling: the job is fixed, N GPUs share it."""
+    [B,S,H] on every rank.  Strong scaling: the job is fixed, N GPUs share it.
+    With w4a16 the same driver runs the W4A16 long-context prefill."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -422,13 +433,14 @@ def run_tp(args):
     if ws > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     dev = torch.device("cuda", local)
-    L = args.layers or TP_WL["layers"]
-    B, S, H, F, Ms, nh = (TP_WL[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
+    L = args.layers or wl["layers"]
+    B, S, H, F, Ms, nh = (wl[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
     comm = (ltm.Comm.from_process_group(local) if ws > 1 else
             ltm.Comm(ltm.comm_unique_id(), 1, 0, local))
     cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
                                memory_slots=Ms)
-    q = ltm.QuantConfig(scheme=ltm.SCHEME_W8A8, act_dtype=ltm.DTYPE_BF16)
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W4A16 if w4a16 else ltm.SCHEME_W8A8,
+                        act_dtype=ltm.DTYPE_BF16)
     blk = ltm.TitanBlock(cfg, q, comm=comm)
     w = synthetic.block_weights(H, F, Ms, 1000)
     blk.load_weights(w)
@@ -508,7 +520,8 @@ def run_tp(args):
     all_ms = sum(ms for name, (n, ms) in kt.result.items())
     roofline = None
     if rank == 0 and not args.no_probe:
-        roofline, i8 = roofline_of(kt.result, step_work_tp(L, ws), torch)
+        work = step_work_tp(L, ws, wl, "w4a16_tc_kernel" if w4a16 else "w8a8_tc_kernel")
+        roofline, i8 = roofline_of(kt.result, work, torch)
         if i8:
             kernels["int8_peak_tops_measured"] = round(i8, 1)
     if rank == 0:
@@ -516,9 +529,10 @@ def run_tp(args):
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4xbf16" if w4a16 else "int8",
             "data": "synthetic (hidden states N(0,0.02^2), weights N(0,0.02), random init)",
-            "config": {"workload": TP_WORKLOAD_NAME, "layers": L, "global_batch": B,
+            "config": {"workload": W4_WORKLOAD_NAME if w4a16 else TP_WORKLOAD_NAME, "layers": L,
+                       "global_batch": B,
                        "seq_len": S, "act_dtype": "bf16", "parallelism": f"tp{ws}",
                        "tokens_per_s_per_gpu": round(value / ws, 1),
                        "comm_fraction_of_rank0_step": round(comm_ms / all_ms, 4) if all_ms else None,
@@ -734,6 +748,8 @@ def main():
         run_reference(args)
     elif args.config == "tp":
         run_tp(args)
+    elif args.config == "w4a16":
+        run_tp(args, W4_WL, w4a16=True)
     else:
         if args.layers is None:
             args.layers = WL["layers"]
