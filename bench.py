@@ -57,9 +57,10 @@ def parse():
                          "over the N GPUs; w4a16: the 4-layer hidden-4096 W4A16 long-context "
                          "prefill (tensor-parallel when N > 1)")
     ap.add_argument("--ncu-case", nargs="?", const="prefill", default=None,
-                    choices=["prefill", "tp"],
+                    choices=["prefill", "tp", "w4a16"],
                     help="launch each kernel of one block once at the workload's shapes (for ncu); "
-                         "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2")
+                         "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2; "
+                         "w4a16: the long-context layer's W4A16 GEMMs at 8192 tokens")
     return ap.parse_args()
 
 
@@ -354,6 +355,21 @@ def probe_tp_case(torch, ltm):
     ltm._check(ltm.lib().ltm_linear_w8a8(ltm._ptr(qa), ltm._ptr(sa), ltm._ptr(qw), ltm._ptr(sw),
                                          ltm._ptr(bias), 0, ltm._ptr(y), ltm.DTYPE_BF16, M, N, K,
                                          ltm._stream()))
+    torch.cuda.synchronize()
+
+
+def probe_w4a16_case(torch, ltm):
+    """One launch each of the long-context layer's W4A16 GEMM shapes at 8192
+    tokens (FFN up 11008 x 4096, FFN down 4096 x 11008), bf16."""
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    M = 8192
+    for N, K in ((11008, 4096), (4096, 11008)):
+        a = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+        w = (torch.randn((N, K), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+        packed, s, zp = ltm.quantize_int4_grouped(w)
+        ltm.linear_w4a16(a, packed, s, zp)
     torch.cuda.synchronize()
 
 
@@ -740,6 +756,8 @@ def main():
         import ltm_b200 as ltm
         if args.ncu_case == "tp":
             probe_tp_case(torch, ltm)
+        elif args.ncu_case == "w4a16":
+            probe_w4a16_case(torch, ltm)
         else:
             probe_kernels(torch, ltm, timed=False)
         emit({"ncu_case": "done", "device_error": ltm.device_error()})

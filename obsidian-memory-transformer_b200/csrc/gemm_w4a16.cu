@@ -34,11 +34,17 @@ struct W4Smem {
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;
 };
 
+// Two floats rounded to a packed pair of 16-bit values (one paired convert;
+// each half rounded to nearest-even as the single conversions do).
 template <class T>
 __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
-  T a = from_f32<T>(lo), b = from_f32<T>(hi);
-  return static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&a)) |
-         (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&b)) << 16);
+  if constexpr (std::is_same<T, __half>::value) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
 }
 
 template <class T, int MODE>
@@ -141,6 +147,11 @@ __global__ void __launch_bounds__(192, 2)
             sc = __ldg(s4 + gi);
             zp = static_cast<float>(__ldg(z4 + gi));
           }
+          // q - zp without an int->float conversion: the float with bits
+          // 0x4B000000 | q is 2^23 + q exactly, and (2^23 + q) - (2^23 + zp) is
+          // exact for 0 <= q, zp <= 15; then one rounding in the multiply, as
+          // in (q - zp) * s
+          const float bias_zp = 8388608.0f + zp;
           const uint4 p0 = *reinterpret_cast<const uint4*>(prow);
           const uint4 p1 = *reinterpret_cast<const uint4*>(prow + 16);
           const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
@@ -151,8 +162,10 @@ __global__ void __launch_bounds__(192, 2)
             uint32_t* o = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float lo = (static_cast<float>((w >> (8 * e)) & 0xF) - zp) * sc;
-              const float hi = (static_cast<float>((w >> (8 * e + 4)) & 0xF) - zp) * sc;
+              const float lo =
+                  (__uint_as_float(((w >> (8 * e)) & 0xFu) | 0x4B000000u) - bias_zp) * sc;
+              const float hi =
+                  (__uint_as_float(((w >> (8 * e + 4)) & 0xFu) | 0x4B000000u) - bias_zp) * sc;
               o[e] = pack_pair<T>(lo, hi);
             }
             *reinterpret_cast<uint4*>(brow + ((c ^ (t & 7)) << 4)) = out;
