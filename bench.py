@@ -51,16 +51,19 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
-    ap.add_argument("--config", choices=["prefill", "tp", "w4a16"], default="prefill",
+    ap.add_argument("--config", choices=["prefill", "tp", "w4a16", "decode"], default="prefill",
                     help="prefill: the 12-layer W8A8 prefill (default; N>1 = data-parallel "
                          "replicas); tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel "
                          "over the N GPUs; w4a16: the 4-layer hidden-4096 W4A16 long-context "
-                         "prefill (tensor-parallel when N > 1)")
+                         "prefill (tensor-parallel when N > 1); decode: the 32-layer hidden-4096 "
+                         "W4A16 batched decode step against a 32768-position KV cache (N > 1 = "
+                         "replicas)")
     ap.add_argument("--ncu-case", nargs="?", const="prefill", default=None,
-                    choices=["prefill", "tp", "w4a16"],
+                    choices=["prefill", "tp", "w4a16", "decode"],
                     help="launch each kernel of one block once at the workload's shapes (for ncu); "
                          "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2; "
-                         "w4a16: the long-context layer's W4A16 GEMMs at 8192 tokens")
+                         "w4a16: the long-context layer's W4A16 GEMMs at 8192 tokens; decode: "
+                         "one decode step of one block at batch 4, 32768 cached positions")
     return ap.parse_args()
 
 
@@ -191,6 +194,31 @@ W4_WL = dict(layers=4, B=4, S=8192, H=4096, nh=32, F=11008, Ms=4096)
 W4_WORKLOAD_NAME = ("4-layer Titan long-context prefill, W4A16 INT4 group-128 weights + bf16 "
                     "activations, hidden 4096, 32 heads (head_dim 128), FFN 11008, 4096 memory "
                     "slots, batch 4, seq 8192")
+
+
+# Batched decode: hidden 4096, 32 heads (head_dim 128), FFN 11008, 2048 memory
+# slots, 32 layers, INT4 group-128 weights, bf16 activations; batch 64, one new
+# token per sequence against a bf16 KV cache of 32768 positions per sequence
+# (N(0,1)); memory read and write (attention-score slot weights) every step.
+DEC_WL = dict(layers=32, B=64, P=32768, H=4096, nh=32, F=11008, Ms=2048)
+DEC_WORKLOAD_NAME = ("32-layer Titan batched decode, W4A16 INT4 group-128 weights + bf16 "
+                     "activations, hidden 4096, 32 heads (head_dim 128), FFN 11008, 2048 memory "
+                     "slots, batch 64 x 1 new token against a 32768-position bf16 KV cache per "
+                     "sequence, memory read + write every step")
+
+
+def decode_layer_bytes(wl: dict = DEC_WL) -> dict:
+    """Algorithmic HBM bytes of one decode layer: the K and V rows of the
+    cache's positions (the new one included), the packed INT4 weights with
+    their fp32 scales and uint8 zero-points, and the bank / K_M | V_M traffic
+    (bank read + write, K_M | V_M read + write by the EMA, K_M | V_M read by
+    the memory attention, K_M read by the slot weights)."""
+    B, P, H, F, Ms = (wl[k] for k in ("B", "P", "H", "F", "Ms"))
+    kv = 2 * B * P * H * 2
+    params = 4 * H * H + 2 * H * H + 3 * H * H + 2 * H * F
+    weights = params // 2 + (params // 128) * 5
+    bank = 2 * Ms * H * 2 + 2 * Ms * 2 * H * 2 + Ms * 2 * H * 2 + Ms * H * 2
+    return {"kv": kv, "weights": weights, "bank": bank, "total": kv + weights + bank}
 
 
 def step_work_tp(layers: int, tp: int, wl: dict = TP_WL, gemm_class: str = "w8a8_tc_kernel") -> dict:
@@ -571,6 +599,215 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False):
         dist.destroy_process_group()
 
 
+def cpu_baseline_decode(wl: dict = DEC_WL, budget_s: float = 12.0):
+    """The oracle's decode step on the host cores, bounded sample: 1 of the
+    layers, 1 of the batch's sequences against the full cache; tokens/s scaled
+    to the whole stack (quantized weights made once, outside the timing)."""
+    import numpy as np
+    from ltm_b200 import synthetic
+    from oracle import oracle as orc
+    H, nh, F, Ms, P = (wl[k] for k in ("H", "nh", "F", "Ms", "P"))
+    ocfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W4A16, dtype=orc.BF16,
+                memory_write=1, use_attention_scores=1, update_rate=0.9)
+    w = synthetic.block_weights(H, F, Ms, 1000)
+    pb = orc.PreparedBlock(ocfg, w)
+    rng = np.random.default_rng(5)
+    kc = orc.round_to(rng.standard_normal((1, P, H), dtype=np.float32), orc.BF16)
+    vc = orc.round_to(rng.standard_normal((1, P, H), dtype=np.float32), orc.BF16)
+    mem = orc.round_to(w["memory"], orc.BF16)
+    kvm = orc.round_to(rng.standard_normal((Ms, 2 * H), dtype=np.float32) * 0.1, orc.BF16)
+    x = orc.round_to(rng.standard_normal((1, H), dtype=np.float32) * 0.02, orc.BF16)
+    n, t0 = 0, time.perf_counter()
+    while n < 5 and (n == 0 or time.perf_counter() - t0 < budget_s):
+        pb.decode_step(x, kc, vc, P - 1, mem, kvm)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    pb.close()
+    return {"value": 1.0 / (dt * wl["layers"]), "unit": "tokens/s", "cores": orc.num_threads(),
+            "kind": "port",
+            "sample": f"oracle decode step, 1 of {wl['layers']} layers, 1 of {wl['B']} sequences "
+                      f"against the full {P}-position cache, {n} steps of {dt:.2f} s; tokens/s "
+                      f"scaled to {wl['layers']} layers"}
+
+
+def run_decode(args, wl: dict = DEC_WL):
+    """The batched decode step: one block per layer (each its own copy of the
+    same seeded weights, bank and resident K_M | V_M), one shared KV-cache
+    buffer for all layers (per-layer caches would need 1.1 TB), every step at
+    the cache's last position (the step rewrites it).  N > 1: independent
+    replicas, one batch per GPU."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import ltm_b200 as ltm
+    from ltm_b200 import synthetic
+    ws, rank, local = dist_env()
+    assert ws == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {ws}"
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    L = args.layers or wl["layers"]
+    B, P, H, F, Ms, nh = (wl[k] for k in ("B", "P", "H", "F", "Ms", "nh"))
+    cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
+                               memory_slots=Ms)
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W4A16, act_dtype=ltm.DTYPE_BF16, memory_write=True,
+                        use_attention_scores=True)
+    w = synthetic.block_weights(H, F, Ms, 1000)
+    blocks = []
+    for _ in range(L):
+        b = ltm.TitanBlock(cfg, q, device=local)
+        b.load_weights(w)
+        blocks.append(b)
+    del w
+    cache = ltm.CacheManager(L, H, torch.bfloat16, device=local, shared_layers=True)
+    cache.allocate(B, P)
+    gen = torch.Generator(device=dev).manual_seed(11 + rank)
+    for t in cache.get(0)[:2]:
+        flat = t.view(-1)
+        chunk = 1 << 28
+        for i in range(0, flat.numel(), chunk):
+            n = min(chunk, flat.numel() - i)
+            flat[i:i + n] = torch.randn(n, generator=gen, device=dev).to(torch.bfloat16)
+    pos = P - 1
+    x = (torch.randn((B, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    bufs = (torch.empty_like(x), torch.empty_like(x))
+    stream = torch.cuda.current_stream()
+
+    def step(inp):
+        a = inp
+        for i, b in enumerate(blocks):
+            kc, vc, _ = cache.get(i)
+            o = bufs[i % 2]
+            b.decode_step(a, kc, vc, pos, out=o)
+            a = o
+        return a
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    args.warmup = max(args.warmup, 3)
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(cvd.split(",")[local] if cvd else local)
+    launches0 = ltm.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    evs = []
+    for _ in range(args.steps):
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record(stream)
+        step(x)
+        e_.record(stream)
+        evs.append((s_, e_))
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    launches = ltm.launch_count() - launches0
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    value = ws * B * args.steps / (total_ms * 1e-3)
+
+    # end to end: pinned H2D of the step's input hidden states, the layers,
+    # D2H of the step's output hidden states
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+    barrier()
+    e2e_evs = []
+    for _ in range(args.steps):
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record(stream)
+        x.copy_(x_host, non_blocking=True)
+        y = step(x)
+        y_host.copy_(y, non_blocking=True)
+        e_.record(stream)
+        e2e_evs.append((s_, e_))
+    torch.cuda.synchronize()
+    barrier()
+    e2e_t = torch.tensor([sum(a.elapsed_time(b) for a, b in e2e_evs)], dtype=torch.float64,
+                         device=dev)
+    if ws > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = ws * B * args.steps / (float(e2e_t.item()) * 1e-3)
+
+    torch.cuda.synchronize()
+    with ltm.KernelTimer() as kt:
+        step(x)
+    kernels = {name: {"launches": n, "ms": round(ms, 4), "ms_per_launch": round(ms / n, 5)}
+               for name, (n, ms) in kt.result.items()}
+    lb = decode_layer_bytes(wl)
+    pk, pk_src = peaks()
+    step_ms = total_ms / args.steps
+    roofline = None
+    if rank == 0 and not args.no_probe:
+        work = {"decode_attn_kernel": {"amount": lb["kv"] * L, "unit": "byte"}}
+        roofline, _ = roofline_of(kt.result, work, torch)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_decode(wl)
+    if rank == 0:
+        step_gbs = lb["total"] * L / (step_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4xbf16",
+            "data": "synthetic (KV cache N(0,1), hidden states N(0,0.02^2), weights N(0,0.02), "
+                    "random init)",
+            "config": {"workload": DEC_WORKLOAD_NAME, "layers": L, "global_batch": B * ws,
+                       "kv_positions": P, "act_dtype": "bf16", "parallelism": f"replicas{ws}",
+                       "tokens_per_s_per_gpu": round(value / ws, 2),
+                       "step_bytes": lb["total"] * L,
+                       "step_hbm_gbs": round(step_gbs, 1),
+                       "step_hbm_frac": round(step_gbs / pk["hbm_gbs"], 4),
+                       "kv_cache": "one buffer shared by the layers (34.4 GB)",
+                       "l2": "inputs (34 GB KV cache per layer) larger than L2"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(x_host.numel() * 2),
+                    "d2h_bytes_per_step": int(y_host.numel() * 2)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "kernels": kernels,
+        }
+        emit(line)
+    for b in blocks:
+        b.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def probe_decode_case(torch, ltm):
+    """One decode step of one hidden-4096 block at batch 4 against a
+    32768-position cache (2.1 GB), after a warm-up step: every decode kernel
+    launched once more at the workload's per-sequence shapes (for ncu)."""
+    from ltm_b200 import synthetic
+    wl = dict(DEC_WL, B=4)
+    B, P, H, F, Ms, nh = (wl[k] for k in ("B", "P", "H", "F", "Ms", "nh"))
+    cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
+                               memory_slots=Ms)
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W4A16, act_dtype=ltm.DTYPE_BF16, memory_write=True,
+                        use_attention_scores=True)
+    blk = ltm.TitanBlock(cfg, q)
+    blk.load_weights(synthetic.block_weights(H, F, Ms, 1000))
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    kc = torch.randn((B, P, H), generator=gen, device="cuda").to(torch.bfloat16)
+    vc = torch.randn((B, P, H), generator=gen, device="cuda").to(torch.bfloat16)
+    x = (torch.randn((B, H), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    blk.decode_step(x, kc, vc, P - 1)
+    blk.decode_step(x, kc, vc, P - 1)
+    torch.cuda.synchronize()
+    blk.close()
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -758,6 +995,8 @@ def main():
             probe_tp_case(torch, ltm)
         elif args.ncu_case == "w4a16":
             probe_w4a16_case(torch, ltm)
+        elif args.ncu_case == "decode":
+            probe_decode_case(torch, ltm)
         else:
             probe_kernels(torch, ltm, timed=False)
         emit({"ncu_case": "done", "device_error": ltm.device_error()})
@@ -768,6 +1007,8 @@ def main():
         run_tp(args)
     elif args.config == "w4a16":
         run_tp(args, W4_WL, w4a16=True)
+    elif args.config == "decode":
+        run_decode(args)
     else:
         if args.layers is None:
             args.layers = WL["layers"]

@@ -289,6 +289,41 @@ LTM_API ltm_status ltm_block_load_weights(ltm_block* blk, const ltm_block_weight
 LTM_API ltm_status ltm_block_forward(ltm_block* blk, const void* x, void* y, const void* attention_mask,
                              int B, int S, void* stream);
 
+/* One batched decode step against a KV cache.  No callable counterpart in the
+ * reference: it replaces the KV-cache stubs CacheManagerImpl::allocate /
+ * update / get (python_bindings/src/main.cpp:101-135) and CacheManager
+ * (python_bindings/ltm/inference.py:101-128) with the TB-v1 block applied to
+ * one new token per sequence:
+ *   x, y     device [B, H] in act_dtype (f16 / bf16; distinct buffers);
+ *   k_cache, v_cache  device [B, max_positions, Hl] in act_dtype, 16-byte
+ *            aligned (Hl = H, or this rank's heads num_heads/n * head_dim
+ *            under tensor parallelism; head h at columns h*head_dim);
+ *            positions [0, cache_len) hold the post-RoPE keys and the values
+ *            of the tokens before; the step writes the new token's K and V at
+ *            position cache_len of every sequence;
+ *   the new token's RoPE position is cache_len; its self-attention reads the
+ *   cache_len + 1 positions [0, cache_len];
+ *   the memory attention reads K_M | V_M, which the block keeps resident
+ *   between decode steps (computed from the bank on the first step after
+ *   load_weights or after a forward that wrote the bank);
+ *   with memory_write the bank is written after the read (state = mean over
+ *   the batch of g * x) and K_M | V_M follow the same EMA towards
+ *   state [Wkm;Wvm]^T + b.
+ * 0 <= cache_len < max_positions.  Workspace grows on the first call at a new
+ * B or max_positions; the RoPE table grows in steps of 4096 positions. */
+LTM_API ltm_status ltm_block_decode_step(ltm_block* blk, const void* x, void* y, void* k_cache,
+                                         void* v_cache, int64_t max_positions, int cache_len, int B,
+                                         void* stream);
+
+/* Memory write of the block's own bank: MemoryBank<T>::store
+ * (src/core/ltm/memory_bank.cu:242-274) with a caller-given state (fp32 [H],
+ * device) and, with use_attention_scores, slot weights from the mean of the T
+ * memory-query rows `queries` (device, act_dtype, row stride ldq; this rank's
+ * heads' columns under tensor parallelism) against the block's K_M.  The
+ * resident K_M | V_M of the decode step follow the same EMA. */
+LTM_API ltm_status ltm_block_memory_write(ltm_block* blk, const float* state, const void* queries,
+                                          int64_t ldq, int64_t T, void* stream);
+
 /* Copies the memory bank [Ms,H] (act_dtype) to a device buffer
  * (getMemoryBank(), titan_inspired_block.cuh:133). */
 LTM_API ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stream);

@@ -207,11 +207,19 @@ struct ltm_block {
   DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, spm, y, zq, zs, z,
       u, uq, us, amax;
   MemoryWriteState mw;
+  // decode: K_M | V_M kept resident between steps (kvm_fresh: kvmb holds them
+  // for the current bank), the state row of the write and its projection,
+  // split-cache attention partials
+  bool kvm_fresh = false;
+  DevBuf crow, cq, cs, kcv, dpart;
 
   size_t act_bytes() const { return dtype_size(dt); }
 
+  // RoPE table of at least S positions (grown in steps of 4096 positions so
+  // that a decode loop rebuilds it once per 4096 steps).
   void ensure_rope(int S) {
     if (S <= rope_S) return;
+    S = (S + 4095) / 4096 * 4096;
     const int half = dh / 2;
     std::vector<float> tab(static_cast<size_t>(S) * dh);
     for (int p = 0; p < S; ++p)
@@ -270,70 +278,69 @@ struct ltm_block {
     launch_rowwise_int8_amax(src, dt, T, K, amx, qd, sd, st);
   }
 
-  void forward(const void* x, void* out, int B, int S, cudaStream_t st) {
-    const int64_t T = static_cast<int64_t>(B) * S;
-    ensure_ws(T);
-    if (cfg.use_rotary) ensure_rope(S);
-    const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
+  // K_M | V_M of the current bank into kvmb.
+  void compute_kvm(cudaStream_t st) {
+    if (q.scheme == LTM_SCHEME_W8A8)
+      launch_rowwise_int8(memory.ptr, dt, Ms, H, mq.as<int8_t>(), ms.as<float>(), st);
+    Epilogue ep;
+    ep.out = kvmb.ptr;
+    ep.ldo = 2 * Hl;
+    kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st);
+    kvm_fresh = true;
+  }
 
-    // 1. LN1 (+ per-token int8 of LN1(x) and of x for W8A8)
-    if (w8a8) {
+  // 1. LN1 (+ per-token int8 of LN1(x) and of x for W8A8); returns the
+  // projection input of the non-W8A8 schemes.
+  const void* ln1(const void* x, int64_t T, cudaStream_t st) {
+    if (q.scheme == LTM_SCHEME_W8A8) {
       launch_ln_x2(x, dt, T, H, ln1_g.as<float>(), ln1_b.as<float>(), nullptr, hq.as<int8_t>(),
                    hs.as<float>(), xq.as<int8_t>(), xs.as<float>(), cfg.use_layer_norm != 0, st);
     } else if (cfg.use_layer_norm) {
       launch_ln_x2(x, dt, T, H, ln1_g.as<float>(), ln1_b.as<float>(), h.ptr, nullptr, nullptr,
                    nullptr, nullptr, true, st);
     }
-    const void* hin = (w8a8 || cfg.use_layer_norm) ? h.ptr : x;
+    return (q.scheme == LTM_SCHEME_W8A8 || cfg.use_layer_norm) ? h.ptr : x;
+  }
 
-    // 2. memory keys / values from the bank
-    if (w8a8) launch_rowwise_int8(memory.ptr, dt, Ms, H, mq.as<int8_t>(), ms.as<float>(), st);
-    {
-      Epilogue ep;
-      ep.out = kvmb.ptr;
-      ep.ldo = 2 * Hl;
-      kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st);
-    }
-    // 3. fused Q | K | V | Qm projection with RoPE on Q, K
-    {
-      Epilogue ep;
-      ep.out = qkv.ptr;
-      ep.ldo = 4 * Hl;
-      ep.rope = rope.as<float2>();
-      ep.rope_cols = cfg.use_rotary ? 2 * Hl : 0;
-      ep.seq_len = S;
-      ep.head_dim = dh;
-      qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
-               ep, st);
-    }
-    // 4. causal self-attention, memory attention
-    {
-      const size_t a = act_bytes();
-      AttnParams p{};
-      p.q = qkv.ptr;
-      p.k = static_cast<const char*>(qkv.ptr) + Hl * a;
-      p.v = static_cast<const char*>(qkv.ptr) + 2 * Hl * a;
-      p.o = os.ptr;
-      p.ldq = p.ldk = p.ldv = 4 * Hl;
-      p.ldo = Hl;
-      p.q_batch_rows = S;
-      p.kv_batch_rows = S;
-      p.Sq = S;
-      p.Skv = S;
-      p.nh = nhl;
-      p.causal_offset = 0;
-      launch_attention(p, B, dh, true, dt, st);
-      AttnParams pm = p;
-      pm.q = static_cast<const char*>(qkv.ptr) + 3 * Hl * a;
-      pm.k = kvmb.ptr;
-      pm.v = static_cast<const char*>(kvmb.ptr) + Hl * a;
-      pm.o = om_.ptr;
-      pm.ldk = pm.ldv = 2 * Hl;
-      pm.kv_batch_rows = 0;
-      pm.Skv = Ms;
-      launch_attention(pm, B, dh, false, dt, st);
-    }
-    // 5. output projections
+  // 3. fused Q | K | V | Qm projection with RoPE on Q, K at position
+  // pos0 + (row % S)
+  void qkv_proj(const void* hin, int64_t T, int S, int pos0, cudaStream_t st) {
+    Epilogue ep;
+    ep.out = qkv.ptr;
+    ep.ldo = 4 * Hl;
+    ep.rope = rope.as<float2>() + static_cast<int64_t>(pos0) * (dh / 2);
+    ep.rope_cols = cfg.use_rotary ? 2 * Hl : 0;
+    ep.seq_len = S;
+    ep.head_dim = dh;
+    qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
+             ep, st);
+  }
+
+  // Memory attention of nb groups of sq query rows against K_M | V_M (the
+  // bank is shared: every group reads the same keys).
+  void mem_attention(int nb, int sq, cudaStream_t st) {
+    const size_t a = act_bytes();
+    AttnParams pm{};
+    pm.q = static_cast<const char*>(qkv.ptr) + 3 * Hl * a;
+    pm.k = kvmb.ptr;
+    pm.v = static_cast<const char*>(kvmb.ptr) + Hl * a;
+    pm.o = om_.ptr;
+    pm.ldq = 4 * Hl;
+    pm.ldk = pm.ldv = 2 * Hl;
+    pm.ldo = Hl;
+    pm.q_batch_rows = sq;
+    pm.kv_batch_rows = 0;
+    pm.Sq = sq;
+    pm.Skv = Ms;
+    pm.nh = nhl;
+    pm.causal_offset = 0;
+    launch_attention(pm, nb, dh, false, dt, st);
+  }
+
+  // 5-7. output projections, gated memory integration, FFN with residual
+  // (os, om_ hold the two attention outputs of the T rows).
+  void tail(const void* x, void* out, int64_t T, cudaStream_t st) {
+    const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
     if (w8a8) {
       quant_rows(os.ptr, T, Hl, osq.as<int8_t>(), oss.as<float>(), amax.as<float>(), st);
       quant_rows(om_.ptr, T, Hl, omq.as<int8_t>(), oms.as<float>(),
@@ -395,13 +402,114 @@ struct ltm_block {
              st);
     }
     if (tp > 1) comm_allreduce(comm, out, out, T * H, dt, false, st);
-    // 8. memory write after the read
-    if (q.memory_write && cfg.use_memory_gating) {
-      const size_t a = act_bytes();
-      mw.update_bank(memory.ptr, kvmb.ptr, 2 * Hl, static_cast<const char*>(qkv.ptr) + 3 * Hl * a,
-                     4 * Hl, T, H, nhl, nh, dh, Ms, cfg.memory_update_rate,
-                     q.use_attention_scores != 0, dt, comm, st);
+  }
+
+  // 8. memory write after the read.  kvm_follow: K_M | V_M follow the bank's
+  // EMA towards the projected state (decode keeps them resident); otherwise
+  // they are recomputed from the bank before their next use.
+  void write(int64_t T, bool kvm_follow, cudaStream_t st) {
+    const size_t a = act_bytes();
+    const float scale = mw.update_bank(memory.ptr, kvmb.ptr, 2 * Hl,
+                                       static_cast<const char*>(qkv.ptr) + 3 * Hl * a, 4 * Hl, T, H,
+                                       nhl, nh, dh, Ms, cfg.memory_update_rate,
+                                       q.use_attention_scores != 0, dt, comm, st);
+    if (!kvm_follow) {
+      kvm_fresh = false;
+      return;
     }
+    follow_kvm(mw.colsum.as<float>(), scale,
+               q.use_attention_scores ? mw.wslot.as<float>() : nullptr, st);
+  }
+
+  // K_M | V_M follow the bank's EMA (slot weights wslot, or the update rate):
+  // kvm[s] = (1 - w_s) kvm[s] + w_s (c [Wkm;Wvm]^T + b) with c = state * scale
+  // rounded to the activation dtype.
+  void follow_kvm(const float* state, float scale, const float* wslot, cudaStream_t st) {
+    const size_t a = act_bytes();
+    crow.ensure(static_cast<size_t>(H) * a);
+    kcv.ensure(static_cast<size_t>(2 * Hl) * a);
+    launch_state_row(state, scale, crow.ptr, H, dt, st);
+    if (q.scheme == LTM_SCHEME_W8A8) {
+      cq.ensure(H);
+      cs.ensure(sizeof(float));
+      launch_rowwise_int8(crow.ptr, dt, 1, H, cq.as<int8_t>(), cs.as<float>(), st);
+    }
+    Epilogue ep;
+    ep.out = kcv.ptr;
+    ep.ldo = 2 * Hl;
+    kvm.run(crow.ptr, cq.as<int8_t>(), cs.as<float>(), 1, kEpiPlain, dt, ep, st);
+    launch_rows_ema(kvmb.ptr, 2 * Hl, 2 * Hl, kcv.ptr, wslot, cfg.memory_update_rate, Ms, dt, st);
+  }
+
+  // Memory write of a caller-given state (fp32 [H]) with slot weights from
+  // the mean of T memory-query rows (this rank's heads' columns, stride ldq)
+  // against the current K_M; K_M | V_M follow when they are resident.
+  void write_state(const float* state, const void* queries, int64_t ldq, int64_t T,
+                   cudaStream_t st) {
+    const bool use_scores = q.use_attention_scores != 0;
+    if (use_scores) {
+      if (!kvm_fresh) compute_kvm(st);
+      mw.qsum.ensure(static_cast<size_t>(Hl) * sizeof(float));
+      mw.wslot.ensure(static_cast<size_t>(Ms) * sizeof(float));
+      launch_slot_weights(kvmb.ptr, 2 * Hl, queries, ldq, T, Ms, nhl, dh, nh,
+                          cfg.memory_update_rate, dt, mw.qsum.as<float>(), mw.wslot.as<float>(),
+                          st);
+      if (tp > 1) comm_allreduce(comm, mw.wslot.ptr, mw.wslot.ptr, Ms, LTM_DTYPE_F32, false, st);
+    }
+    const float* wslot = use_scores ? mw.wslot.as<float>() : nullptr;
+    launch_bank_update(memory.ptr, state, 1.0f, wslot, cfg.memory_update_rate, Ms, H, dt, st);
+    if (kvm_fresh) follow_kvm(state, 1.0f, wslot, st);
+  }
+
+  void forward(const void* x, void* out, int B, int S, cudaStream_t st) {
+    const int64_t T = static_cast<int64_t>(B) * S;
+    ensure_ws(T);
+    if (cfg.use_rotary) ensure_rope(S);
+    const void* hin = ln1(x, T, st);
+    // 2. memory keys / values from the bank
+    compute_kvm(st);
+    qkv_proj(hin, T, S, 0, st);
+    // 4. causal self-attention, memory attention
+    {
+      const size_t a = act_bytes();
+      AttnParams p{};
+      p.q = qkv.ptr;
+      p.k = static_cast<const char*>(qkv.ptr) + Hl * a;
+      p.v = static_cast<const char*>(qkv.ptr) + 2 * Hl * a;
+      p.o = os.ptr;
+      p.ldq = p.ldk = p.ldv = 4 * Hl;
+      p.ldo = Hl;
+      p.q_batch_rows = S;
+      p.kv_batch_rows = S;
+      p.Sq = S;
+      p.Skv = S;
+      p.nh = nhl;
+      p.causal_offset = 0;
+      launch_attention(p, B, dh, true, dt, st);
+      mem_attention(B, S, st);
+    }
+    tail(x, out, T, st);
+    if (q.memory_write && cfg.use_memory_gating) write(T, false, st);
+  }
+
+  // One decode step: x, out [B, H], every sequence's new token at position L;
+  // k_cache / v_cache [B, P, Hl] hold positions [0, L) and receive position L.
+  void decode(const void* x, void* out, void* kc, void* vc, int64_t P, int L, int B,
+              cudaStream_t st) {
+    const int64_t T = B;
+    ensure_ws(T);
+    if (cfg.use_rotary) ensure_rope(L + 1);
+    if (!kvm_fresh) compute_kvm(st);
+    const void* hin = ln1(x, T, st);
+    qkv_proj(hin, T, 1, L, st);
+    launch_kv_append(qkv.ptr, 4 * Hl, Hl, kc, vc, P * Hl, L, B, dt, st);
+    const size_t pb = decode_partials_bytes(B, nhl, dh, P);
+    if (pb > dpart.bytes) dpart.ensure(pb);
+    launch_decode_attention(qkv.ptr, 4 * Hl, kc, vc, P * Hl, Hl, L + 1, B, nhl, dh, dt,
+                            dpart.as<float>(), os.ptr, Hl, st);
+    mem_attention(1, B, st);  // the batch's rows share the bank: one group of B queries
+    tail(x, out, T, st);
+    if (q.memory_write && cfg.use_memory_gating) write(T, true, st);
   }
 };
 
@@ -508,6 +616,7 @@ void load_block(ltm_block* b, const ltm_block_weights* w, cudaStream_t st) {
   }
   LTM_CUDA_TRY(cudaStreamSynchronize(st));
   b->loaded = true;
+  b->kvm_fresh = false;
 }
 
 struct DeviceGuard {
@@ -626,6 +735,42 @@ extern "C" ltm_status ltm_block_forward(ltm_block* blk, const void* x, void* y,
     LTM_REQUIRE(x && y && x != y, "x and y must be distinct device buffers");
     DeviceGuard g(blk->device);
     blk->forward(x, y, B, S, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_block_decode_step(ltm_block* blk, const void* x, void* y, void* k_cache,
+                                            void* v_cache, int64_t max_positions, int cache_len,
+                                            int B, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded, "block not created or weights not loaded");
+    LTM_REQUIRE(B >= 0, "negative batch");
+    if (B == 0) return;
+    LTM_REQUIRE(x && y && x != y, "x and y must be distinct device buffers");
+    LTM_REQUIRE(k_cache && v_cache && k_cache != v_cache, "NULL or aliased KV cache");
+    LTM_REQUIRE(blk->dt != LTM_DTYPE_F32, "decode needs f16 or bf16 activations (W8A8 / W4A16)");
+    LTM_REQUIRE(cache_len >= 0 && static_cast<int64_t>(cache_len) < max_positions,
+                "cache_len must lie in [0, max_positions)");
+    LTM_REQUIRE((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 == 0,
+                "KV cache must be 16-byte aligned");
+    DeviceGuard g(blk->device);
+    blk->decode(x, y, k_cache, v_cache, max_positions, cache_len, B, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_block_memory_write(ltm_block* blk, const float* state,
+                                             const void* queries, int64_t ldq, int64_t T,
+                                             void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded, "block not created or weights not loaded");
+    LTM_REQUIRE(state, "NULL state");
+    if (blk->q.use_attention_scores) {
+      LTM_REQUIRE(queries && T > 0, "attention-score slot weights need at least one query row");
+      LTM_REQUIRE(ldq >= blk->Hl, "query row stride smaller than the block's query width");
+      LTM_REQUIRE(static_cast<size_t>(blk->Ms) * sizeof(float) <= 200 * 1024,
+                  "memory_slots too large for the slot-weight kernel (max 51200)");
+    }
+    DeviceGuard g(blk->device);
+    blk->write_state(state, queries, ldq, T, as_stream(stream));
   });
 }
 

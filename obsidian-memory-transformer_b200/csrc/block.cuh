@@ -72,10 +72,33 @@ struct MemoryWriteState {
   // kvm: K_M [Ms, heads*dh] with row stride ldk; qm: memory queries [T,
   // heads*dh] with row stride ldq (this rank's `heads` of nh_total; comm
   // sums the slot weights over the ranks when given).
-  void update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm, int64_t ldq,
-                   int64_t T, int H, int heads, int nh_total, int dh, int Ms, float rate,
-                   bool use_scores, ltm_dtype dt, ltm_comm* comm, cudaStream_t st);
+  // Returns the factor that turns colsum into the state c (1 / T, and the
+  // mean over the ranks under tensor parallelism).
+  float update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm, int64_t ldq,
+                    int64_t T, int H, int heads, int nh_total, int dh, int Ms, float rate,
+                    bool use_scores, ltm_dtype dt, ltm_comm* comm, cudaStream_t st);
 };
+
+// The state c = state * scale as one row [H] in the activation dtype.
+void launch_state_row(const float* state, float scale, void* out, int H, ltm_dtype dt,
+                      cudaStream_t st);
+
+// rows[s, :width] = (1 - w_s) rows[s, :width] + w_s v  (w_s = wslot[s], or
+// rate when wslot is NULL); rows of stride ld, 16-bit activations.
+void launch_rows_ema(void* rows, int64_t ld, int width, const void* v, const float* wslot,
+                     float rate, int Ms, ltm_dtype dt, cudaStream_t st);
+
+// Decode step: the new token's K | V rows (columns [width, 3 width) of the
+// fused projection rows, stride ldq) to position pos of every sequence's
+// cache (seq_stride elements apart, rows of `width`).
+void launch_kv_append(const void* qkv, int64_t ldq, int width, void* kc, void* vc,
+                      int64_t seq_stride, int64_t pos, int B, ltm_dtype dt, cudaStream_t st);
+// Self-attention of one query row per (sequence, head) over L cached
+// positions (split into chunks, partials in `part`, then merged into o).
+size_t decode_partials_bytes(int B, int nh, int D, int64_t L);
+void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const void* vc,
+                             int64_t seq_stride, int width, int L, int B, int nh, int D,
+                             ltm_dtype dt, float* part, void* o, int64_t ldo, cudaStream_t st);
 
 // Slot weights of `heads` heads (rate / nh_total per head, summed into wslot;
 // qsum [heads*dh] and wslot [Ms] are cleared here) and the bank EMA.

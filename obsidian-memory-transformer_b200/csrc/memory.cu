@@ -99,7 +99,62 @@ __global__ void __launch_bounds__(256) bank_update_kernel(T* __restrict__ mem,
   }
 }
 
+// rows[s, :] = (1 - w_s) rows[s, :] + w_s v  (K_M | V_M following the bank's
+// EMA; v = the state row's projection), 8 elements per thread.
+template <class T>
+__global__ void __launch_bounds__(256) rows_ema_kernel(T* __restrict__ rows, int64_t ld, int width,
+                                                       const T* __restrict__ v,
+                                                       const float* __restrict__ wslot, float rate,
+                                                       int Ms) {
+  const int nv = width / 8;
+  const int64_t n = static_cast<int64_t>(Ms) * nv;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(i / nv), c = static_cast<int>(i - static_cast<int64_t>(s) * nv);
+    const float w = wslot ? wslot[s] : rate;
+    uint4* rp = reinterpret_cast<uint4*>(rows + s * ld) + c;
+    uint4 r = *rp;
+    const uint4 vv = __ldg(reinterpret_cast<const uint4*>(v) + c);
+    T* re = reinterpret_cast<T*>(&r);
+    const T* ve = reinterpret_cast<const T*>(&vv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) re[k] = from_f32<T>((1.0f - w) * to_f32(re[k]) + w * to_f32(ve[k]));
+    *rp = r;
+  }
+}
+
+// out[j] = state[j] * scale in the activation dtype
+template <class T>
+__global__ void state_row_kernel(const float* __restrict__ state, float scale, T* __restrict__ out,
+                                 int H) {
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x)
+    out[j] = from_f32<T>(state[j] * scale);
+}
+
 }  // namespace
+
+void launch_rows_ema(void* rows, int64_t ld, int width, const void* v, const float* wslot,
+                     float rate, int Ms, ltm_dtype dt, cudaStream_t st) {
+  LTM_REQUIRE(dt != LTM_DTYPE_F32 && width % 8 == 0 && ld % 8 == 0,
+              "row EMA needs 16-bit rows of a multiple of 8 elements");
+  dispatch_dtype(dt, [&](auto tag) {
+    using TT = decltype(tag);
+    const int64_t n = static_cast<int64_t>(Ms) * (width / 8);
+    const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
+    rows_ema_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(rows), ld, width,
+                                              static_cast<const TT*>(v), wslot, rate, Ms);
+    check_launch("rows_ema_kernel", st);
+  });
+}
+
+void launch_state_row(const float* state, float scale, void* out, int H, ltm_dtype dt,
+                      cudaStream_t st) {
+  dispatch_dtype(dt, [&](auto tag) {
+    using TT = decltype(tag);
+    state_row_kernel<TT><<<(H + 255) / 256, 256, 0, st>>>(state, scale, static_cast<TT*>(out), H);
+    check_launch("state_row_kernel", st);
+  });
+}
 
 void MemoryWriteState::prepare_gate_epilogue(Epilogue& ep, int H, cudaStream_t st) {
   colsum.ensure(H * sizeof(float));
@@ -166,11 +221,11 @@ void validate_memory_store(const void* memory, const void* keys, int64_t ldk, co
   }
 }
 
-void MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm,
-                                   int64_t ldq, int64_t T, int H, int heads, int nh_total, int dh,
-                                   int Ms, float rate, bool use_scores, ltm_dtype dt,
-                                   ltm_comm* comm, cudaStream_t st) {
-  if (T == 0 || Ms == 0) return;
+float MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm,
+                                    int64_t ldq, int64_t T, int H, int heads, int nh_total, int dh,
+                                    int Ms, float rate, bool use_scores, ltm_dtype dt,
+                                    ltm_comm* comm, cudaStream_t st) {
+  if (T == 0 || Ms == 0) return 0.0f;
   const int Hq = heads * dh;
   if (use_scores) {
     qsum.ensure(Hq * sizeof(float));
@@ -191,6 +246,7 @@ void MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, c
   }
   launch_bank_update(memory, colsum.as<float>(), state_scale,
                      use_scores ? wslot.as<float>() : nullptr, rate, Ms, H, dt, st);
+  return state_scale;
 }
 
 namespace {

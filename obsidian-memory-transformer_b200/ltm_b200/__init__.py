@@ -96,6 +96,8 @@ def _declare(L):
         "ltm_block_load_weights": ([vp, C.POINTER(BlockWeightsC)], ci),
         "ltm_block_forward": ([vp, vp, vp, vp, ci, ci, vp], ci),
         "ltm_block_get_memory": ([vp, vp, vp], ci),
+        "ltm_block_decode_step": ([vp, vp, vp, vp, vp, i64, ci, ci, vp], ci),
+        "ltm_block_memory_write": ([vp, vp, vp, i64, i64, vp], ci),
         "ltm_block_destroy": ([vp], ci),
         "ltm_model_create": ([C.POINTER(BlockConfigC), C.POINTER(QuantConfigC), ci, ci, ci,
                               C.POINTER(vp)], ci),
@@ -530,6 +532,33 @@ class TitanBlock:
 
     __call__ = forward
 
+    def decode_step(self, x, k_cache, v_cache, cache_len: int, stream=None, out=None):
+        """One decode step: x [B, H] (one new token per sequence, all at
+        position cache_len) -> y [B, H].  k_cache / v_cache: CUDA tensors
+        [B, max_positions, Hl] in the act dtype holding positions
+        [0, cache_len); the step writes position cache_len."""
+        torch = _torch()
+        _need_cuda(x, k_cache, v_cache, out)
+        B = x.shape[0]
+        if k_cache.shape != v_cache.shape or k_cache.dim() != 3 or k_cache.shape[0] != B:
+            raise LtmError(ERR_INVALID_ARG, "k_cache / v_cache must both be [B, max_positions, Hl]")
+        if not (k_cache.is_contiguous() and v_cache.is_contiguous() and x.is_contiguous()):
+            raise LtmError(ERR_INVALID_ARG, "x and the caches must be contiguous")
+        y = torch.empty_like(x) if out is None else out
+        _check(lib().ltm_block_decode_step(self._h, _ptr(x), _ptr(y), _ptr(k_cache), _ptr(v_cache),
+                                           k_cache.shape[1], int(cache_len), B, _stream(stream)))
+        return y
+
+    def memory_write(self, state, queries=None, stream=None) -> None:
+        """Memory write of the block's bank towards `state` (fp32 [H]) with
+        slot weights from the mean of the memory-query rows `queries` [T, Hl]
+        (when use_attention_scores)."""
+        _need_cuda(state, queries)
+        T = 0 if queries is None else queries.shape[0]
+        ldq = 0 if queries is None else queries.stride(0)
+        _check(lib().ltm_block_memory_write(self._h, _ptr(state), _ptr(queries), ldq, T,
+                                            _stream(stream)))
+
     def memory(self, stream=None):
         torch = _torch()
         out = torch.empty((self.config.memory_slots, self.config.hidden_dim),
@@ -547,6 +576,63 @@ class TitanBlock:
             self.close()
         except Exception:  # noqa: BLE001 - interpreter shutdown
             pass
+
+
+class CacheManager:
+    """KV caches of a stack of blocks for decoding (the reference's
+    CacheManager, python_bindings/ltm/inference.py:101-128, whose native side
+    is a stub): allocate(batch_size, seq_length) makes one K and one V tensor
+    [batch_size, seq_length, width] per layer; update(...) records that a step
+    appended one position; get(index) returns the (keys, values, None) of
+    layer `index`; clear() forgets the cached positions.
+
+    `shared_layers` makes every layer use the same two tensors (a benchmark
+    whose per-layer caches do not fit in device memory)."""
+
+    def __init__(self, n_layers: int, width: int, dtype, device: int = 0,
+                 shared_layers: bool = False):
+        self.n_layers, self.width, self.dtype, self.device = n_layers, width, dtype, device
+        self.shared_layers = shared_layers
+        self.length = 0
+        self._k, self._v = [], []
+
+    def allocate(self, batch_size: int, seq_length: int) -> None:
+        torch = _torch()
+        n = 1 if self.shared_layers else self.n_layers
+        shape = (batch_size, seq_length, self.width)
+        dev = f"cuda:{self.device}"
+        self._k = [torch.empty(shape, dtype=self.dtype, device=dev) for _ in range(n)]
+        self._v = [torch.empty(shape, dtype=self.dtype, device=dev) for _ in range(n)]
+        self.length = 0
+
+    @property
+    def max_positions(self) -> int:
+        return self._k[0].shape[1] if self._k else 0
+
+    def update(self, key=None, value=None, memory=None) -> None:
+        """Marks one appended position (the decode step wrote it in place)."""
+        if self.length >= self.max_positions:
+            raise LtmError(ERR_INVALID_ARG, "KV cache full")
+        self.length += 1
+
+    def get(self, index: int):
+        i = 0 if self.shared_layers else index
+        return self._k[i], self._v[i], None
+
+    def clear(self) -> None:
+        self.length = 0
+
+
+def decode_step(blocks, x, cache: CacheManager, stream=None):
+    """One decode step of a stack of blocks: x [B, H] -> hidden [B, H]; every
+    layer reads and appends position cache.length of its cache, then the cache
+    advances by one position."""
+    cur = x
+    for i, blk in enumerate(blocks):
+        k, v, _ = cache.get(i)
+        cur = blk.decode_step(cur, k, v, cache.length, stream=stream)
+    cache.update()
+    return cur
 
 
 class TitanModel:

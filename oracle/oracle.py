@@ -71,6 +71,14 @@ def _declare(L):
         "orc_attention": ([f, i64, f, f, i64, ci, ci, ci, ci, ci, ci, ci, ci, f, i64], None),
         "orc_memory_store": ([f, f, i64, f, i64, i64, f, ci, ci, ci, C.c_float, ci, ci], None),
         "orc_block_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci], ci),
+        "orc_block_forward_kv": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci, f], ci),
+        "orc_block_kvm": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f], ci),
+        "orc_block_decode_step": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, f, f, i64, ci,
+                                   ci, f], ci),
+        "orc_block_prepare": ([_p(OrcBlockCfg), _p(OrcBlockWeights)], C.c_void_p),
+        "orc_block_release": ([C.c_void_p], None),
+        "orc_block_decode_step_prepared": ([C.c_void_p, _p(OrcBlockCfg), _p(OrcBlockWeights), f, f,
+                                            f, f, f, i64, ci, ci, f], ci),
         "orc_model_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), _p(f), ci, f, ci, i32, f, ci,
                                ci], ci),
     }
@@ -234,17 +242,85 @@ def _weights(w: dict):
     return st, keep
 
 
-def block_forward(cfg: dict, w: dict, x, B: int, S: int, memory=None):
-    """TB-v1 block forward. Returns (y [B*S,H], memory after the optional write)."""
+def block_forward(cfg: dict, w: dict, x, B: int, S: int, memory=None, return_kv=False):
+    """TB-v1 block forward. Returns (y [B*S,H], memory after the optional write)
+    and, with return_kv, the post-RoPE K | V rows [B*S, 2H] as a third item."""
     c = _cfg(cfg)
     st, keep = _weights(w)
     mem = round_to(w["memory"] if memory is None else memory, cfg["dtype"])
     x = _f32(x)
     y = np.empty_like(x)
-    r = lib().orc_block_forward(C.byref(c), C.byref(st), _ptr(mem), _ptr(x), _ptr(y), B, S)
+    kv = np.empty((x.shape[0], 2 * cfg["H"]), np.float32) if return_kv else None
+    r = lib().orc_block_forward_kv(C.byref(c), C.byref(st), _ptr(mem), _ptr(x), _ptr(y), B, S,
+                                   _ptr(kv))
     if r != 0:
         raise RuntimeError(f"orc_block_forward failed ({r})")
-    return y, mem
+    return (y, mem, kv) if return_kv else (y, mem)
+
+
+def block_kvm(cfg: dict, w: dict, memory=None):
+    """K_M | V_M [Ms, 2H] of a bank (the block's weights' bank by default)."""
+    c = _cfg(cfg)
+    st, keep = _weights(w)
+    mem = round_to(w["memory"] if memory is None else memory, cfg["dtype"])
+    out = np.empty((cfg["Ms"], 2 * cfg["H"]), np.float32)
+    r = lib().orc_block_kvm(C.byref(c), C.byref(st), _ptr(mem), _ptr(out))
+    if r != 0:
+        raise RuntimeError(f"orc_block_kvm failed ({r})")
+    return out
+
+
+def block_decode_step(cfg: dict, w: dict, x, k_cache, v_cache, cache_len: int, memory, kvm):
+    """One decode step (x [B, H], every sequence at position cache_len).
+    k_cache, v_cache: float32 [B, P, H]; memory [Ms, H]; kvm [Ms, 2H] -- all
+    updated in place.  Returns y [B, H]."""
+    c = _cfg(cfg)
+    st, keep = _weights(w)
+    x = _f32(x)
+    B = x.shape[0]
+    for a in (k_cache, v_cache, memory, kvm):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    P = k_cache.shape[1]
+    y = np.empty_like(x)
+    r = lib().orc_block_decode_step(C.byref(c), C.byref(st), _ptr(memory), _ptr(kvm), _ptr(x),
+                                    _ptr(k_cache), _ptr(v_cache), P, cache_len, B, _ptr(y))
+    if r != 0:
+        raise RuntimeError(f"orc_block_decode_step failed ({r})")
+    return y
+
+
+class PreparedBlock:
+    """A block whose quantized linears are made once, for repeated decode
+    steps (same arithmetic as block_decode_step)."""
+
+    def __init__(self, cfg: dict, w: dict):
+        self.c = _cfg(cfg)
+        self.st, self._keep = _weights(w)
+        self.h = lib().orc_block_prepare(C.byref(self.c), C.byref(self.st))
+
+    def decode_step(self, x, k_cache, v_cache, cache_len: int, memory, kvm):
+        x = _f32(x)
+        for a in (k_cache, v_cache, memory, kvm):
+            assert a.dtype == np.float32 and a.flags.c_contiguous
+        y = np.empty_like(x)
+        r = lib().orc_block_decode_step_prepared(self.h, C.byref(self.c), C.byref(self.st),
+                                                 _ptr(memory), _ptr(kvm), _ptr(x), _ptr(k_cache),
+                                                 _ptr(v_cache), k_cache.shape[1], cache_len,
+                                                 x.shape[0], _ptr(y))
+        if r != 0:
+            raise RuntimeError(f"orc_block_decode_step failed ({r})")
+        return y
+
+    def close(self):
+        if self.h:
+            lib().orc_block_release(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 def model_forward(cfg: dict, layers: list, embedding, tokens, B: int, S: int):

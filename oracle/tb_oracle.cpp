@@ -334,82 +334,101 @@ std::vector<float> concat_rows(const float* a, int64_t na, const float* b, int64
 
 }  // namespace
 
+namespace {
+
+// Slot weights of the write: rate * mean over heads of softmax_s(qbar_h .
+// K_M[s]_h / sqrt(dh)), qbar = mean of the T query rows; rate alone without
+// scores.
+std::vector<float> slot_weights(const float* keys, int64_t ldk, const float* queries, int64_t ldq,
+                                int64_t T, int Ms, int H, int nh, float rate, int use_scores) {
+  const int dh = H / nh;
+  std::vector<float> wsl(Ms, rate);
+  if (!use_scores) return wsl;
+  std::vector<double> qbar(H, 0.0);
+  for (int64_t t = 0; t < T; ++t)
+    for (int j = 0; j < H; ++j) qbar[j] += queries[t * ldq + j];
+  for (int j = 0; j < H; ++j) qbar[j] /= static_cast<double>(T);
+  std::vector<double> a(Ms, 0.0), sc(Ms);
+  const double scale = 1.0 / std::sqrt(static_cast<double>(dh));
+  for (int hh = 0; hh < nh; ++hh) {
+    double mx = -1e300;
+    for (int s = 0; s < Ms; ++s) {
+      double d = 0;
+      for (int e = 0; e < dh; ++e) d += qbar[hh * dh + e] * keys[static_cast<int64_t>(s) * ldk + hh * dh + e];
+      sc[s] = d * scale;
+      mx = std::max(mx, sc[s]);
+    }
+    double den = 0;
+    for (int s = 0; s < Ms; ++s) den += std::exp(sc[s] - mx);
+    for (int s = 0; s < Ms; ++s) a[s] += std::exp(sc[s] - mx) / den;
+  }
+  for (int s = 0; s < Ms; ++s) wsl[s] = rate * static_cast<float>(a[s] / nh);
+  return wsl;
+}
+
+// rows[s, :] = (1 - w_s) rows[s, :] + w_s * v, rounded to dtype
+void ema_rows(float* rows, int Ms, int64_t n, const float* v, const std::vector<float>& wsl, int dt) {
+  for (int s = 0; s < Ms; ++s)
+    for (int64_t j = 0; j < n; ++j) {
+      float& mv = rows[static_cast<int64_t>(s) * n + j];
+      mv = rnd((1.0f - wsl[s]) * mv + wsl[s] * v[j], dt);
+    }
+}
+
+}  // namespace
+
 extern "C" void orc_memory_store(float* memory, const float* keys, int64_t ldk,
                                  const float* queries, int64_t ldq, int64_t T, const float* state,
                                  int Ms, int H, int nh, float rate, int use_scores, int dtype) {
   // MemoryBank<T>::store / storeStateKernel, src/core/ltm/memory_bank.cu:39-68,242-274
-  const int dh = H / nh;
-  std::vector<float> wsl(Ms, rate);
-  if (use_scores) {
-    std::vector<double> qbar(H, 0.0);
-    for (int64_t t = 0; t < T; ++t)
-      for (int j = 0; j < H; ++j) qbar[j] += queries[t * ldq + j];
-    for (int j = 0; j < H; ++j) qbar[j] /= static_cast<double>(T);
-    std::vector<double> a(Ms, 0.0), sc(Ms);
-    const double scale = 1.0 / std::sqrt(static_cast<double>(dh));
-    for (int hh = 0; hh < nh; ++hh) {
-      double mx = -1e300;
-      for (int s = 0; s < Ms; ++s) {
-        double d = 0;
-        for (int e = 0; e < dh; ++e) d += qbar[hh * dh + e] * keys[static_cast<int64_t>(s) * ldk + hh * dh + e];
-        sc[s] = d * scale;
-        mx = std::max(mx, sc[s]);
-      }
-      double den = 0;
-      for (int s = 0; s < Ms; ++s) den += std::exp(sc[s] - mx);
-      for (int s = 0; s < Ms; ++s) a[s] += std::exp(sc[s] - mx) / den;
-    }
-    for (int s = 0; s < Ms; ++s) wsl[s] = rate * static_cast<float>(a[s] / nh);
-  }
-  for (int s = 0; s < Ms; ++s)
-    for (int j = 0; j < H; ++j) {
-      float& mv = memory[static_cast<int64_t>(s) * H + j];
-      mv = rnd((1.0f - wsl[s]) * mv + wsl[s] * state[j], dtype);
-    }
+  const std::vector<float> wsl = slot_weights(keys, ldk, queries, ldq, T, Ms, H, nh, rate, use_scores);
+  ema_rows(memory, Ms, H, state, wsl, dtype);
 }
 
-extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights* w,
-                                 float* memory_inout, const float* x, float* y, int B, int S) {
-  const int H = c->H, F = c->F, nh = c->nh, dh = c->dh, Ms = c->Ms;
-  const int dt = c->dtype;
-  if (nh * dh != H) return 1;
-  const int64_t T = static_cast<int64_t>(B) * S;
-  const bool ub = c->use_bias != 0;
+namespace {
 
-  // fused projections: [Wq;Wk;Wv;Wqm] and [Wkm;Wvm]
-  std::vector<float> w_qkvm = concat_rows(w->w_qkv, 3 * H, w->w_qm, H, H);
-  std::vector<float> b_qkvm;
-  if (ub) b_qkvm = concat_rows(w->b_qkv, 3 * H, w->b_qm, H, 1);
-  std::vector<float> w_kvm = concat_rows(w->w_km, H, w->w_vm, H, H);
-  std::vector<float> b_kvm;
-  if (ub) b_kvm = concat_rows(w->b_km, H, w->b_vm, H, 1);
+// The block's quantized linears (weights quantized from the fp32 masters).
+struct OrcLins {
+  Lin qkvm, kvm, o, om, g, l1, l2;
+  OrcLins(const orc_block_cfg* c, const orc_block_weights* w) {
+    const int H = c->H, F = c->F, dt = c->dtype;
+    const bool ub = c->use_bias != 0;
+    // fused projections: [Wq;Wk;Wv;Wqm] and [Wkm;Wvm]
+    std::vector<float> w_qkvm = concat_rows(w->w_qkv, 3 * H, w->w_qm, H, H);
+    std::vector<float> b_qkvm;
+    if (ub) b_qkvm = concat_rows(w->b_qkv, 3 * H, w->b_qm, H, 1);
+    std::vector<float> w_kvm = concat_rows(w->w_km, H, w->w_vm, H, H);
+    std::vector<float> b_kvm;
+    if (ub) b_kvm = concat_rows(w->b_km, H, w->b_vm, H, 1);
+    qkvm.init(c->scheme, dt, w_qkvm.data(), ub ? b_qkvm.data() : nullptr, 4 * H, H);
+    kvm.init(c->scheme, dt, w_kvm.data(), ub ? b_kvm.data() : nullptr, 2 * H, H);
+    o.init(c->scheme, dt, w->w_o, ub ? w->b_o : nullptr, H, H);
+    om.init(c->scheme, dt, w->w_om, ub ? w->b_om : nullptr, H, H);
+    g.init(c->scheme, dt, w->w_g, ub ? w->b_g : nullptr, H, H);
+    l1.init(c->scheme, dt, w->w_1, ub ? w->b_1 : nullptr, F, H);
+    l2.init(c->scheme, dt, w->w_2, ub ? w->b_2 : nullptr, H, F);
+  }
+};
 
-  Lin l_qkvm, l_kvm, l_o, l_om, l_g, l_1, l_2;
-  l_qkvm.init(c->scheme, dt, w_qkvm.data(), ub ? b_qkvm.data() : nullptr, 4 * H, H);
-  l_kvm.init(c->scheme, dt, w_kvm.data(), ub ? b_kvm.data() : nullptr, 2 * H, H);
-  l_o.init(c->scheme, dt, w->w_o, ub ? w->b_o : nullptr, H, H);
-  l_om.init(c->scheme, dt, w->w_om, ub ? w->b_om : nullptr, H, H);
-  l_g.init(c->scheme, dt, w->w_g, ub ? w->b_g : nullptr, H, H);
-  l_1.init(c->scheme, dt, w->w_1, ub ? w->b_1 : nullptr, F, H);
-  l_2.init(c->scheme, dt, w->w_2, ub ? w->b_2 : nullptr, H, F);
-
-  // 1. h = LN1(x + x)
+// h = LN1(x + x); qkvm = h [Wq;Wk;Wv;Wqm]^T + b with RoPE on the Q and K
+// columns at position pos0 + (t % S) of row t; rounded to dtype.
+std::vector<float> qkvm_rows(const orc_block_cfg* c, const orc_block_weights* w, const OrcLins& L,
+                             const float* x, int64_t T, int S, int pos0) {
+  const int H = c->H, dh = c->dh, dt = c->dtype;
   std::vector<float> h(T * H);
   if (c->use_layer_norm)
     orc_layernorm_x2(x, T, H, w->ln1_g, w->ln1_b, h.data());
   else
     std::memcpy(h.data(), x, sizeof(float) * T * H);
   if (c->scheme != ORC_W8A8) orc_round(h.data(), T * H, dt);
-
-  // 2. fused Q | K | V | Qm projection, RoPE on Q and K
   std::vector<float> qkvm(T * 4 * H);
-  l_qkvm.apply(h.data(), T, qkvm.data(), ORC_ACT_NONE);
+  L.qkvm.apply(h.data(), T, qkvm.data(), ORC_ACT_NONE);
   if (c->use_rotary) {
-    std::vector<float> tab(static_cast<size_t>(S) * dh);
-    orc_rope_table(S, dh, tab.data());
+    std::vector<float> tab(static_cast<size_t>(pos0 + S) * dh);
+    orc_rope_table(pos0 + S, dh, tab.data());
 #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; ++t) {
-      const int pos = static_cast<int>(t % S);
+      const int pos = pos0 + static_cast<int>(t % S);
       float* row = qkvm.data() + t * 4 * H;
       for (int col = 0; col < 2 * H; col += 2) {
         const int i = (col % dh) / 2;
@@ -421,39 +440,41 @@ extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights
     }
   }
   orc_round(qkvm.data(), T * 4 * H, dt);
+  return qkvm;
+}
 
-  // 3. memory keys/values from the bank
-  std::vector<float> kvm(static_cast<size_t>(Ms) * 2 * H);
-  l_kvm.apply(memory_inout, Ms, kvm.data(), ORC_ACT_NONE);
-  orc_round(kvm.data(), static_cast<int64_t>(Ms) * 2 * H, dt);
+// K_M | V_M = M [Wkm;Wvm]^T + b, rounded: [Ms, 2H]
+std::vector<float> kvm_rows(const orc_block_cfg* c, const OrcLins& L, const float* memory) {
+  std::vector<float> kvm(static_cast<size_t>(c->Ms) * 2 * c->H);
+  L.kvm.apply(memory, c->Ms, kvm.data(), ORC_ACT_NONE);
+  orc_round(kvm.data(), static_cast<int64_t>(c->Ms) * 2 * c->H, c->dtype);
+  return kvm;
+}
 
-  // 4. causal self-attention and memory attention
-  std::vector<float> os(T * H), om(T * H);
-  orc_attention(qkvm.data(), 4 * H, qkvm.data() + H, qkvm.data() + 2 * H, 4 * H, B, S, S, S, nh,
-                dh, 1, dt, os.data(), H);
-  orc_attention(qkvm.data() + 3 * H, 4 * H, kvm.data(), kvm.data() + H, 2 * H, B, S, Ms, 0, nh, dh,
-                0, dt, om.data(), H);
-
-  // 5. output projections
+// Steps after the attentions: output projections, gated memory integration
+// and FFN with residual; returns the gate g (fp32, [T, H]) when gating is on.
+std::vector<float> block_tail(const orc_block_cfg* c, const orc_block_weights* w, const OrcLins& L,
+                              const float* x, std::vector<float>& os, std::vector<float>& om,
+                              int64_t T, float* y) {
+  const int H = c->H, F = c->F, dt = c->dtype;
+  // output projections
   std::vector<float> sp(T * H), mp(T * H);
-  l_o.apply(os.data(), T, sp.data(), ORC_ACT_NONE);
+  L.o.apply(os.data(), T, sp.data(), ORC_ACT_NONE);
   orc_round(sp.data(), T * H, dt);
-  l_om.apply(om.data(), T, mp.data(), ORC_ACT_NONE);
+  L.om.apply(om.data(), T, mp.data(), ORC_ACT_NONE);
   orc_round(mp.data(), T * H, dt);
-
-  // 6. gated memory integration y = s + g*m + (1-g)*x
+  // gated memory integration y = s + g*m + (1-g)*x
   std::vector<float> yv(T * H), g;
   if (c->use_memory_gating) {
     g.resize(T * H);
-    l_g.apply(x, T, g.data(), ORC_ACT_SIGMOID);
+    L.g.apply(x, T, g.data(), ORC_ACT_SIGMOID);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < T * H; ++i) yv[i] = rnd(sp[i] + g[i] * mp[i] + (1.0f - g[i]) * x[i], dt);
   } else {
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < T * H; ++i) yv[i] = rnd(sp[i] + mp[i] + x[i], dt);
   }
-
-  // 7. FFN with residual: out = y + W2 GELU(W1 LN2(y) + b1) + b2
+  // FFN with residual: out = y + W2 GELU(W1 LN2(y) + b1) + b2
   std::vector<float> z(T * H);
   if (c->use_layer_norm)
     orc_layernorm_x2(yv.data(), T, H, w->ln2_g, w->ln2_b, z.data());
@@ -461,24 +482,139 @@ extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights
     std::memcpy(z.data(), yv.data(), sizeof(float) * T * H);
   if (c->scheme != ORC_W8A8) orc_round(z.data(), T * H, dt);
   std::vector<float> u(T * static_cast<int64_t>(F));
-  l_1.apply(z.data(), T, u.data(), ORC_ACT_GELU);
+  L.l1.apply(z.data(), T, u.data(), ORC_ACT_GELU);
   orc_round(u.data(), T * F, dt);
   std::vector<float> f(T * H);
-  l_2.apply(u.data(), T, f.data(), ORC_ACT_NONE);
+  L.l2.apply(u.data(), T, f.data(), ORC_ACT_NONE);
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < T * H; ++i) y[i] = rnd(f[i] + yv[i], dt);
+  return g;
+}
 
-  // 8. memory write after the read (optional)
-  if (c->memory_write && c->use_memory_gating) {
-    std::vector<double> cacc(H, 0.0);
-    for (int64_t t = 0; t < T; ++t)
-      for (int j = 0; j < H; ++j) cacc[j] += static_cast<double>(g[t * H + j]) * x[t * H + j];
-    std::vector<float> state(H);
-    for (int j = 0; j < H; ++j) state[j] = static_cast<float>(cacc[j] / static_cast<double>(T));
-    orc_memory_store(memory_inout, kvm.data(), 2 * H, qkvm.data() + 3 * H, 4 * H, T, state.data(),
-                     Ms, H, nh, c->update_rate, c->use_attention_scores, dt);
+// Memory write after the read: state c = mean_t g_t * x_t; slot weights from
+// the memory queries against K_M (before the write); the bank's EMA, and with
+// kvm_follow the same EMA of K_M | V_M towards c [Wkm;Wvm]^T + b (the decode
+// step keeps K_M | V_M resident instead of recomputing them from the bank).
+void block_write(const orc_block_cfg* c, const OrcLins& L, float* memory, float* kvm,
+                 const float* qm, int64_t ldq, const std::vector<float>& g, const float* x,
+                 int64_t T, bool kvm_follow) {
+  const int H = c->H, Ms = c->Ms, dt = c->dtype;
+  std::vector<double> cacc(H, 0.0);
+  for (int64_t t = 0; t < T; ++t)
+    for (int j = 0; j < H; ++j) cacc[j] += static_cast<double>(g[t * H + j]) * x[t * H + j];
+  std::vector<float> state(H);
+  for (int j = 0; j < H; ++j) state[j] = static_cast<float>(cacc[j] / static_cast<double>(T));
+  const std::vector<float> wsl =
+      slot_weights(kvm, 2 * H, qm, ldq, T, Ms, H, c->nh, c->update_rate, c->use_attention_scores);
+  ema_rows(memory, Ms, H, state.data(), wsl, dt);
+  if (kvm_follow) {
+    std::vector<float> crow(state);
+    orc_round(crow.data(), H, dt);
+    std::vector<float> kc(2 * H);
+    L.kvm.apply(crow.data(), 1, kc.data(), ORC_ACT_NONE);
+    orc_round(kc.data(), 2 * H, dt);
+    ema_rows(kvm, Ms, 2 * H, kc.data(), wsl, dt);
   }
+}
+
+}  // namespace
+
+extern "C" int orc_block_forward_kv(const orc_block_cfg* c, const orc_block_weights* w,
+                                    float* memory_inout, const float* x, float* y, int B, int S,
+                                    float* kv_out) {
+  const int H = c->H, nh = c->nh, dh = c->dh, Ms = c->Ms;
+  const int dt = c->dtype;
+  if (nh * dh != H) return 1;
+  const int64_t T = static_cast<int64_t>(B) * S;
+  OrcLins L(c, w);
+  // 1-2. LN1, fused Q | K | V | Qm projection, RoPE on Q and K
+  std::vector<float> qkvm = qkvm_rows(c, w, L, x, T, S, 0);
+  if (kv_out)
+    for (int64_t t = 0; t < T; ++t)
+      std::memcpy(kv_out + t * 2 * H, qkvm.data() + t * 4 * H + H, sizeof(float) * 2 * H);
+  // 3. memory keys/values from the bank
+  std::vector<float> kvm = kvm_rows(c, L, memory_inout);
+  // 4. causal self-attention and memory attention
+  std::vector<float> os(T * H), om(T * H);
+  orc_attention(qkvm.data(), 4 * H, qkvm.data() + H, qkvm.data() + 2 * H, 4 * H, B, S, S, S, nh,
+                dh, 1, dt, os.data(), H);
+  orc_attention(qkvm.data() + 3 * H, 4 * H, kvm.data(), kvm.data() + H, 2 * H, B, S, Ms, 0, nh, dh,
+                0, dt, om.data(), H);
+  // 5-7. output projections, gated integration, FFN with residual
+  std::vector<float> g = block_tail(c, w, L, x, os, om, T, y);
+  // 8. memory write after the read (optional)
+  if (c->memory_write && c->use_memory_gating)
+    block_write(c, L, memory_inout, kvm.data(), qkvm.data() + 3 * H, 4 * H, g, x, T, false);
   return 0;
+}
+
+extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights* w,
+                                 float* memory_inout, const float* x, float* y, int B, int S) {
+  return orc_block_forward_kv(c, w, memory_inout, x, y, B, S, nullptr);
+}
+
+extern "C" int orc_block_kvm(const orc_block_cfg* c, const orc_block_weights* w,
+                             const float* memory, float* kvm_out) {
+  if (c->nh * c->dh != c->H) return 1;
+  OrcLins L(c, w);
+  const std::vector<float> kvm = kvm_rows(c, L, memory);
+  std::memcpy(kvm_out, kvm.data(), sizeof(float) * kvm.size());
+  return 0;
+}
+
+namespace {
+
+int decode_step(const orc_block_cfg* c, const orc_block_weights* w, const OrcLins& L,
+                float* memory_inout, float* kvm_inout, const float* x, float* k_cache,
+                float* v_cache, int64_t max_positions, int cache_len, int B, float* y) {
+  const int H = c->H, nh = c->nh, dh = c->dh, Ms = c->Ms;
+  const int dt = c->dtype;
+  if (nh * dh != H) return 1;
+  if (cache_len < 0 || cache_len >= max_positions) return 2;
+  // the new token of every sequence sits at position cache_len
+  std::vector<float> qkvm = qkvm_rows(c, w, L, x, B, 1, cache_len);
+  for (int b = 0; b < B; ++b) {
+    const int64_t dst = (static_cast<int64_t>(b) * max_positions + cache_len) * H;
+    std::memcpy(k_cache + dst, qkvm.data() + static_cast<int64_t>(b) * 4 * H + H, sizeof(float) * H);
+    std::memcpy(v_cache + dst, qkvm.data() + static_cast<int64_t>(b) * 4 * H + 2 * H, sizeof(float) * H);
+  }
+  // self-attention of the new token over positions [0, cache_len]; memory
+  // attention against the resident K_M | V_M
+  std::vector<float> os(B * static_cast<int64_t>(H)), om(B * static_cast<int64_t>(H));
+  orc_attention(qkvm.data(), 4 * H, k_cache, v_cache, H, B, 1, cache_len + 1,
+                static_cast<int>(max_positions), nh, dh, 0, dt, os.data(), H);
+  orc_attention(qkvm.data() + 3 * H, 4 * H, kvm_inout, kvm_inout + H, 2 * H, B, 1, Ms, 0, nh, dh, 0,
+                dt, om.data(), H);
+  std::vector<float> g = block_tail(c, w, L, x, os, om, B, y);
+  if (c->memory_write && c->use_memory_gating)
+    block_write(c, L, memory_inout, kvm_inout, qkvm.data() + 3 * H, 4 * H, g, x, B, true);
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int orc_block_decode_step(const orc_block_cfg* c, const orc_block_weights* w,
+                                     float* memory_inout, float* kvm_inout, const float* x,
+                                     float* k_cache, float* v_cache, int64_t max_positions,
+                                     int cache_len, int B, float* y) {
+  OrcLins L(c, w);
+  return decode_step(c, w, L, memory_inout, kvm_inout, x, k_cache, v_cache, max_positions,
+                     cache_len, B, y);
+}
+
+extern "C" void* orc_block_prepare(const orc_block_cfg* c, const orc_block_weights* w) {
+  return new OrcLins(c, w);
+}
+
+extern "C" void orc_block_release(void* prepared) { delete static_cast<OrcLins*>(prepared); }
+
+extern "C" int orc_block_decode_step_prepared(const void* prepared, const orc_block_cfg* c,
+                                              const orc_block_weights* w, float* memory_inout,
+                                              float* kvm_inout, const float* x, float* k_cache,
+                                              float* v_cache, int64_t max_positions,
+                                              int cache_len, int B, float* y) {
+  return decode_step(c, w, *static_cast<const OrcLins*>(prepared), memory_inout, kvm_inout, x,
+                     k_cache, v_cache, max_positions, cache_len, B, y);
 }
 
 extern "C" int orc_model_forward(const orc_block_cfg* c, const orc_block_weights* w, float** banks,

@@ -95,6 +95,35 @@ typedef struct orc_block_weights {
 int orc_block_forward(const orc_block_cfg* c, const orc_block_weights* w, float* memory_inout,
                       const float* x, float* y, int B, int S);
 
+/* orc_block_forward that also writes the post-RoPE K | V rows of every token
+ * ([B*S, 2H], rounded) into kv_out when it is not NULL. */
+int orc_block_forward_kv(const orc_block_cfg* c, const orc_block_weights* w, float* memory_inout,
+                         const float* x, float* y, int B, int S, float* kv_out);
+
+/* K_M | V_M of a bank: [Ms, 2H], rounded. */
+int orc_block_kvm(const orc_block_cfg* c, const orc_block_weights* w, const float* memory,
+                  float* kvm_out);
+
+/* One decode step: x, y [B, H] (one new token per sequence, all at position
+ * cache_len); k_cache, v_cache [B, max_positions, H] hold positions
+ * [0, cache_len) and receive the new token's K, V at cache_len; kvm_inout
+ * [Ms, 2H] is the resident K_M | V_M.  With memory_write the bank and K_M |
+ * V_M follow the same EMA (K_M | V_M towards c [Wkm;Wvm]^T + b). */
+int orc_block_decode_step(const orc_block_cfg* c, const orc_block_weights* w, float* memory_inout,
+                          float* kvm_inout, const float* x, float* k_cache, float* v_cache,
+                          int64_t max_positions, int cache_len, int B, float* y);
+
+/* The block's quantized linears made once (orc_block_prepare) for repeated
+ * decode steps (the same step as orc_block_decode_step; w still supplies the
+ * LayerNorm parameters). */
+void* orc_block_prepare(const orc_block_cfg* c, const orc_block_weights* w);
+void orc_block_release(void* prepared);
+int orc_block_decode_step_prepared(const void* prepared, const orc_block_cfg* c,
+                                   const orc_block_weights* w, float* memory_inout,
+                                   float* kvm_inout, const float* x, float* k_cache,
+                                   float* v_cache, int64_t max_positions, int cache_len, int B,
+                                   float* y);
+
 /* Embedding gather + n_layers blocks (weights[l], banks[l]).  tokens [B*S]. */
 int orc_model_forward(const orc_block_cfg* c, const orc_block_weights* w, float** banks,
                       int n_layers, const float* embedding, int vocab, const int32_t* tokens,

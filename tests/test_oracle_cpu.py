@@ -169,3 +169,28 @@ def test_golden_fixtures(orc):
             np.testing.assert_array_equal(got[k], want[k], err_msg=k)
         else:
             np.testing.assert_allclose(got[k], want[k], rtol=1e-6, atol=1e-6, err_msg=k)
+
+
+def test_oracle_decode_step_is_last_row_of_forward(orc):
+    """The oracle's decode step over a cache holding its own prefix keys /
+    values reproduces the last row of its causal forward (and appends that
+    row's K | V)."""
+    from ltm_b200 import synthetic
+    for scheme, dt in ((1, 1), (2, 2)):
+        H, nh, F, Ms, B, L, P = 128, 2, 256, 32, 2, 9, 12
+        S = L + 1
+        ocfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=scheme, dtype=dt, memory_write=0,
+                    use_attention_scores=1, update_rate=0.9)
+        w = synthetic.block_weights(H, F, Ms, 3)
+        x = orc.round_to(synthetic.activations(B * S, H, 4), dt)
+        y, _, kv = orc.block_forward(ocfg, w, x, B, S, return_kv=True)
+        kv = kv.reshape(B, S, 2 * H)
+        kc = np.zeros((B, P, H), np.float32)
+        vc = np.zeros((B, P, H), np.float32)
+        kc[:, :L], vc[:, :L] = kv[:, :L, :H], kv[:, :L, H:]
+        mem = orc.round_to(w["memory"], dt)
+        kvm = orc.block_kvm(ocfg, w, mem)
+        yd = orc.block_decode_step(ocfg, w, x.reshape(B, S, H)[:, L], kc, vc, L, mem, kvm)
+        np.testing.assert_array_equal(yd, y.reshape(B, S, H)[:, L])
+        np.testing.assert_array_equal(kc[:, L], kv[:, L, :H])
+        np.testing.assert_array_equal(vc[:, L], kv[:, L, H:])
