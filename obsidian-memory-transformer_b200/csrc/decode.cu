@@ -7,27 +7,45 @@
 // parallelism), head h at columns h*D; position p of sequence b at
 // cache + b * seq_stride + p * width.
 //
-// Attention of one query row per (sequence, head) over L cached positions:
-// the positions are split into chunks of kChunk; a 128-thread CTA reads one
-// chunk of one (sequence, head): 4 warps x 4 key groups of 8 lanes, lane l of
-// a group holding dims [l*D/8, (l+1)*D/8) of q, of the running output and of
-// the key / value rows it reads (each group reads whole rows, the 4 groups of
-// a warp consecutive rows).  Scores are reduced across the group's 8 lanes;
-// every group keeps its own online-softmax state (max, sum, output), combined
-// across the groups and warps of the CTA into one partial (max, sum, output)
-// per chunk; decode_combine_kernel merges the chunks.  Every key and value
-// byte is read once.
+// Attention of one query row per (sequence, head) over L cached positions
+// (flash decoding): the positions are split into chunks of kDChunk (the work
+// items, one partial (max, sum, output) each); a persistent grid of one CTA
+// per SM walks its share of the work items.  In each CTA warp 0 streams
+// 64-position K and V tiles of the items (TMA, box [64 rows x head_dim]) into
+// a ring of shared-memory stages that never drains between items, and 8
+// consumer warps run the online softmax: each takes 8 rows of a tile as 4
+// groups of 8 lanes x 2 keys, lane l of a group holding the dims
+// c*64 + l*8 .. +7 of q, of the output and of the rows it reads (one 16-byte
+// shared load per lane and half row, 128 contiguous bytes per 8 lanes: no
+// bank conflicts).  Scores are reduced over the group's 8 lanes; each group
+// keeps its own (max, sum, output), merged over the warp and then over the 8
+// warps at the end of an item.  decode_combine_kernel merges the chunks.
+// Every key and value byte is read from HBM once.
 //
-// Replaces the KV-cache decode stubs of the reference
-// (python_bindings/src/main.cpp:101-135, python_bindings/ltm/inference.py:101-128)
-// with the attention of flash_attention.cu:241 (scale 1/sqrt(head_dim)).
 #include "block.cuh"
 
 namespace ltm_b200 {
 namespace {
 
-constexpr int kChunk = 512;  // cache positions per CTA
-constexpr int kKB = 4;       // keys per group per step
+constexpr int kDChunk = 1024;  // cache positions per work item
+constexpr int kDTile = 64;     // cache positions per TMA tile
+constexpr int kDCons = 8;      // consumer warps
+constexpr int kDKeys = kDTile / (kDCons * 4);  // keys per lane group per tile
+
+// Shared memory of the decode kernel: the K | V stages, their full / empty
+// barriers, the abort flag and the per-item merge scratch (double-buffered by
+// item parity).
+template <int D>
+struct DecSmem {
+  static constexpr int kTile = kDTile * D * 2;              // one K or V tile (16-bit)
+  static constexpr int kStages = D == 128 ? 6 : 12;         // 192 KiB of stages
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kOffBar = kStages * kStage;
+  static constexpr int kOffFlag = kOffBar + 2 * kStages * 8;
+  static constexpr int kOffMerge = (kOffFlag + 16 + 15) / 16 * 16;
+  static constexpr int kMerge = 2 * kDCons * (D + 2) * 4;
+  static constexpr int kBytes = kOffMerge + kMerge + 1024;  // + alignment slack
+};
 
 // Dims of a head row held by lane gl of an 8-lane group: for each 64-dim half
 // c, the 8 consecutive dims c*64 + gl*8 .. +7, so one 16-byte load per lane
@@ -63,113 +81,189 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const T* __restrict__ qk
   }
 }
 
+__device__ __forceinline__ void consumer_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kDCons * 32) : "memory");
+}
+
 template <class T, int D>
-__global__ void __launch_bounds__(128) decode_attn_kernel(
-    const T* __restrict__ q, int64_t ldq, const T* __restrict__ kc, const T* __restrict__ vc,
-    int64_t seq_stride, int width, int L, float sl2, float* __restrict__ part, int nchunk) {
+__global__ void __launch_bounds__(32 * (kDCons + 1), 1) decode_attn_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    const T* __restrict__ q, int64_t ldq, int L, int P, int nh, int nchunk, int items, float sl2,
+    float* __restrict__ part, int* err) {
+  using S = DecSmem<D>;
   constexpr int DL = D / 8;  // dims per lane
-  __shared__ float sm[4][D + 2];
-  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  constexpr int NS = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
+  uint64_t* empty = full + NS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kOffFlag);
+  float* merge = reinterpret_cast<float*>(smem + S::kOffMerge);  // [2][kDCons][D + 2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int grp = lane >> 3, gl = lane & 7;
-  float qv[DL];
-  load_row_part<T, DL>(q + b * ldq + h * D, gl, qv);
-  const T* kb = kc + b * seq_stride + h * D;
-  const T* vb = vc + b * seq_stride + h * D;
-  const int c0 = chunk * kChunk;
-  const int c1 = min(L, c0 + kChunk);
-  const int w0 = c0 + warp * (kChunk / 4);  // this warp's 128 positions
-  float m = -INFINITY, l = 0.0f, o[DL];
-#pragma unroll
-  for (int i = 0; i < DL; ++i) o[i] = 0.0f;
-  for (int i0 = 0; i0 < kChunk / 4; i0 += 4 * kKB) {
-    float s[kKB];
-    float vv[kKB][DL];
-    bool valid[kKB];
-#pragma unroll
-    for (int j = 0; j < kKB; ++j) {
-      const int k = w0 + i0 + 4 * j + grp;  // the warp's 4 groups read 4 consecutive rows
-      valid[j] = k < c1;
-      float kr[DL];
-      if (valid[j]) {
-        load_row_part<T, DL>(kb + static_cast<int64_t>(k) * width, gl, kr);
-        load_row_part<T, DL>(vb + static_cast<int64_t>(k) * width, gl, vv[j]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < DL; ++i) kr[i] = vv[j][i] = 0.0f;
-      }
-      float d = 0.0f;
-#pragma unroll
-      for (int i = 0; i < DL; ++i) d = fmaf(qv[i], kr[i], d);
-      s[j] = d;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, kDCons);
     }
-#pragma unroll
-    for (int j = 0; j < kKB; ++j) {  // sum over the group's 8 lanes
-      s[j] += __shfl_xor_sync(0xffffffffu, s[j], 1);
-      s[j] += __shfl_xor_sync(0xffffffffu, s[j], 2);
-      s[j] += __shfl_xor_sync(0xffffffffu, s[j], 4);
-      if (!valid[j]) s[j] = -INFINITY;
-    }
-    float mb = s[0];
-#pragma unroll
-    for (int j = 1; j < kKB; ++j) mb = fmaxf(mb, s[j]);
-    // no branch on the group's state: the shuffles above need the whole warp
-    const float m_new = fmaxf(m, mb);
-    const float mu = (m_new == -INFINITY) ? 0.0f : m_new;  // nothing visible yet
-    const float corr = ex2_approx((m - mu) * sl2);  // m = -inf -> 0
-    l *= corr;
-#pragma unroll
-    for (int i = 0; i < DL; ++i) o[i] *= corr;
-#pragma unroll
-    for (int j = 0; j < kKB; ++j) {
-      const float pj = ex2_approx((s[j] - mu) * sl2);  // -inf -> 0
-      l += pj;
-#pragma unroll
-      for (int i = 0; i < DL; ++i) o[i] = fmaf(pj, vv[j][i], o[i]);
-    }
-    m = m_new;
-  }
-  // merge the warp's 4 groups (lanes gl, gl+8, gl+16, gl+24 hold the same dims)
-  float mw = m;
-  mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, 8));
-  mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, 16));
-  const float f = (mw == -INFINITY) ? 0.0f : ex2_approx((m - mw) * sl2);
-  l *= f;
-#pragma unroll
-  for (int i = 0; i < DL; ++i) o[i] *= f;
-  l += __shfl_xor_sync(0xffffffffu, l, 8);
-  l += __shfl_xor_sync(0xffffffffu, l, 16);
-#pragma unroll
-  for (int i = 0; i < DL; ++i) {
-    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
-    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
-  }
-  if (grp == 0) {
-#pragma unroll
-    for (int i = 0; i < DL; ++i) sm[warp][part_dim(gl, i)] = o[i];
-    if (gl == 0) {
-      sm[warp][D] = mw;
-      sm[warp][D + 1] = l;
-    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
   }
   __syncthreads();
-  // merge the 4 warps; thread t < D writes output dim t of the chunk's partial
-  if (threadIdx.x < D) {
-    float mc = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) mc = fmaxf(mc, sm[w][D]);
-    float lc = 0.0f, oc = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float g = (mc == -INFINITY) ? 0.0f : ex2_approx((sm[w][D] - mc) * sl2);
-      lc += sm[w][D + 1] * g;
-      oc += sm[w][threadIdx.x] * g;
+
+  if (warp == 0) {
+    // ---- producer: K | V tiles of this CTA's items into the ring
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+        const int c = w % nchunk, bh = w / nchunk;
+        const int h = bh % nh, b = bh / nh;
+        const int c0 = c * kDChunk, c1 = min(L, c0 + kDChunk);
+        const int nt = (c1 - c0 + kDTile - 1) / kDTile;
+        for (int t = 0; t < nt; ++t, ++it) {
+          const int st = it % NS;
+          if (!mbar_wait_bounded(empty + st, ((it / NS) & 1) ^ 1, abort_flag, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + st, S::kStage);
+          uint8_t* dst = smem + st * S::kStage;
+          const int row = b * P + c0 + t * kDTile;
+          tma_load_2d(dst, &tmK, full + st, h * D, row);
+          tma_load_2d(dst + S::kTile, &tmV, full + st, h * D, row);
+        }
+      }
+      if (!ok) {  // let the copies in flight land before the CTA exits
+        volatile int never = 0;
+        for (int j = (it > NS ? it - NS : 0); j < it; ++j)
+          mbar_wait_bounded(full + j % NS, (j / NS) & 1, &never, err, kErrWaitOther);
+      }
     }
-    float* pp = part + ((static_cast<int64_t>(b) * gridDim.y + h) * nchunk + chunk) * (D + 2);
-    pp[threadIdx.x] = oc;
-    if (threadIdx.x == 0) {
-      pp[D] = mc;
-      pp[D + 1] = lc;
+    return;
+  }
+
+  // ---- consumers
+  const int cw = warp - 1;
+  const int grp = lane >> 3, gl = lane & 7;
+  int it = 0, parity = 0;
+  for (int w = blockIdx.x; w < items; w += gridDim.x, parity ^= 1) {
+    const int c = w % nchunk, bh = w / nchunk;
+    const int h = bh % nh, b = bh / nh;
+    const int c0 = c * kDChunk, c1 = min(L, c0 + kDChunk);
+    const int nt = (c1 - c0 + kDTile - 1) / kDTile;
+    float qv[DL];
+    load_row_part<T, DL>(q + b * ldq + h * D, gl, qv);
+    float m = -INFINITY, l = 0.0f, o[DL];
+#pragma unroll
+    for (int i = 0; i < DL; ++i) o[i] = 0.0f;
+    for (int t = 0; t < nt; ++t, ++it) {
+      const int st = it % NS;
+      bool ok = mbar_wait_bounded(full + st, (it / NS) & 1, abort_flag, err, kErrWaitFull);
+      if (!__all_sync(0xffffffffu, ok)) return;
+      const T* tk = reinterpret_cast<const T*>(smem + st * S::kStage);
+      const T* tv = reinterpret_cast<const T*>(smem + st * S::kStage + S::kTile);
+      float sc[kDKeys];
+      float vv[kDKeys][DL];
+      bool valid[kDKeys];
+#pragma unroll
+      for (int j = 0; j < kDKeys; ++j) {
+        const int r = cw * (4 * kDKeys) + 4 * j + grp;  // row of the tile
+        valid[j] = c0 + t * kDTile + r < c1;
+        float kr[DL];
+#pragma unroll
+        for (int hh = 0; hh < DL / 8; ++hh) {
+          const uint4 kraw = *reinterpret_cast<const uint4*>(tk + r * D + hh * 64 + gl * 8);
+          const uint4 vraw = *reinterpret_cast<const uint4*>(tv + r * D + hh * 64 + gl * 8);
+          const T* ke = reinterpret_cast<const T*>(&kraw);
+          const T* ve = reinterpret_cast<const T*>(&vraw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            kr[hh * 8 + i] = to_f32(ke[i]);
+            // rows past the cache may hold anything: they contribute 0 * nothing
+            vv[j][hh * 8 + i] = valid[j] ? to_f32(ve[i]) : 0.0f;
+          }
+        }
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) d = fmaf(qv[i], kr[i], d);
+        sc[j] = d;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + st);  // the stage's bytes are in registers
+#pragma unroll
+      for (int j = 0; j < kDKeys; ++j) {  // sum over the group's 8 lanes
+        sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 1);
+        sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 2);
+        sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], 4);
+        if (!valid[j]) sc[j] = -INFINITY;
+      }
+      float mb = sc[0];
+#pragma unroll
+      for (int j = 1; j < kDKeys; ++j) mb = fmaxf(mb, sc[j]);
+      // no branch on the group's state: the shuffles above need the whole warp
+      const float m_new = fmaxf(m, mb);
+      const float mu = (m_new == -INFINITY) ? 0.0f : m_new;  // nothing visible yet
+      const float corr = ex2_approx((m - mu) * sl2);          // m = -inf -> 0
+      l *= corr;
+#pragma unroll
+      for (int i = 0; i < DL; ++i) o[i] *= corr;
+#pragma unroll
+      for (int j = 0; j < kDKeys; ++j) {
+        const float pj = ex2_approx((sc[j] - mu) * sl2);  // -inf -> 0
+        l += pj;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) o[i] = fmaf(pj, vv[j][i], o[i]);
+      }
+      m = m_new;
+    }
+    // merge the warp's 4 groups (lanes gl, gl+8, gl+16, gl+24 hold the same dims)
+    float mw = m;
+    mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, 8));
+    mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, 16));
+    const float f = (mw == -INFINITY) ? 0.0f : ex2_approx((m - mw) * sl2);
+    l *= f;
+#pragma unroll
+    for (int i = 0; i < DL; ++i) o[i] *= f;
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+#pragma unroll
+    for (int i = 0; i < DL; ++i) {
+      o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
+      o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
+    }
+    float* mg = merge + parity * (kDCons * (D + 2));
+    if (grp == 0) {
+#pragma unroll
+      for (int i = 0; i < DL; ++i) mg[cw * (D + 2) + part_dim(gl, i)] = o[i];
+      if (gl == 0) {
+        mg[cw * (D + 2) + D] = mw;
+        mg[cw * (D + 2) + D + 1] = l;
+      }
+    }
+    consumer_bar_sync();  // merge scratch of this parity complete; the other parity is free
+    // merge the warps; consumer thread ct < D writes output dim ct of the item's partial
+    const int ct = threadIdx.x - 32;
+    if (ct < D) {
+      float mc = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kDCons; ++k) mc = fmaxf(mc, mg[k * (D + 2) + D]);
+      float lc = 0.0f, oc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kDCons; ++k) {
+        const float g = (mc == -INFINITY) ? 0.0f : ex2_approx((mg[k * (D + 2) + D] - mc) * sl2);
+        lc += mg[k * (D + 2) + D + 1] * g;
+        oc += mg[k * (D + 2) + ct] * g;
+      }
+      float* pp = part + static_cast<int64_t>(w) * (D + 2);
+      pp[ct] = oc;
+      if (ct == 0) {
+        pp[D] = mc;
+        pp[D + 1] = lc;
+      }
     }
   }
 }
@@ -195,7 +289,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
 }  // namespace
 
 size_t decode_partials_bytes(int B, int nh, int D, int64_t L) {
-  const int64_t nchunk = (L + kChunk - 1) / kChunk;
+  const int64_t nchunk = (L + kDChunk - 1) / kDChunk;
   return static_cast<size_t>(B) * nh * nchunk * (D + 2) * sizeof(float);
 }
 
@@ -217,28 +311,40 @@ void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const v
   LTM_REQUIRE(D == 64 || D == 128, "decode attention head_dim must be 64 or 128");
   LTM_REQUIRE(L >= 1, "empty cache");
   LTM_REQUIRE(dt != LTM_DTYPE_F32, "decode attention needs 16-bit activations");
-  const int nchunk = (L + kChunk - 1) / kChunk;
+  LTM_REQUIRE(seq_stride % width == 0, "sequence stride must be whole cache rows");
+  const int64_t P = seq_stride / width;
+  LTM_REQUIRE(static_cast<int64_t>(B) * P < (1ll << 31), "cache rows exceed int32");
+  const int nchunk = (L + kDChunk - 1) / kDChunk;
+  const int items = B * nh * nchunk;
   const float sl2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  const CUtensorMapDataType tdt =
+      dt == LTM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tk, tv;
+  make_tma_2d(&tk, kc, tdt, 2, static_cast<uint64_t>(B) * P, width, width, D, kDTile,
+              CU_TENSOR_MAP_SWIZZLE_NONE);
+  make_tma_2d(&tv, vc, tdt, 2, static_cast<uint64_t>(B) * P, width, width, D, kDTile,
+              CU_TENSOR_MAP_SWIZZLE_NONE);
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (!std::is_same<T, float>::value) {
-      dim3 grid(nchunk, nh, B);
-      if (D == 64) {
-        decode_attn_kernel<T, 64><<<grid, 128, 0, st>>>(
-            static_cast<const T*>(q), ldq, static_cast<const T*>(kc), static_cast<const T*>(vc),
-            seq_stride, width, L, sl2, part, nchunk);
+      auto run = [&](auto dtag) {
+        constexpr int DD = decltype(dtag)::value;
+        auto kern = decode_attn_kernel<T, DD>;
+        constexpr int smem = DecSmem<DD>::kBytes;
+        LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        const int grid = persistent_grid(kern, 32 * (kDCons + 1), smem, items);
+        kern<<<grid, 32 * (kDCons + 1), smem, st>>>(tk, tv, static_cast<const T*>(q), ldq, L,
+                                                    static_cast<int>(P), nh, nchunk, items, sl2,
+                                                    part, device_error_ptr());
         check_launch("decode_attn_kernel", st);
-        decode_combine_kernel<T, 64><<<dim3(nh, B), 64, 0, st>>>(part, nchunk, sl2,
+        decode_combine_kernel<T, DD><<<dim3(nh, B), DD, 0, st>>>(part, nchunk, sl2,
                                                                  static_cast<T*>(o), ldo);
-      } else {
-        decode_attn_kernel<T, 128><<<grid, 128, 0, st>>>(
-            static_cast<const T*>(q), ldq, static_cast<const T*>(kc), static_cast<const T*>(vc),
-            seq_stride, width, L, sl2, part, nchunk);
-        check_launch("decode_attn_kernel", st);
-        decode_combine_kernel<T, 128><<<dim3(nh, B), 128, 0, st>>>(part, nchunk, sl2,
-                                                                   static_cast<T*>(o), ldo);
-      }
-      check_launch("decode_combine_kernel", st);
+        check_launch("decode_combine_kernel", st);
+      };
+      if (D == 64)
+        run(std::integral_constant<int, 64>{});
+      else
+        run(std::integral_constant<int, 128>{});
     }
   });
 }

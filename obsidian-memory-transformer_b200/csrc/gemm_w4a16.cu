@@ -14,7 +14,16 @@
 //               the T weight tile in the UMMA K-major 128-byte-swizzled layout,
 //               fence it to the async proxy; then the fused epilogue
 // All waits are bounded (common.cuh).
+//
+// Split-K for grids smaller than the GPU (decode, M <= 128): CTA z of the
+// grid's third dimension reduces the K-blocks [z*kps, (z+1)*kps) and dumps its
+// raw fp32 accumulator tile to partials[z] (the int32 store mode of the
+// epilogue, bit for bit); splitk_epilogue_kernel sums the slices in order and
+// applies the fused epilogue.
+#include <memory>
+#include <mutex>
 #include <type_traits>
+#include <vector>
 
 #include "block.cuh"
 #include "epilogue.cuh"
@@ -51,7 +60,7 @@ template <class T, int MODE>
 __global__ void __launch_bounds__(192, 2)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                     const float* __restrict__ s4, const uint8_t* __restrict__ z4, int M, int N, int K,
-                    Epilogue ep, int* err) {
+                    int kps, Epilogue ep, int* err) {
   using L = W4Smem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -65,7 +74,8 @@ __global__ void __launch_bounds__(192, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
-  const int nkb = K / kBKe;
+  const int kb0 = blockIdx.z * kps;                // this CTA's K-blocks [kb0, kb0 + nkb)
+  const int nkb = min(K / kBKe - kb0, kps);
   const int G = K / 128;
 
   if (threadIdx.x == 0) {
@@ -95,8 +105,8 @@ __global__ void __launch_bounds__(192, 2)
         if (!mbar_wait_bounded(empty + s, ph ^ 1, abort_flag, err, kErrWaitEmpty)) break;
         uint8_t* st = smem + s * L::kStage;
         mbar_arrive_expect_tx(full + s, L::kA + L::kP);
-        tma_load_2d(st, &tmA, full + s, kb * kBKe, m0);
-        tma_load_2d(st + L::kA + L::kB, &tmP, full + s, kb * (kBKe / 2), n0);
+        tma_load_2d(st, &tmA, full + s, (kb0 + kb) * kBKe, m0);
+        tma_load_2d(st + L::kA + L::kB, &tmP, full + s, (kb0 + kb) * (kBKe / 2), n0);
         ++issued;
       }
       if (*abort_flag) {
@@ -143,7 +153,7 @@ __global__ void __launch_bounds__(192, 2)
           uint8_t* brow = st + L::kA + t * 128;
           float sc = 0.0f, zp = 0.0f;
           if (n < N) {
-            const int64_t gi = static_cast<int64_t>(n) * G + (kb >> 1);
+            const int64_t gi = static_cast<int64_t>(n) * G + ((kb0 + kb) >> 1);
             sc = __ldg(s4 + gi);
             zp = static_cast<float>(__ldg(z4 + gi));
           }
@@ -184,9 +194,13 @@ __global__ void __launch_bounds__(192, 2)
                                                               kErrWaitAccum) &&
                                                 !*abort_flag);
     tc_fence_after();
+    using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, T>::type;
+    Epilogue pe = ep;
+    if constexpr (MODE == kEpiAccI32)  // split-K slice: raw fp32 bits into partials[z]
+      pe.out = static_cast<int32_t*>(ep.out) + static_cast<int64_t>(blockIdx.z) * M * N;
     if (ok)
-      tc_tile_epilogue_passes<MODE, T, kBN, false>(ep, tmem, q, lane, m0, n0, M, N,
-                                                   smem + q * 32 * epi_stage_row_bytes<T>());
+      tc_tile_epilogue_passes<MODE, T, kBN, false>(pe, tmem, q, lane, m0, n0, M, N,
+                                                   smem + q * 32 * epi_stage_row_bytes<StoreT>());
   }
 
   tc_fence_before();
@@ -197,10 +211,43 @@ __global__ void __launch_bounds__(192, 2)
   }
 }
 
+// Sum of the split-K slices: one warp per 32-column row chunk, lane j summing
+// column j over the slices (coalesced 128-byte reads), then lane 0 applies
+// the fused epilogue to the chunk and stores it.
+template <int MODE, class OutT>
+__global__ void __launch_bounds__(256) splitk_epilogue_kernel(const float* __restrict__ part,
+                                                              int splits, int M, int N,
+                                                              Epilogue ep) {
+  const int nch = N / 32;
+  const int64_t chunk = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (chunk >= static_cast<int64_t>(M) * nch) return;  // whole warps leave together
+  const int m = static_cast<int>(chunk / nch);
+  const int c = static_cast<int>(chunk - static_cast<int64_t>(m) * nch);
+  const float* p = part + static_cast<int64_t>(m) * N + c * 32 + lane;
+  const int64_t slice = static_cast<int64_t>(M) * N;
+  float acc = 0.0f;
+  int z = 0;
+  for (; z + 4 <= splits; z += 4) {
+    const float a0 = __ldg(p + z * slice), a1 = __ldg(p + (z + 1) * slice);
+    const float a2 = __ldg(p + (z + 2) * slice), a3 = __ldg(p + (z + 3) * slice);
+    acc += a0;
+    acc += a1;
+    acc += a2;
+    acc += a3;
+  }
+  for (; z < splits; ++z) acc += __ldg(p + z * slice);
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __shfl_sync(0xffffffffu, acc, i);
+  if (lane == 0) epilogue_store32<MODE, OutT>(ep, m, static_cast<int64_t>(c) * 32, v);
+}
+
 }  // namespace
 
 void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s4, const uint8_t* z4,
-                  int64_t M, int64_t N, int64_t K, int mode, const Epilogue& ep, cudaStream_t stream) {
+                  int64_t M, int64_t N, int64_t K, int mode, const Epilogue& ep, cudaStream_t stream,
+                  DevBuf* splitk_ws) {
   LTM_REQUIRE(M >= 0 && N >= 0 && K >= 0, "negative size");
   LTM_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "size exceeds int32");
   if (M == 0 || N == 0) return;
@@ -217,14 +264,55 @@ void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s
               2, M, K, K, kBKe, kBM);
   make_tma_2d(&tp, q4, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, kBKe / 2, kBN,
               CU_TENSOR_MAP_SWIZZLE_NONE);
-  dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+  const int tiles_n = static_cast<int>((N + kBN - 1) / kBN), tiles_m = static_cast<int>((M + kBM - 1) / kBM);
+  const int nkb = static_cast<int>(K / kBKe);
+  // split K when the tile grid leaves most SMs idle (two CTAs fit per SM),
+  // with at least 8 K-blocks per slice
+  int splits = 1;
+  if (splitk_ws != nullptr) {
+    const int want = 2 * device_sm_count() / (tiles_n * tiles_m);
+    splits = std::max(1, std::min(want, nkb / 8));
+  }
+  const int kps = (nkb + splits - 1) / splits;
+  splits = (nkb + kps - 1) / kps;
+  dim3 grid(tiles_n, tiles_m, splits);
+  if (splits > 1) {
+    const size_t need = static_cast<size_t>(splits) * M * N * sizeof(float);
+    splitk_ws->ensure(need);
+    Epilogue pe;
+    pe.out = splitk_ws->ptr;
+    pe.ldo = N;
+    dispatch_dtype(dt, [&](auto tag) {
+      using T = decltype(tag);
+      if constexpr (!std::is_same<T, float>::value) {
+        auto kern = w4a16_tc_kernel<T, kEpiAccI32>;
+        LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          W4Smem::kBytes));
+        kern<<<grid, 192, W4Smem::kBytes, stream>>>(ta, tp, s4, z4, static_cast<int>(M),
+                                                     static_cast<int>(N), static_cast<int>(K), kps,
+                                                     pe, device_error_ptr());
+      }
+    });
+    check_launch("w4a16_tc_kernel/splitk", stream);
+    const int64_t threads = M * N;  // one warp per 32-column row chunk
+    dispatch_epilogue(mode, dt, [&](auto mode_c, auto out_tag) {
+      using OutT = decltype(out_tag);
+      constexpr int MODE = decltype(mode_c)::value;
+      if constexpr (MODE != kEpiAccI32 && !std::is_same<OutT, float>::value)
+        splitk_epilogue_kernel<MODE, OutT><<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
+                                             stream>>>(splitk_ws->as<float>(), splits,
+                                                       static_cast<int>(M), static_cast<int>(N), ep);
+    });
+    check_launch("splitk_epilogue_kernel", stream);
+    return;
+  }
   auto go = [&](auto tag, auto mode_c) {
     using T = decltype(tag);
     constexpr int MODE = decltype(mode_c)::value;
     auto kern = w4a16_tc_kernel<T, MODE>;
     LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, W4Smem::kBytes));
     kern<<<grid, 192, W4Smem::kBytes, stream>>>(ta, tp, s4, z4, static_cast<int>(M),
-                                                 static_cast<int>(N), static_cast<int>(K), ep,
+                                                 static_cast<int>(N), static_cast<int>(K), kps, ep,
                                                  device_error_ptr());
   };
   dispatch_epilogue(mode, dt, [&](auto mode_c, auto out_tag) {
@@ -234,6 +322,19 @@ void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s
   });
   check_launch("w4a16_tc_kernel", stream);
 }
+
+namespace {
+// Per-device split-K partials of ltm_linear_w4a16 (grown on demand, held
+// until exit; calls whose GPU work overlaps on one device share it).
+DevBuf& splitk_scratch(int dev) {
+  static std::mutex mu;
+  static std::vector<std::unique_ptr<DevBuf>> per_dev;
+  std::lock_guard<std::mutex> lk(mu);
+  if (static_cast<int>(per_dev.size()) <= dev) per_dev.resize(dev + 1);
+  if (!per_dev[dev]) per_dev[dev] = std::make_unique<DevBuf>();
+  return *per_dev[dev];
+}
+}  // namespace
 
 }  // namespace ltm_b200
 
@@ -251,6 +352,9 @@ extern "C" ltm_status ltm_linear_w4a16(const void* a, ltm_dtype a_dtype, const u
     ep.bias = bias;
     ep.out = y;
     ep.ldo = N;
-    launch_w4a16(a, a_dtype, packed, s, zp, M, N, K, kEpiPlain, ep, as_stream(stream));
+    int dev = 0;
+    LTM_CUDA_TRY(cudaGetDevice(&dev));
+    launch_w4a16(a, a_dtype, packed, s, zp, M, N, K, kEpiPlain, ep, as_stream(stream),
+                 &splitk_scratch(dev));
   });
 }

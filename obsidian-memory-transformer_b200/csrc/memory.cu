@@ -41,46 +41,122 @@ __global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ x, in
   }
 }
 
-// One CTA per head: slot softmax of the mean memory query against K_M, added
-// into wslot with weight rate / nh_total (the mean over all heads; a
-// tensor-parallel rank adds its own heads and the ranks sum wslot).
+// Slot softmax of the mean memory query against K_M, one cluster of kSlotCL
+// CTAs per head: CTA r of the cluster scores the slots [r*per, (r+1)*per)
+// (lane groups of dh/8 lanes read one slot's 16-byte pieces of the head's key
+// row: coalesced, 16 loads in flight per lane), the softmax max and sum are
+// combined over the cluster through distributed shared memory, and every CTA
+// adds its slots' weights rate / nh_total * softmax into wslot (the mean over
+// all heads; a tensor-parallel rank adds its own heads and the ranks sum
+// wslot).
+constexpr int kSlotCL = 8;
+constexpr int kSlotUnroll = 4;
+
+// 8 consecutive elements (16-byte aligned) as floats.
 template <class T>
-__global__ void __launch_bounds__(256) slot_weight_kernel(const float* __restrict__ qsum,
-                                                          float inv_T, const T* __restrict__ kvm,
-                                                          int64_t ldk, int Ms, int dh, int nh_total,
-                                                          float rate, float* __restrict__ wslot) {
-  extern __shared__ float sc[];  // [Ms] scores, then reduction scratch
-  __shared__ float red[32];
-  const int h = blockIdx.x;
-  const float scale = rsqrtf(static_cast<float>(dh));
-  float mx = -INFINITY;
-  for (int s = threadIdx.x; s < Ms; s += blockDim.x) {
-    const T* kr = kvm + static_cast<int64_t>(s) * ldk + h * dh;
-    float d = 0.0f;
-    for (int e = 0; e < dh; ++e) d += qsum[h * dh + e] * inv_T * to_f32(kr[e]);
-    d *= scale;
-    sc[s] = d;
-    mx = fmaxf(mx, d);
+__device__ __forceinline__ void load8_f32(const T* p, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = to_f32(e[i]);
   }
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+template <class T>
+__global__ void __cluster_dims__(kSlotCL, 1, 1) __launch_bounds__(256)
+    slot_weight_kernel(const float* __restrict__ qsum, float inv_T, const T* __restrict__ kvm,
+                       int64_t ldk, int Ms, int dh, int nh_total, float rate,
+                       float* __restrict__ wslot) {
+  extern __shared__ float sc[];  // [per] scores of this CTA's slots
+  __shared__ __align__(16) float qh[128];
+  __shared__ float red[8];
+  __shared__ float stat[2];  // this CTA's (max, sum), read by the cluster
+  const int h = blockIdx.y;
+  const int r = static_cast<int>(cluster_ctarank());
+  const int per = (Ms + kSlotCL - 1) / kSlotCL;
+  const int s0 = min(Ms, r * per), s1 = min(Ms, s0 + per);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = rsqrtf(static_cast<float>(dh));
+  for (int e = threadIdx.x; e < dh; e += blockDim.x) qh[e] = qsum[h * dh + e] * inv_T;
+  __syncthreads();
+  // lane group g of LPS = dh/8 lanes scores one slot per step
+  const int lps = dh >> 3, spw = 32 / lps;  // lanes per slot, slots per warp step
+  const int gl = lane % lps, g = lane / lps;
+  float q8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q8[i] = qh[gl * 8 + i];
+  float mx = -INFINITY;
+  const int step = 8 * spw;  // slots per CTA step
+  for (int sb = s0 + warp * spw; sb < s1; sb += step * kSlotUnroll) {
+    float kv[kSlotUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kSlotUnroll; ++u) {
+      const int s = sb + u * step + g;
+      if (s < s1) {
+        load8_f32(kvm + static_cast<int64_t>(s) * ldk + h * dh + gl * 8, kv[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kv[u][i] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSlotUnroll; ++u) {
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d = fmaf(q8[i], kv[u][i], d);
+      for (int o = lps >> 1; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const int s = sb + u * step + g;
+      if (s < s1) {
+        d *= scale;
+        if (gl == 0) sc[s - s0] = d;
+        mx = fmaxf(mx, d);
+      }
+    }
+  }
+  // cluster max
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  if (lane == 0) red[warp] = mx;
   __syncthreads();
-  mx = -INFINITY;
-  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
-  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = red[0];
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+    stat[0] = m;
+  }
+  cluster_sync();
+  float gmax = -INFINITY;
+  for (int c = 0; c < kSlotCL; ++c) gmax = fmaxf(gmax, ld_cluster_f32(mapa_shared(&stat[0], c)));
+  // cluster sum of exp(score - max)
   float sum = 0.0f;
-  for (int s = threadIdx.x; s < Ms; s += blockDim.x) {
-    const float e = expf(sc[s] - mx);
-    sc[s] = e;
+  for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
+    const float e = expf(sc[s - s0] - gmax);
+    sc[s - s0] = e;
     sum += e;
   }
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  if (lane == 0) red[warp] = sum;
   __syncthreads();
-  sum = 0.0f;
-  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) sum += red[i];
-  const float f = rate / (sum * static_cast<float>(nh_total));
-  for (int s = threadIdx.x; s < Ms; s += blockDim.x) atomicAdd(wslot + s, sc[s] * f);
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    stat[1] = t;
+  }
+  cluster_sync();
+  float gsum = 0.0f;
+  for (int c = 0; c < kSlotCL; ++c) gsum += ld_cluster_f32(mapa_shared(&stat[1], c));
+  const float f = rate / (gsum * static_cast<float>(nh_total));
+  for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) atomicAdd(wslot + s, sc[s - s0] * f);
+  cluster_sync();  // no CTA leaves while the cluster still reads its stat
 }
 
 template <class T>
@@ -131,6 +207,33 @@ __global__ void state_row_kernel(const float* __restrict__ state, float scale, T
     out[j] = from_f32<T>(state[j] * scale);
 }
 
+// bank_update_kernel on 8 elements (16-bit, 16-byte aligned) per thread
+// (H a multiple of 8); the same arithmetic per element.
+template <class T>
+__global__ void __launch_bounds__(256) bank_update8_kernel(T* __restrict__ mem,
+                                                           const float* __restrict__ state,
+                                                           float state_scale,
+                                                           const float* __restrict__ wslot,
+                                                           float rate, int Ms, int H) {
+  const int nv = H / 8;
+  const int64_t n = static_cast<int64_t>(Ms) * nv;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(i / nv), c = static_cast<int>(i - static_cast<int64_t>(s) * nv);
+    const float w = wslot ? wslot[s] : rate;
+    uint4* mp = reinterpret_cast<uint4*>(mem + static_cast<int64_t>(s) * H) + c;
+    uint4 r = *mp;
+    T* e = reinterpret_cast<T*>(&r);
+    const float4 a = __ldg(reinterpret_cast<const float4*>(state + c * 8));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(state + c * 8) + 1);
+    const float cv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      e[k] = from_f32<T>((1.0f - w) * to_f32(e[k]) + w * (cv[k] * state_scale));
+    *mp = r;
+  }
+}
+
 }  // namespace
 
 void launch_rows_ema(void* rows, int64_t ld, int width, const void* v, const float* wslot,
@@ -166,6 +269,10 @@ void launch_slot_weights(const void* keys, int64_t ldk, const void* queries, int
                          int64_t T, int Ms, int heads, int dh, int nh_total, float rate,
                          ltm_dtype dt, float* qsum, float* wslot, cudaStream_t st) {
   const int Hq = heads * dh;
+  LTM_REQUIRE(dh == 8 || dh == 16 || dh == 32 || dh == 64 || dh == 128,
+              "attention-score slot weights need head_dim 8, 16, 32, 64 or 128");
+  LTM_REQUIRE(reinterpret_cast<uintptr_t>(keys) % 16 == 0 && (ldk * dtype_size(dt)) % 16 == 0,
+              "keys must be 16-byte aligned with a row stride of a multiple of 16 bytes");
   dispatch_dtype(dt, [&](auto tag) {
     using TT = decltype(tag);
     LTM_CUDA_TRY(cudaMemsetAsync(qsum, 0, Hq * sizeof(float), st));
@@ -174,12 +281,13 @@ void launch_slot_weights(const void* keys, int64_t ldk, const void* queries, int
     dim3 g1((Hq + 31) / 32, splits);
     colsum_kernel<TT><<<g1, 256, 0, st>>>(static_cast<const TT*>(queries), ldq, T, Hq, qsum);
     check_launch("colsum_kernel", st);
-    const size_t smem = static_cast<size_t>(Ms) * sizeof(float);
+    const size_t smem = static_cast<size_t>((Ms + kSlotCL - 1) / kSlotCL) * sizeof(float);
     auto kern = slot_weight_kernel<TT>;
     LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(smem)));
-    kern<<<heads, 256, smem, st>>>(qsum, 1.0f / static_cast<float>(T), static_cast<const TT*>(keys),
-                                   ldk, Ms, dh, nh_total, rate, wslot);
+    kern<<<dim3(kSlotCL, heads), 256, smem, st>>>(qsum, 1.0f / static_cast<float>(T),
+                                                  static_cast<const TT*>(keys), ldk, Ms, dh,
+                                                  nh_total, rate, wslot);
     check_launch("slot_weight_kernel", st);
   });
 }
@@ -188,10 +296,16 @@ void launch_bank_update(void* memory, const float* state, float state_scale, con
                         float rate, int Ms, int H, ltm_dtype dt, cudaStream_t st) {
   dispatch_dtype(dt, [&](auto tag) {
     using TT = decltype(tag);
-    const int64_t n = static_cast<int64_t>(Ms) * H;
+    const bool vec = sizeof(TT) == 2 && H % 8 == 0 && reinterpret_cast<uintptr_t>(memory) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(state) % 16 == 0;
+    const int64_t n = static_cast<int64_t>(Ms) * (vec ? H / 8 : H);
     const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, device_sm_count() * 8));
-    bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale,
-                                                 wslot, rate, Ms, H);
+    if (vec)
+      bank_update8_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale,
+                                                    wslot, rate, Ms, H);
+    else
+      bank_update_kernel<TT><<<grid, 256, 0, st>>>(static_cast<TT*>(memory), state, state_scale,
+                                                   wslot, rate, Ms, H);
     check_launch("bank_update_kernel", st);
   });
 }

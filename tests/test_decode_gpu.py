@@ -226,3 +226,29 @@ def test_cache_manager_decode_loop(ltm, orc):
     assert cache.length == 3
     for b in blocks:
         b.close()
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_decode_wide_block_split_k(ltm, orc, dt):
+    """A block wide enough that the decode GEMMs split K over CTAs (every
+    fused epilogue: RoPE, gate-mix with the write's column sums, GELU,
+    residual) for a few steps with the memory write."""
+    from ltm_b200 import synthetic
+    H, nh, F, Ms, B, L0, P = 1024, 8, 2048, 64, 4, 30, 40
+    cfg, q, ocfg = make(ltm, "w4a16", dt, H, nh, F, Ms, memory_write=True)
+    w = synthetic.block_weights(H, F, Ms, 21)
+    blk = ltm.TitanBlock(cfg, q)
+    blk.load_weights(w)
+    kd, vd, kh, vh = _caches(B, P, H, L0, dt, 22)
+    mem = orc.round_to(w["memory"], ocfg["dtype"])
+    kvm = orc.block_kvm(ocfg, w, mem)
+    for i in range(3):
+        x = _round(synthetic.activations(B, H, 200 + i), dt)
+        y = blk.decode_step(to_device(x, dt), kd, vd, L0 + i)
+        ref = orc.block_decode_step(ocfg, w, x, kh, vh, L0 + i, mem, kvm)
+        assert_close(as_f32(y), ref, *TOL[dt], what=f"wide step {i} {dt}")
+        kh[:, L0 + i] = as_f32(kd[:, L0 + i])
+        vh[:, L0 + i] = as_f32(vd[:, L0 + i])
+    assert_close(as_f32(blk.memory()), mem, 2e-3, 1e-2, what="wide bank after the decode writes")
+    assert ltm.device_error() == 0
+    blk.close()

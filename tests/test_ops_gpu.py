@@ -74,7 +74,10 @@ def test_linear_w8a32(ltm, orc, act, M, N, K):
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("act", [0, 1])
 @pytest.mark.parametrize("M,N,K", [(256, 256, 256), (300, 384, 1024), (64, 4096, 4096),
-                                   (130, 11008 // 32 * 32, 512)])
+                                   (130, 11008 // 32 * 32, 512),
+                                   # small grids: K split over CTAs, partials summed by the epilogue
+                                   (1, 8192, 4096), (3, 256, 11008), (64, 11008, 4096),
+                                   (129, 512, 2048)])
 def test_linear_w4a16(ltm, orc, dt, act, M, N, K):
     import torch
     rng = np.random.default_rng(M + N + K + act)
