@@ -612,8 +612,8 @@ def cpu_baseline_decode(wl: dict = DEC_WL, budget_s: float = 12.0):
     w = synthetic.block_weights(H, F, Ms, 1000)
     pb = orc.PreparedBlock(ocfg, w)
     rng = np.random.default_rng(5)
-    kc = orc.round_to(rng.standard_normal((1, P, H), dtype=np.float32), orc.BF16)
-    vc = orc.round_to(rng.standard_normal((1, P, H), dtype=np.float32), orc.BF16)
+    kc = orc.round_to(rng.standard_normal((1, nh, P, H // nh), dtype=np.float32), orc.BF16)
+    vc = orc.round_to(rng.standard_normal((1, nh, P, H // nh), dtype=np.float32), orc.BF16)
     mem = orc.round_to(w["memory"], orc.BF16)
     kvm = orc.round_to(rng.standard_normal((Ms, 2 * H), dtype=np.float32) * 0.1, orc.BF16)
     x = orc.round_to(rng.standard_normal((1, H), dtype=np.float32) * 0.02, orc.BF16)
@@ -660,7 +660,7 @@ def run_decode(args, wl: dict = DEC_WL):
         b.load_weights(w)
         blocks.append(b)
     del w
-    cache = ltm.CacheManager(L, H, torch.bfloat16, device=local, shared_layers=True)
+    cache = ltm.CacheManager(L, nh, H // nh, torch.bfloat16, device=local, shared_layers=True)
     cache.allocate(B, P)
     gen = torch.Generator(device=dev).manual_seed(11 + rank)
     for t in cache.get(0)[:2]:
@@ -766,7 +766,8 @@ def run_decode(args, wl: dict = DEC_WL):
                        "step_bytes": lb["total"] * L,
                        "step_hbm_gbs": round(step_gbs, 1),
                        "step_hbm_frac": round(step_gbs / pk["hbm_gbs"], 4),
-                       "kv_cache": "one buffer shared by the layers (34.4 GB)",
+                       "kv_cache": "head-major [64, 32, 32768, 128] bf16 K and V, one pair shared "
+                                   "by the layers (34.4 GB)",
                        "l2": "inputs (34 GB KV cache per layer) larger than L2"},
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x_host.numel() * 2),
@@ -799,8 +800,8 @@ def probe_decode_case(torch, ltm):
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(synthetic.block_weights(H, F, Ms, 1000))
     gen = torch.Generator(device="cuda").manual_seed(3)
-    kc = torch.randn((B, P, H), generator=gen, device="cuda").to(torch.bfloat16)
-    vc = torch.randn((B, P, H), generator=gen, device="cuda").to(torch.bfloat16)
+    kc = torch.randn((B, nh, P, H // nh), generator=gen, device="cuda").to(torch.bfloat16)
+    vc = torch.randn((B, nh, P, H // nh), generator=gen, device="cuda").to(torch.bfloat16)
     x = (torch.randn((B, H), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
     blk.decode_step(x, kc, vc, P - 1)
     blk.decode_step(x, kc, vc, P - 1)

@@ -295,12 +295,12 @@ LTM_API ltm_status ltm_block_forward(ltm_block* blk, const void* x, void* y, con
  * (python_bindings/ltm/inference.py:101-128) with the TB-v1 block applied to
  * one new token per sequence:
  *   x, y     device [B, H] in act_dtype (f16 / bf16; distinct buffers);
- *   k_cache, v_cache  device [B, max_positions, Hl] in act_dtype, 16-byte
- *            aligned (Hl = H, or this rank's heads num_heads/n * head_dim
- *            under tensor parallelism; head h at columns h*head_dim);
+ *   k_cache, v_cache  device [B, heads, max_positions, head_dim] in
+ *            act_dtype (head-major; heads = num_heads, or this rank's
+ *            num_heads / n under tensor parallelism), 16-byte aligned;
  *            positions [0, cache_len) hold the post-RoPE keys and the values
  *            of the tokens before; the step writes the new token's K and V at
- *            position cache_len of every sequence;
+ *            position cache_len of every head of every sequence;
  *   the new token's RoPE position is cache_len; its self-attention reads the
  *   cache_len + 1 positions [0, cache_len];
  *   the memory attention reads K_M | V_M, which the block keeps resident

@@ -494,7 +494,8 @@ struct ltm_block {
   }
 
   // One decode step: x, out [B, H], every sequence's new token at position L;
-  // k_cache / v_cache [B, P, Hl] hold positions [0, L) and receive position L.
+  // k_cache / v_cache [B, nhl, P, dh] hold positions [0, L) and receive
+  // position L.
   void decode(const void* x, void* out, void* kc, void* vc, int64_t P, int L, int B,
               cudaStream_t st) {
     const int64_t T = B;
@@ -503,11 +504,11 @@ struct ltm_block {
     if (!kvm_fresh) compute_kvm(st);
     const void* hin = ln1(x, T, st);
     qkv_proj(hin, T, 1, L, st);
-    launch_kv_append(qkv.ptr, 4 * Hl, Hl, kc, vc, P * Hl, L, B, dt, st);
+    launch_kv_append(qkv.ptr, 4 * Hl, Hl, dh, kc, vc, P, L, B, dt, st);
     const size_t pb = decode_partials_bytes(B, nhl, dh, P);
     if (pb > dpart.bytes) dpart.ensure(pb);
-    launch_decode_attention(qkv.ptr, 4 * Hl, kc, vc, P * Hl, Hl, L + 1, B, nhl, dh, dt,
-                            dpart.as<float>(), os.ptr, Hl, st);
+    launch_decode_attention(qkv.ptr, 4 * Hl, kc, vc, P, L + 1, B, nhl, dh, dt, dpart.as<float>(),
+                            os.ptr, Hl, st);
     mem_attention(1, B, st);  // the batch's rows share the bank: one group of B queries
     tail(x, out, T, st);
     if (q.memory_write && cfg.use_memory_gating) write(T, true, st);

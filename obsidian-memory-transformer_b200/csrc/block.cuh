@@ -89,17 +89,18 @@ void launch_state_row(const float* state, float scale, void* out, int H, ltm_dty
 void launch_rows_ema(void* rows, int64_t ld, int width, const void* v, const float* wslot,
                      float rate, int Ms, ltm_dtype dt, cudaStream_t st);
 
-// Decode step: the new token's K | V rows (columns [width, 3 width) of the
-// fused projection rows, stride ldq) to position pos of every sequence's
-// cache (seq_stride elements apart, rows of `width`).
-void launch_kv_append(const void* qkv, int64_t ldq, int width, void* kc, void* vc,
-                      int64_t seq_stride, int64_t pos, int B, ltm_dtype dt, cudaStream_t st);
-// Self-attention of one query row per (sequence, head) over L cached
-// positions (split into chunks, partials in `part`, then merged into o).
+// Decode step, head-major caches [B, width / dh, P, dh]: the new token's K | V
+// rows (columns [width, 3 width) of the fused projection rows, stride ldq) to
+// position pos of every head of its sequence.
+void launch_kv_append(const void* qkv, int64_t ldq, int width, int dh, void* kc, void* vc,
+                      int64_t P, int64_t pos, int B, ltm_dtype dt, cudaStream_t st);
+// Self-attention of one query row per (sequence, head) over the first L of
+// the P cached positions (split into chunks, partials in `part`, then merged
+// into o).
 size_t decode_partials_bytes(int B, int nh, int D, int64_t L);
 void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const void* vc,
-                             int64_t seq_stride, int width, int L, int B, int nh, int D,
-                             ltm_dtype dt, float* part, void* o, int64_t ldo, cudaStream_t st);
+                             int64_t P, int L, int B, int nh, int D, ltm_dtype dt, float* part,
+                             void* o, int64_t ldo, cudaStream_t st);
 
 // Slot weights of `heads` heads (rate / nh_total per head, summed into wslot;
 // qsum [heads*dh] and wslot [Ms] are cleared here) and the bank EMA.

@@ -2,16 +2,18 @@
 // appending the new token's keys / values and the self-attention read of the
 // whole cache (flash decoding, HBM-bound).
 //
-// Cache layout: per sequence b a [max_positions, width] row-major block of the
-// activation dtype (width = hidden, or this rank's heads under tensor
-// parallelism), head h at columns h*D; position p of sequence b at
-// cache + b * seq_stride + p * width.
+// Cache layout (head-major): [B, heads, max_positions, head_dim] in the
+// activation dtype (heads = num_heads, or this rank's heads under tensor
+// parallelism): the row of position p of head h of sequence b starts at
+// cache + ((b * heads + h) * max_positions + p) * head_dim, so the 64 rows of a
+// tile are one contiguous block.
 //
 // Attention of one query row per (sequence, head) over L cached positions
 // (flash decoding): the positions are split into chunks of kDChunk (the work
 // items, one partial (max, sum, output) each); a persistent grid of one CTA
 // per SM walks its share of the work items.  In each CTA warp 0 streams
-// 64-position K and V tiles of the items (TMA, box [64 rows x head_dim]) into
+// 64-position K and V tiles of the items (TMA, box [64 rows x head_dim], one
+// contiguous block of the head-major cache) into
 // a ring of shared-memory stages that never drains between items, and 8
 // consumer warps run the online softmax: each takes 8 rows of a tile as 4
 // groups of 8 lanes x 2 keys, lane l of a group holding the dims
@@ -64,20 +66,23 @@ __device__ __forceinline__ void load_row_part(const T* row, int gl, float (&v)[D
 
 __device__ __forceinline__ int part_dim(int gl, int i) { return (i >> 3) * 64 + gl * 8 + (i & 7); }
 
+// K | V rows of the new token (columns [width, 3 width) of its fused
+// projection row) into position pos of every head of its sequence.
 template <class T>
 __global__ void __launch_bounds__(256) kv_append_kernel(const T* __restrict__ qkv, int64_t ldq,
-                                                        int width, T* __restrict__ kc,
-                                                        T* __restrict__ vc, int64_t seq_stride,
+                                                        int width, int dh, T* __restrict__ kc,
+                                                        T* __restrict__ vc, int64_t P,
                                                         int64_t pos) {
   const int b = blockIdx.x;
-  const int nv = width * static_cast<int>(sizeof(T)) / 16;
+  const int nv = width / 8, vph = dh / 8;  // 16-byte vectors per row / per head
+  const int heads = width / dh;
   const uint4* ks = reinterpret_cast<const uint4*>(qkv + b * ldq + width);
   const uint4* vs = reinterpret_cast<const uint4*>(qkv + b * ldq + 2 * static_cast<int64_t>(width));
-  uint4* kd = reinterpret_cast<uint4*>(kc + b * seq_stride + pos * width);
-  uint4* vd = reinterpret_cast<uint4*>(vc + b * seq_stride + pos * width);
   for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-    kd[i] = ks[i];
-    vd[i] = vs[i];
+    const int h = i / vph, c = i - h * vph;
+    const int64_t dst = ((static_cast<int64_t>(b) * heads + h) * P + pos) * dh;
+    reinterpret_cast<uint4*>(kc + dst)[c] = ks[i];
+    reinterpret_cast<uint4*>(vc + dst)[c] = vs[i];
   }
 }
 
@@ -121,7 +126,6 @@ __global__ void __launch_bounds__(32 * (kDCons + 1), 1) decode_attn_kernel(
       bool ok = true;
       for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
         const int c = w % nchunk, bh = w / nchunk;
-        const int h = bh % nh, b = bh / nh;
         const int c0 = c * kDChunk, c1 = min(L, c0 + kDChunk);
         const int nt = (c1 - c0 + kDTile - 1) / kDTile;
         for (int t = 0; t < nt; ++t, ++it) {
@@ -132,9 +136,9 @@ __global__ void __launch_bounds__(32 * (kDCons + 1), 1) decode_attn_kernel(
           }
           mbar_arrive_expect_tx(full + st, S::kStage);
           uint8_t* dst = smem + st * S::kStage;
-          const int row = b * P + c0 + t * kDTile;
-          tma_load_2d(dst, &tmK, full + st, h * D, row);
-          tma_load_2d(dst + S::kTile, &tmV, full + st, h * D, row);
+          const int row = bh * P + c0 + t * kDTile;  // head-major: (b * nh + h) * P + position
+          tma_load_2d(dst, &tmK, full + st, 0, row);
+          tma_load_2d(dst + S::kTile, &tmV, full + st, 0, row);
         }
       }
       if (!ok) {  // let the copies in flight land before the CTA exits
@@ -293,37 +297,34 @@ size_t decode_partials_bytes(int B, int nh, int D, int64_t L) {
   return static_cast<size_t>(B) * nh * nchunk * (D + 2) * sizeof(float);
 }
 
-void launch_kv_append(const void* qkv, int64_t ldq, int width, void* kc, void* vc,
-                      int64_t seq_stride, int64_t pos, int B, ltm_dtype dt, cudaStream_t st) {
-  LTM_REQUIRE((width * dtype_size(dt)) % 16 == 0, "cache width must be a multiple of 16 bytes");
+void launch_kv_append(const void* qkv, int64_t ldq, int width, int dh, void* kc, void* vc,
+                      int64_t P, int64_t pos, int B, ltm_dtype dt, cudaStream_t st) {
+  LTM_REQUIRE(dt != LTM_DTYPE_F32 && dh % 8 == 0 && width % dh == 0,
+              "KV append needs 16-bit rows of whole heads");
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
-    kv_append_kernel<T><<<B, 256, 0, st>>>(static_cast<const T*>(qkv), ldq, width,
-                                            static_cast<T*>(kc), static_cast<T*>(vc), seq_stride,
-                                            pos);
+    kv_append_kernel<T><<<B, 256, 0, st>>>(static_cast<const T*>(qkv), ldq, width, dh,
+                                            static_cast<T*>(kc), static_cast<T*>(vc), P, pos);
   });
   check_launch("kv_append_kernel", st);
 }
 
 void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const void* vc,
-                             int64_t seq_stride, int width, int L, int B, int nh, int D,
-                             ltm_dtype dt, float* part, void* o, int64_t ldo, cudaStream_t st) {
+                             int64_t P, int L, int B, int nh, int D, ltm_dtype dt, float* part,
+                             void* o, int64_t ldo, cudaStream_t st) {
   LTM_REQUIRE(D == 64 || D == 128, "decode attention head_dim must be 64 or 128");
-  LTM_REQUIRE(L >= 1, "empty cache");
+  LTM_REQUIRE(L >= 1 && L <= P, "cache length outside [1, max_positions]");
   LTM_REQUIRE(dt != LTM_DTYPE_F32, "decode attention needs 16-bit activations");
-  LTM_REQUIRE(seq_stride % width == 0, "sequence stride must be whole cache rows");
-  const int64_t P = seq_stride / width;
-  LTM_REQUIRE(static_cast<int64_t>(B) * P < (1ll << 31), "cache rows exceed int32");
+  LTM_REQUIRE(static_cast<int64_t>(B) * nh * P < (1ll << 31), "cache rows exceed int32");
   const int nchunk = (L + kDChunk - 1) / kDChunk;
   const int items = B * nh * nchunk;
   const float sl2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   const CUtensorMapDataType tdt =
       dt == LTM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tk, tv;
-  make_tma_2d(&tk, kc, tdt, 2, static_cast<uint64_t>(B) * P, width, width, D, kDTile,
-              CU_TENSOR_MAP_SWIZZLE_NONE);
-  make_tma_2d(&tv, vc, tdt, 2, static_cast<uint64_t>(B) * P, width, width, D, kDTile,
-              CU_TENSOR_MAP_SWIZZLE_NONE);
+  const uint64_t rows = static_cast<uint64_t>(B) * nh * P;
+  make_tma_2d(&tk, kc, tdt, 2, rows, D, D, D, kDTile, CU_TENSOR_MAP_SWIZZLE_NONE);
+  make_tma_2d(&tv, vc, tdt, 2, rows, D, D, D, kDTile, CU_TENSOR_MAP_SWIZZLE_NONE);
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (!std::is_same<T, float>::value) {

@@ -535,18 +535,22 @@ class TitanBlock:
     def decode_step(self, x, k_cache, v_cache, cache_len: int, stream=None, out=None):
         """One decode step: x [B, H] (one new token per sequence, all at
         position cache_len) -> y [B, H].  k_cache / v_cache: CUDA tensors
-        [B, max_positions, Hl] in the act dtype holding positions
-        [0, cache_len); the step writes position cache_len."""
+        [B, heads, max_positions, head_dim] (head-major; heads = this
+        block's heads) in the act dtype holding positions [0, cache_len); the
+        step writes position cache_len."""
         torch = _torch()
         _need_cuda(x, k_cache, v_cache, out)
         B = x.shape[0]
-        if k_cache.shape != v_cache.shape or k_cache.dim() != 3 or k_cache.shape[0] != B:
-            raise LtmError(ERR_INVALID_ARG, "k_cache / v_cache must both be [B, max_positions, Hl]")
+        heads = self.config.num_heads // (self._comm.nranks if self._comm is not None else 1)
+        if (k_cache.shape != v_cache.shape or k_cache.dim() != 4 or k_cache.shape[0] != B
+                or k_cache.shape[1] != heads or k_cache.shape[3] != self.config.head_dim):
+            raise LtmError(ERR_INVALID_ARG,
+                           "k_cache / v_cache must both be [B, heads, max_positions, head_dim]")
         if not (k_cache.is_contiguous() and v_cache.is_contiguous() and x.is_contiguous()):
             raise LtmError(ERR_INVALID_ARG, "x and the caches must be contiguous")
         y = torch.empty_like(x) if out is None else out
         _check(lib().ltm_block_decode_step(self._h, _ptr(x), _ptr(y), _ptr(k_cache), _ptr(v_cache),
-                                           k_cache.shape[1], int(cache_len), B, _stream(stream)))
+                                           k_cache.shape[2], int(cache_len), B, _stream(stream)))
         return y
 
     def memory_write(self, state, queries=None, stream=None) -> None:
@@ -582,16 +586,18 @@ class CacheManager:
     """KV caches of a stack of blocks for decoding (the reference's
     CacheManager, python_bindings/ltm/inference.py:101-128, whose native side
     is a stub): allocate(batch_size, seq_length) makes one K and one V tensor
-    [batch_size, seq_length, width] per layer; update(...) records that a step
-    appended one position; get(index) returns the (keys, values, None) of
-    layer `index`; clear() forgets the cached positions.
+    [batch_size, heads, seq_length, head_dim] (head-major) per layer;
+    update(...) records that a step appended one position; get(index) returns
+    the (keys, values, None) of layer `index`; clear() forgets the cached
+    positions.
 
     `shared_layers` makes every layer use the same two tensors (a benchmark
     whose per-layer caches do not fit in device memory)."""
 
-    def __init__(self, n_layers: int, width: int, dtype, device: int = 0,
+    def __init__(self, n_layers: int, heads: int, head_dim: int, dtype, device: int = 0,
                  shared_layers: bool = False):
-        self.n_layers, self.width, self.dtype, self.device = n_layers, width, dtype, device
+        self.n_layers, self.heads, self.head_dim = n_layers, heads, head_dim
+        self.dtype, self.device = dtype, device
         self.shared_layers = shared_layers
         self.length = 0
         self._k, self._v = [], []
@@ -599,7 +605,7 @@ class CacheManager:
     def allocate(self, batch_size: int, seq_length: int) -> None:
         torch = _torch()
         n = 1 if self.shared_layers else self.n_layers
-        shape = (batch_size, seq_length, self.width)
+        shape = (batch_size, self.heads, seq_length, self.head_dim)
         dev = f"cuda:{self.device}"
         self._k = [torch.empty(shape, dtype=self.dtype, device=dev) for _ in range(n)]
         self._v = [torch.empty(shape, dtype=self.dtype, device=dev) for _ in range(n)]
@@ -607,7 +613,7 @@ class CacheManager:
 
     @property
     def max_positions(self) -> int:
-        return self._k[0].shape[1] if self._k else 0
+        return self._k[0].shape[2] if self._k else 0
 
     def update(self, key=None, value=None, memory=None) -> None:
         """Marks one appended position (the decode step wrote it in place)."""

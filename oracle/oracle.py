@@ -272,15 +272,15 @@ def block_kvm(cfg: dict, w: dict, memory=None):
 
 def block_decode_step(cfg: dict, w: dict, x, k_cache, v_cache, cache_len: int, memory, kvm):
     """One decode step (x [B, H], every sequence at position cache_len).
-    k_cache, v_cache: float32 [B, P, H]; memory [Ms, H]; kvm [Ms, 2H] -- all
-    updated in place.  Returns y [B, H]."""
+    k_cache, v_cache: float32 [B, nh, P, dh] (head-major); memory [Ms, H];
+    kvm [Ms, 2H] -- all updated in place.  Returns y [B, H]."""
     c = _cfg(cfg)
     st, keep = _weights(w)
     x = _f32(x)
     B = x.shape[0]
     for a in (k_cache, v_cache, memory, kvm):
         assert a.dtype == np.float32 and a.flags.c_contiguous
-    P = k_cache.shape[1]
+    P = k_cache.shape[2]
     y = np.empty_like(x)
     r = lib().orc_block_decode_step(C.byref(c), C.byref(st), _ptr(memory), _ptr(kvm), _ptr(x),
                                     _ptr(k_cache), _ptr(v_cache), P, cache_len, B, _ptr(y))
@@ -305,7 +305,7 @@ class PreparedBlock:
         y = np.empty_like(x)
         r = lib().orc_block_decode_step_prepared(self.h, C.byref(self.c), C.byref(self.st),
                                                  _ptr(memory), _ptr(kvm), _ptr(x), _ptr(k_cache),
-                                                 _ptr(v_cache), k_cache.shape[1], cache_len,
+                                                 _ptr(v_cache), k_cache.shape[2], cache_len,
                                                  x.shape[0], _ptr(y))
         if r != 0:
             raise RuntimeError(f"orc_block_decode_step failed ({r})")

@@ -240,6 +240,35 @@ void orc_rope_table(int S, int dh, float* tab) {
     }
 }
 
+}  // extern "C"
+
+namespace {
+
+// softmax(q . K^T * scale) V of one query row over the key / value rows
+// kbase + j * kstride, j < jmax (scores and sums in double), rounded to dtype.
+void attend_row(const float* qr, const float* kbase, const float* vbase, int64_t kstride, int jmax,
+                int dh, double scale, int dtype, std::vector<double>& sc, std::vector<double>& o,
+                float* orow) {
+  double mx = -1e300;
+  for (int j = 0; j < jmax; ++j) {
+    sc[j] = dot_f(qr, kbase + j * kstride, dh) * scale;
+    mx = std::max(mx, sc[j]);
+  }
+  double den = 0;
+  std::fill(o.begin(), o.end(), 0.0);
+  for (int j = 0; j < jmax; ++j) {
+    const double p = std::exp(sc[j] - mx);
+    den += p;
+    const float* vr = vbase + j * kstride;
+    for (int d = 0; d < dh; ++d) o[d] += p * vr[d];
+  }
+  for (int d = 0; d < dh; ++d) orow[d] = rnd(static_cast<float>(o[d] / den), dtype);
+}
+
+}  // namespace
+
+extern "C" {
+
 void orc_attention(const float* q, int64_t ldq, const float* k, const float* v, int64_t ldk, int B,
                    int Sq, int Skv, int kv_batch_stride_rows, int nh, int dh, int causal, int dtype,
                    float* out, int64_t ldo) {
@@ -254,22 +283,9 @@ void orc_attention(const float* q, int64_t ldq, const float* k, const float* v, 
         const int t = i / nh, h = i % nh;
         const float* qr = q + (static_cast<int64_t>(b) * Sq + t) * ldq + h * dh;
         const int jmax = causal ? std::min(t + 1, Skv) : Skv;
-        double mx = -1e300;
-        for (int j = 0; j < jmax; ++j) {
-          const float* kr = k + (static_cast<int64_t>(b) * kv_batch_stride_rows + j) * ldk + h * dh;
-          sc[j] = dot_f(qr, kr, dh) * scale;
-          mx = std::max(mx, sc[j]);
-        }
-        double den = 0;
-        std::fill(o.begin(), o.end(), 0.0);
-        for (int j = 0; j < jmax; ++j) {
-          const double p = std::exp(sc[j] - mx);
-          den += p;
-          const float* vr = v + (static_cast<int64_t>(b) * kv_batch_stride_rows + j) * ldk + h * dh;
-          for (int d = 0; d < dh; ++d) o[d] += p * vr[d];
-        }
-        float* orow = out + (static_cast<int64_t>(b) * Sq + t) * ldo + h * dh;
-        for (int d = 0; d < dh; ++d) orow[d] = rnd(static_cast<float>(o[d] / den), dtype);
+        const int64_t kb = static_cast<int64_t>(b) * kv_batch_stride_rows * ldk + h * dh;
+        attend_row(qr, k + kb, v + kb, ldk, jmax, dh, scale, dtype, sc, o,
+                   out + (static_cast<int64_t>(b) * Sq + t) * ldo + h * dh);
       }
   }
 }
@@ -573,16 +589,32 @@ int decode_step(const orc_block_cfg* c, const orc_block_weights* w, const OrcLin
   if (cache_len < 0 || cache_len >= max_positions) return 2;
   // the new token of every sequence sits at position cache_len
   std::vector<float> qkvm = qkvm_rows(c, w, L, x, B, 1, cache_len);
-  for (int b = 0; b < B; ++b) {
-    const int64_t dst = (static_cast<int64_t>(b) * max_positions + cache_len) * H;
-    std::memcpy(k_cache + dst, qkvm.data() + static_cast<int64_t>(b) * 4 * H + H, sizeof(float) * H);
-    std::memcpy(v_cache + dst, qkvm.data() + static_cast<int64_t>(b) * 4 * H + 2 * H, sizeof(float) * H);
-  }
-  // self-attention of the new token over positions [0, cache_len]; memory
-  // attention against the resident K_M | V_M
+  const int64_t P = max_positions;
+  for (int b = 0; b < B; ++b)
+    for (int h = 0; h < nh; ++h) {
+      const int64_t dst = ((static_cast<int64_t>(b) * nh + h) * P + cache_len) * dh;
+      const float* src = qkvm.data() + static_cast<int64_t>(b) * 4 * H + h * dh;
+      std::memcpy(k_cache + dst, src + H, sizeof(float) * dh);
+      std::memcpy(v_cache + dst, src + 2 * H, sizeof(float) * dh);
+    }
+  // self-attention of the new token over positions [0, cache_len] of each
+  // head's cache rows (one sequence and head per call); memory attention
+  // against the resident K_M | V_M
   std::vector<float> os(B * static_cast<int64_t>(H)), om(B * static_cast<int64_t>(H));
-  orc_attention(qkvm.data(), 4 * H, k_cache, v_cache, H, B, 1, cache_len + 1,
-                static_cast<int>(max_positions), nh, dh, 0, dt, os.data(), H);
+  const double scale = 1.0 / std::sqrt(static_cast<double>(dh));
+#pragma omp parallel
+  {
+    std::vector<double> sc(static_cast<size_t>(cache_len) + 1);
+    std::vector<double> o(static_cast<size_t>(dh));
+#pragma omp for schedule(dynamic, 1) collapse(2)
+    for (int b = 0; b < B; ++b)
+      for (int h = 0; h < nh; ++h) {
+        const int64_t base = (static_cast<int64_t>(b) * nh + h) * P * dh;
+        attend_row(qkvm.data() + static_cast<int64_t>(b) * 4 * H + h * dh, k_cache + base,
+                   v_cache + base, dh, cache_len + 1, dh, scale, dt, sc, o,
+                   os.data() + static_cast<int64_t>(b) * H + h * dh);
+      }
+  }
   orc_attention(qkvm.data() + 3 * H, 4 * H, kvm_inout, kvm_inout + H, 2 * H, B, 1, Ms, 0, nh, dh, 0,
                 dt, om.data(), H);
   std::vector<float> g = block_tail(c, w, L, x, os, om, B, y);

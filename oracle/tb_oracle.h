@@ -105,8 +105,8 @@ int orc_block_kvm(const orc_block_cfg* c, const orc_block_weights* w, const floa
                   float* kvm_out);
 
 /* One decode step: x, y [B, H] (one new token per sequence, all at position
- * cache_len); k_cache, v_cache [B, max_positions, H] hold positions
- * [0, cache_len) and receive the new token's K, V at cache_len; kvm_inout
+ * cache_len); k_cache, v_cache [B, nh, max_positions, dh] (head-major) hold
+ * positions [0, cache_len) and receive the new token's K, V at cache_len; kvm_inout
  * [Ms, 2H] is the resident K_M | V_M.  With memory_write the bank and K_M |
  * V_M follow the same EMA (K_M | V_M towards c [Wkm;Wvm]^T + b). */
 int orc_block_decode_step(const orc_block_cfg* c, const orc_block_weights* w, float* memory_inout,

@@ -27,19 +27,27 @@ def _round(a, dt):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch_dtype(dt)).float().numpy()
 
 
-def _caches(B, P, H, L, dt, seed, fill=None):
-    """Device caches [B, P, H] whose first L positions hold `fill` [B, L, H]
-    (or seeded N(0,1) values) and the rest a sentinel that must not be read."""
+def _heads(a, nh):
+    """[B, L, H] rows -> head-major [B, nh, L, dh]."""
+    B, L, H = a.shape
+    return np.ascontiguousarray(a.reshape(B, L, nh, H // nh).transpose(0, 2, 1, 3))
+
+
+def _caches(B, P, H, nh, L, dt, seed, fill=None):
+    """Head-major device caches [B, nh, P, dh] whose first L positions hold
+    `fill` ([B, L, H] rows of K and of V) or seeded N(0,1) values, and the
+    rest a sentinel that must not be read."""
     import torch
     from _util import torch_dtype
     rng = np.random.default_rng(seed)
-    k = np.full((B, P, H), 1e4, np.float32)  # a read past the cache would blow up the result
-    v = np.full((B, P, H), -1e4, np.float32)
+    dh = H // nh
+    k = np.full((B, nh, P, dh), 1e4, np.float32)  # a read past the cache would blow up the result
+    v = np.full((B, nh, P, dh), -1e4, np.float32)
     if L:
         kf, vf = fill if fill is not None else (rng.standard_normal((B, L, H)),
                                                 rng.standard_normal((B, L, H)))
-        k[:, :L] = _round(kf, dt)
-        v[:, :L] = _round(vf, dt)
+        k[:, :, :L] = _heads(_round(kf, dt), nh)
+        v[:, :, :L] = _heads(_round(vf, dt), nh)
     td = torch_dtype(dt)
     return (torch.from_numpy(k).to(td).cuda(), torch.from_numpy(v).to(td).cuda(),
             k.copy(), v.copy())
@@ -56,7 +64,7 @@ def test_decode_is_last_row_of_prefill(ltm, orc, scheme, dt, nh):
     x = _round(synthetic.activations(B * S, H, 6), dt)
     y_full, _, kv = orc.block_forward(ocfg, w, x, B, S, return_kv=True)
     kv = kv.reshape(B, S, 2 * H)
-    kd, vd, _, _ = _caches(B, P, H, L, dt, 0, fill=(kv[:, :L, :H], kv[:, :L, H:]))
+    kd, vd, _, _ = _caches(B, P, H, nh, L, dt, 0, fill=(kv[:, :L, :H], kv[:, :L, H:]))
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(w)
     xt = to_device(x.reshape(B, S, H)[:, L], dt)
@@ -64,10 +72,12 @@ def test_decode_is_last_row_of_prefill(ltm, orc, scheme, dt, nh):
     want = y_full.reshape(B, S, H)[:, L]
     assert_close(as_f32(y), want, *TOL[dt], what=f"decode {scheme} {dt} vs prefill row")
     # the step appended the new token's key / value at position L
-    assert_close(as_f32(kd[:, L]), kv[:, L, :H], *TOL[dt], what="appended K")
-    assert_close(as_f32(vd[:, L]), kv[:, L, H:], *TOL[dt], what="appended V")
+    assert_close(as_f32(kd[:, :, L]), _heads(kv[:, L:L + 1, :H], nh)[:, :, 0], *TOL[dt],
+                 what="appended K")
+    assert_close(as_f32(vd[:, :, L]), _heads(kv[:, L:L + 1, H:], nh)[:, :, 0], *TOL[dt],
+                 what="appended V")
     sentinel = _round(np.float32(1e4), dt)
-    assert np.all(as_f32(kd[:, L + 1:]) == sentinel), "positions past the new token were written"
+    assert np.all(as_f32(kd[:, :, L + 1:]) == sentinel), "positions past the new token were written"
     assert ltm.device_error() == 0
     blk.close()
 
@@ -81,7 +91,7 @@ def test_decode_steps_with_memory_write(ltm, orc, scheme, dt, scores):
     w = synthetic.block_weights(H, F, Ms, 7)
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(w)
-    kd, vd, kh, vh = _caches(B, P, H, L0, dt, 8)
+    kd, vd, kh, vh = _caches(B, P, H, nh, L0, dt, 8)
     mem = orc.round_to(w["memory"], ocfg["dtype"])
     kvm = orc.block_kvm(ocfg, w, mem)
     for i in range(steps):
@@ -90,8 +100,8 @@ def test_decode_steps_with_memory_write(ltm, orc, scheme, dt, scores):
         ref = orc.block_decode_step(ocfg, w, x, kh, vh, L0 + i, mem, kvm)
         assert_close(as_f32(y), ref, *TOL[dt], what=f"step {i} {scheme} {dt}")
         # keep the oracle's cache on the device's values so the steps stay comparable
-        kh[:, L0 + i] = as_f32(kd[:, L0 + i])
-        vh[:, L0 + i] = as_f32(vd[:, L0 + i])
+        kh[:, :, L0 + i] = as_f32(kd[:, :, L0 + i])
+        vh[:, :, L0 + i] = as_f32(vd[:, :, L0 + i])
     assert_close(as_f32(blk.memory()), mem, 2e-3, 1e-2, what="bank after the decode writes")
     assert ltm.device_error() == 0
     blk.close()
@@ -109,7 +119,7 @@ def test_decode_long_and_edge_caches(ltm, orc, dt, nh, L):
     w = synthetic.block_weights(H, F, Ms, 9)
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(w)
-    kd, vd, kh, vh = _caches(B, P, H, L, dt, 10)
+    kd, vd, kh, vh = _caches(B, P, H, nh, L, dt, 10)
     mem = orc.round_to(w["memory"], ocfg["dtype"])
     kvm = orc.block_kvm(ocfg, w, mem)
     x = _round(synthetic.activations(B, H, 11), dt)
@@ -129,15 +139,15 @@ def test_decode_after_forward_recomputes_memory_keys(ltm, orc):
     w = synthetic.block_weights(H, F, Ms, 12)
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(w)
-    kd, vd, kh, vh = _caches(B, P, H, 5, dt, 13)
+    kd, vd, kh, vh = _caches(B, P, H, nh, 5, dt, 13)
     x0 = _round(synthetic.activations(B, H, 14), dt)
     blk.decode_step(to_device(x0, dt), kd, vd, 5)  # makes K_M | V_M resident
     xs = _round(synthetic.activations(B * S, H, 15), dt)
     blk(to_device(xs, dt).reshape(B, S, H))  # writes the bank
     mem = as_f32(blk.memory())
     kvm = orc.block_kvm(ocfg, w, mem)
-    kh[:, 5] = as_f32(kd[:, 5])
-    vh[:, 5] = as_f32(vd[:, 5])
+    kh[:, :, 5] = as_f32(kd[:, :, 5])
+    vh[:, :, 5] = as_f32(vd[:, :, 5])
     x1 = _round(synthetic.activations(B, H, 16), dt)
     y = blk.decode_step(to_device(x1, dt), kd, vd, 6)
     ref = orc.block_decode_step(ocfg, w, x1, kh, vh, 6, mem, kvm)
@@ -173,7 +183,7 @@ def test_decode_argument_errors(ltm):
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(synthetic.block_weights(H, F, Ms, 19))
     x = torch.zeros((B, H), dtype=torch.bfloat16, device="cuda")
-    kc = torch.zeros((B, P, H), dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros((B, nh, P, H // nh), dtype=torch.bfloat16, device="cuda")
     vc = torch.zeros_like(kc)
     for bad_len in (P, -1):
         with pytest.raises(ltm.LtmError) as e:
@@ -185,7 +195,7 @@ def test_decode_argument_errors(ltm):
     b32 = ltm.TitanBlock(cfg32, q32)
     b32.load_weights(synthetic.block_weights(H, F, Ms, 19))
     x32 = torch.zeros((B, H), dtype=torch.float32, device="cuda")
-    k32 = torch.zeros((B, P, H), dtype=torch.float32, device="cuda")
+    k32 = torch.zeros((B, nh, P, H // nh), dtype=torch.float32, device="cuda")
     with pytest.raises(ltm.LtmError):
         b32.decode_step(x32, k32, torch.zeros_like(k32), 0)
     assert ltm.device_error() == 0
@@ -205,10 +215,10 @@ def test_cache_manager_decode_loop(ltm, orc):
         b = ltm.TitanBlock(cfg, q)
         b.load_weights(w)
         blocks.append(b)
-    cache = ltm.CacheManager(2, H, __import__("torch").bfloat16)
+    cache = ltm.CacheManager(2, nh, H // nh, __import__("torch").bfloat16)
     cache.allocate(B, P)
-    hk = [np.zeros((B, P, H), np.float32) for _ in ws]
-    hv = [np.zeros((B, P, H), np.float32) for _ in ws]
+    hk = [np.zeros((B, nh, P, H // nh), np.float32) for _ in ws]
+    hv = [np.zeros((B, nh, P, H // nh), np.float32) for _ in ws]
     mems = [orc.round_to(w["memory"], ocfg["dtype"]) for w in ws]
     kvms = [orc.block_kvm(ocfg, w, m) for w, m in zip(ws, mems)]
     for step in range(3):
@@ -219,8 +229,8 @@ def test_cache_manager_decode_loop(ltm, orc):
         for i, w in enumerate(ws):
             cur = orc.block_decode_step(ocfg, w, cur, hk[i], hv[i], pos, mems[i], kvms[i])
             k, v, _ = cache.get(i)
-            hk[i][:, pos] = as_f32(k[:, pos])
-            hv[i][:, pos] = as_f32(v[:, pos])
+            hk[i][:, :, pos] = as_f32(k[:, :, pos])
+            hv[i][:, :, pos] = as_f32(v[:, :, pos])
             cur = _round(cur, dt)
         assert_close(as_f32(y), cur, *TOL[dt], what=f"2-layer decode step {step}")
     assert cache.length == 3
@@ -239,7 +249,7 @@ def test_decode_wide_block_split_k(ltm, orc, dt):
     w = synthetic.block_weights(H, F, Ms, 21)
     blk = ltm.TitanBlock(cfg, q)
     blk.load_weights(w)
-    kd, vd, kh, vh = _caches(B, P, H, L0, dt, 22)
+    kd, vd, kh, vh = _caches(B, P, H, nh, L0, dt, 22)
     mem = orc.round_to(w["memory"], ocfg["dtype"])
     kvm = orc.block_kvm(ocfg, w, mem)
     for i in range(3):
@@ -247,8 +257,8 @@ def test_decode_wide_block_split_k(ltm, orc, dt):
         y = blk.decode_step(to_device(x, dt), kd, vd, L0 + i)
         ref = orc.block_decode_step(ocfg, w, x, kh, vh, L0 + i, mem, kvm)
         assert_close(as_f32(y), ref, *TOL[dt], what=f"wide step {i} {dt}")
-        kh[:, L0 + i] = as_f32(kd[:, L0 + i])
-        vh[:, L0 + i] = as_f32(vd[:, L0 + i])
+        kh[:, :, L0 + i] = as_f32(kd[:, :, L0 + i])
+        vh[:, :, L0 + i] = as_f32(vd[:, :, L0 + i])
     assert_close(as_f32(blk.memory()), mem, 2e-3, 1e-2, what="wide bank after the decode writes")
     assert ltm.device_error() == 0
     blk.close()

@@ -185,12 +185,14 @@ def test_oracle_decode_step_is_last_row_of_forward(orc):
         x = orc.round_to(synthetic.activations(B * S, H, 4), dt)
         y, _, kv = orc.block_forward(ocfg, w, x, B, S, return_kv=True)
         kv = kv.reshape(B, S, 2 * H)
-        kc = np.zeros((B, P, H), np.float32)
-        vc = np.zeros((B, P, H), np.float32)
-        kc[:, :L], vc[:, :L] = kv[:, :L, :H], kv[:, :L, H:]
+        dh = H // nh
+        heads = kv.reshape(B, S, 2, nh, dh).transpose(2, 0, 3, 1, 4)  # K|V, b, head, pos, dim
+        kc = np.zeros((B, nh, P, dh), np.float32)
+        vc = np.zeros((B, nh, P, dh), np.float32)
+        kc[:, :, :L], vc[:, :, :L] = heads[0][:, :, :L], heads[1][:, :, :L]
         mem = orc.round_to(w["memory"], dt)
         kvm = orc.block_kvm(ocfg, w, mem)
         yd = orc.block_decode_step(ocfg, w, x.reshape(B, S, H)[:, L], kc, vc, L, mem, kvm)
         np.testing.assert_array_equal(yd, y.reshape(B, S, H)[:, L])
-        np.testing.assert_array_equal(kc[:, L], kv[:, L, :H])
-        np.testing.assert_array_equal(vc[:, L], kv[:, L, H:])
+        np.testing.assert_array_equal(kc[:, :, L], heads[0][:, :, L])
+        np.testing.assert_array_equal(vc[:, :, L], heads[1][:, :, L])
