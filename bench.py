@@ -63,7 +63,7 @@ def parse():
                     help="launch each kernel of one block once at the workload's shapes (for ncu); "
                          "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2; "
                          "w4a16: the long-context layer's W4A16 GEMMs at 8192 tokens; decode: "
-                         "one decode step of one block at batch 4, 32768 cached positions")
+                         "one decode step of one block at batch 64, 2048 cached positions")
     return ap.parse_args()
 
 
@@ -787,11 +787,12 @@ def run_decode(args, wl: dict = DEC_WL):
 
 
 def probe_decode_case(torch, ltm):
-    """One decode step of one hidden-4096 block at batch 4 against a
-    32768-position cache (2.1 GB), after a warm-up step: every decode kernel
-    launched once more at the workload's per-sequence shapes (for ncu)."""
+    """One decode step of one hidden-4096 block at batch 64 against a
+    2048-position cache (2.1 GB), after a warm-up step: every decode kernel
+    launched once more at the workload's batch (GEMMs at M = 64; the cache
+    kernel with the same tiles, 1/16 of the positions) for ncu."""
     from ltm_b200 import synthetic
-    wl = dict(DEC_WL, B=4)
+    wl = dict(DEC_WL, P=2048)
     B, P, H, F, Ms, nh = (wl[k] for k in ("B", "P", "H", "F", "Ms", "nh"))
     cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
                                memory_slots=Ms)

@@ -162,7 +162,7 @@ void QLinear::load_cols(const ltm_quant_config& q, const float* w_host, const fl
 // Runs y = epilogue(a W^T) for the block's scheme.  a_act: activation in the
 // act dtype (W8A32 / W4A16); aq/as: its per-token int8 codes (W8A8).
 void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode,
-                  ltm_dtype dt, Epilogue ep, cudaStream_t stream, DevBuf* splitk) const {
+                  ltm_dtype dt, Epilogue ep, cudaStream_t stream) const {
   ep.bias = bias.as<float>();
   if (scheme == LTM_SCHEME_W8A8) {
     ep.row_scale = as;
@@ -176,7 +176,7 @@ void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t 
     ep.row_scale = nullptr;
     ep.col_scale = nullptr;
     launch_w4a16(a_act, dt, q4.as<uint8_t>(), s4.as<float>(), z4.as<uint8_t>(), M, N, K, mode, ep,
-                 stream, splitk);
+                 stream);
   }
 }
 
@@ -212,7 +212,6 @@ struct ltm_block {
   // split-cache attention partials
   bool kvm_fresh = false;
   DevBuf crow, cq, cs, kcv, dpart;
-  DevBuf splitk;  // fp32 partials of the small-M (split-K) W4A16 GEMMs
 
   size_t act_bytes() const { return dtype_size(dt); }
 
@@ -286,7 +285,7 @@ struct ltm_block {
     Epilogue ep;
     ep.out = kvmb.ptr;
     ep.ldo = 2 * Hl;
-    kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st, &splitk);
+    kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st);
     kvm_fresh = true;
   }
 
@@ -314,7 +313,7 @@ struct ltm_block {
     ep.seq_len = S;
     ep.head_dim = dh;
     qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
-             ep, st, &splitk);
+             ep, st);
   }
 
   // Memory attention of nb groups of sq query rows against K_M | V_M (the
@@ -353,9 +352,9 @@ struct ltm_block {
       Epilogue ep;
       ep.out = sp;
       ep.ldo = H;
-      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st, &splitk);
+      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st);
       ep.out = mp;
-      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st, &splitk);
+      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st);
     }
     // row-parallel partial sums of s and m (the biases were added by rank 0)
     if (tp > 1) comm_allreduce(comm, spm.ptr, spm.ptr, 2 * T * H, dt, false, st);
@@ -370,7 +369,7 @@ struct ltm_block {
       ep.aux2 = x;
       ep.ld_aux = H;
       if (q.memory_write) mw.prepare_gate_epilogue(ep, H, st);
-      g.run(x, xq.as<int8_t>(), xs.as<float>(), T, kEpiGateMix, dt, ep, st, &splitk);
+      g.run(x, xq.as<int8_t>(), xs.as<float>(), T, kEpiGateMix, dt, ep, st);
     } else {
       launch_add3(sp, mp, x, y.ptr, T * H, dt, st);
     }
@@ -388,7 +387,7 @@ struct ltm_block {
       ep.act = LTM_EPI_GELU;
       ep.out = u.ptr;
       ep.ldo = Fl;
-      w1.run(zin, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st, &splitk);
+      w1.run(zin, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st);
     }
     if (w8a8) quant_rows(u.ptr, T, Fl, uq.as<int8_t>(), us.as<float>(), amax.as<float>(), st);
     {
@@ -400,7 +399,7 @@ struct ltm_block {
       ep.aux0 = y.ptr;
       ep.ld_aux = H;
       w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, tpr == 0 ? kEpiResid : kEpiPlain, dt, ep,
-             st, &splitk);
+             st);
     }
     if (tp > 1) comm_allreduce(comm, out, out, T * H, dt, false, st);
   }
@@ -438,7 +437,7 @@ struct ltm_block {
     Epilogue ep;
     ep.out = kcv.ptr;
     ep.ldo = 2 * Hl;
-    kvm.run(crow.ptr, cq.as<int8_t>(), cs.as<float>(), 1, kEpiPlain, dt, ep, st, &splitk);
+    kvm.run(crow.ptr, cq.as<int8_t>(), cs.as<float>(), 1, kEpiPlain, dt, ep, st);
     launch_rows_ema(kvmb.ptr, 2 * Hl, 2 * Hl, kcv.ptr, wslot, cfg.memory_update_rate, Ms, dt, st);
   }
 

@@ -45,9 +45,8 @@ struct QLinear {
   // weight's scales (row-parallel tensor-parallel layers).
   void load_cols(const ltm_quant_config& q, const float* w_host, const float* b_host, int64_t n,
                  int64_t k, int64_t c0, int64_t nc, cudaStream_t stream);
-  // splitk: workspace of the W4A16 split-K path (small-M GEMMs), or NULL
   void run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode, ltm_dtype dt,
-           Epilogue ep, cudaStream_t stream, DevBuf* splitk = nullptr) const;
+           Epilogue ep, cudaStream_t stream) const;
 };
 
 struct AttnParams {
@@ -133,11 +132,11 @@ void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64
                  ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream);
 void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
                   const Epilogue& ep, cudaStream_t stream);
-// splitk_ws: fp32 partials of the split-K path (grown on demand); NULL keeps
-// one CTA per output tile.
+// split_k: grids smaller than the GPU split K over a cluster of CTAs per
+// output tile (reduced through distributed shared memory).
 void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s4, const uint8_t* z4,
                   int64_t M, int64_t N, int64_t K, int mode, const Epilogue& ep, cudaStream_t stream,
-                  DevBuf* splitk_ws = nullptr);
+                  bool split_k = true);
 void launch_ln_x2(const void* x, ltm_dtype dt, int64_t rows, int H, const float* gamma,
                   const float* beta, void* y, int8_t* yq, float* ys, int8_t* xq, float* xs,
                   bool do_norm, cudaStream_t stream, const void* residual = nullptr);

@@ -218,10 +218,12 @@ __host__ __device__ constexpr int epi_stage_row_bytes() {
   return kEpiPassCols * static_cast<int>(sizeof(StoreT)) + 16;
 }
 
-template <int MODE, class OutT, int BN, bool ACC_INT>
-__device__ __forceinline__ void tc_tile_epilogue_passes(const Epilogue& ep, uint32_t tacc, int q,
-                                                        int lane, int64_t m0, int64_t n0, int M,
-                                                        int N, uint8_t* stg) {
+// The same passes with the 32 accumulator values of a chunk taken from
+// src(c, v) (column chunk c of this lane's row; called by every lane).
+template <int MODE, class OutT, int BN, class Src>
+__device__ __forceinline__ void tile_epilogue_passes_src(const Epilogue& ep, Src&& src, int q,
+                                                         int lane, int64_t m0, int64_t n0, int M,
+                                                         int N, uint8_t* stg) {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
   constexpr int OB = sizeof(StoreT);
   constexpr int ROWB = epi_stage_row_bytes<StoreT>();
@@ -234,18 +236,10 @@ __device__ __forceinline__ void tc_tile_epilogue_passes(const Epilogue& ep, uint
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int c = p * 2 + h;
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tacc + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
-      tmem_wait_ld();
+      float v[32];
+      src(c, v);
       const int64_t n = n0 + c * 32;
       const bool valid = m < M && n < N;
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if constexpr (MODE == kEpiAccI32) v[i] = __int_as_float(static_cast<int>(r[i]));
-        else if constexpr (ACC_INT) v[i] = static_cast<float>(static_cast<int>(r[i]));
-        else v[i] = __uint_as_float(r[i]);
-      }
       if constexpr (MODE == kEpiGateMix) {
         float gx[32];
 #pragma unroll
@@ -272,6 +266,26 @@ __device__ __forceinline__ void tc_tile_epilogue_passes(const Epilogue& ep, uint
     }
     __syncwarp();
   }
+}
+
+template <int MODE, class OutT, int BN, bool ACC_INT>
+__device__ __forceinline__ void tc_tile_epilogue_passes(const Epilogue& ep, uint32_t tacc, int q,
+                                                        int lane, int64_t m0, int64_t n0, int M,
+                                                        int N, uint8_t* stg) {
+  tile_epilogue_passes_src<MODE, OutT, BN>(
+      ep,
+      [&](int c, float (&v)[32]) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tacc + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if constexpr (MODE == kEpiAccI32) v[i] = __int_as_float(static_cast<int>(r[i]));
+          else if constexpr (ACC_INT) v[i] = static_cast<float>(static_cast<int>(r[i]));
+          else v[i] = __uint_as_float(r[i]);
+        }
+      },
+      q, lane, m0, n0, M, N, stg);
 }
 
 // Runtime (mode, out dtype) -> template dispatch used by the launchers.

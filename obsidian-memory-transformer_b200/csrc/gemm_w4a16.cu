@@ -15,11 +15,12 @@
 //               fence it to the async proxy; then the fused epilogue
 // All waits are bounded (common.cuh).
 //
-// Split-K for grids smaller than the GPU (decode, M <= 128): CTA z of the
-// grid's third dimension reduces the K-blocks [z*kps, (z+1)*kps) and dumps its
-// raw fp32 accumulator tile to partials[z] (the int32 store mode of the
-// epilogue, bit for bit); splitk_epilogue_kernel sums the slices in order and
-// applies the fused epilogue.
+// Split-K for grids smaller than the GPU (decode, M <= 128): the grid's third
+// dimension is a thread-block cluster of up to 8 CTAs per output tile; CTA z
+// reduces the K-blocks [z*kps, (z+1)*kps) and parks its fp32 accumulator tile
+// in its own shared memory; after a cluster barrier CTA r sums its share of
+// the tile's rows over the slices (in slice order) through distributed shared
+// memory and applies the fused epilogue.
 #include <memory>
 #include <mutex>
 #include <type_traits>
@@ -33,6 +34,20 @@ namespace {
 
 constexpr int kBM = 128, kBN = 128, kBKe = 64;  // K elements per stage
 constexpr int kStages = 3;
+constexpr int kRedLd = kBN + 4;  // row stride (floats) of a split-K slice in shared memory
+constexpr int kMaxSplits = 8;    // portable cluster size
+
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+static_assert(kBM * (kBN + 4) * 4 <= kStages * (kBM * 128 + kBN * 128 + kBN * 32),
+              "a split-K slice fits in the pipeline stages");
 
 struct W4Smem {
   static constexpr uint32_t kA = kBM * 128;     // 128 rows x 128 bytes
@@ -143,20 +158,37 @@ __global__ void __launch_bounds__(192, 2)
     // ---- transform: packed int4 -> T, 128-byte swizzled K-major rows
     {
       const int n = n0 + t;
+      // group scale / zero-point of this row: the current group's and the next
+      // group's, loaded one group (two K-blocks) before they are needed
+      const float* srow = s4 + static_cast<int64_t>(n) * G;
+      const uint8_t* zrow = z4 + static_cast<int64_t>(n) * G;
+      int gcur = kb0 >> 1;
+      float sc = 0.0f, zp = 0.0f, sc_n = 0.0f, zp_n = 0.0f;
+      if (n < N) {
+        sc = __ldg(srow + gcur);
+        zp = static_cast<float>(__ldg(zrow + gcur));
+        if (gcur + 1 < G) {
+          sc_n = __ldg(srow + gcur + 1);
+          zp_n = static_cast<float>(__ldg(zrow + gcur + 1));
+        }
+      }
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % kStages;
         const uint32_t ph = (kb / kStages) & 1;
+        if (((kb0 + kb) >> 1) != gcur) {
+          gcur = (kb0 + kb) >> 1;
+          sc = sc_n;
+          zp = zp_n;
+          if (n < N && gcur + 1 < G) {
+            sc_n = __ldg(srow + gcur + 1);
+            zp_n = static_cast<float>(__ldg(zrow + gcur + 1));
+          }
+        }
         const bool ok = mbar_wait_bounded(full + s, ph, abort_flag, err, kErrWaitFull);
         if (ok) {
           uint8_t* st = smem + s * L::kStage;
           const uint8_t* prow = st + L::kA + L::kB + t * 32;
           uint8_t* brow = st + L::kA + t * 128;
-          float sc = 0.0f, zp = 0.0f;
-          if (n < N) {
-            const int64_t gi = static_cast<int64_t>(n) * G + ((kb0 + kb) >> 1);
-            sc = __ldg(s4 + gi);
-            zp = static_cast<float>(__ldg(z4 + gi));
-          }
           // q - zp without an int->float conversion: the float with bits
           // 0x4B000000 | q is 2^23 + q exactly, and (2^23 + q) - (2^23 + zp) is
           // exact for 0 <= q, zp <= 15; then one rounding in the multiply, as
@@ -194,13 +226,60 @@ __global__ void __launch_bounds__(192, 2)
                                                               kErrWaitAccum) &&
                                                 !*abort_flag);
     tc_fence_after();
-    using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, T>::type;
-    Epilogue pe = ep;
-    if constexpr (MODE == kEpiAccI32)  // split-K slice: raw fp32 bits into partials[z]
-      pe.out = static_cast<int32_t*>(ep.out) + static_cast<int64_t>(blockIdx.z) * M * N;
-    if (ok)
-      tc_tile_epilogue_passes<MODE, T, kBN, false>(pe, tmem, q, lane, m0, n0, M, N,
-                                                   smem + q * 32 * epi_stage_row_bytes<StoreT>());
+    if (gridDim.z == 1) {
+      if (ok)
+        tc_tile_epilogue_passes<MODE, T, kBN, false>(ep, tmem, q, lane, m0, n0, M, N,
+                                                     smem + q * 32 * epi_stage_row_bytes<T>());
+    } else if (ok) {
+      // this slice's fp32 accumulator tile into this CTA's shared memory
+      // (row-major, rows padded to kRedLd floats), read by the cluster below
+      float* red = reinterpret_cast<float*>(smem);
+      float* row = red + (q * 32 + lane) * kRedLd;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(row + c * 32 + 4 * j) =
+              make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+      }
+    }
+  }
+
+  if (gridDim.z > 1) {
+    // split K over the cluster's CTAs: once every slice is in its CTA's shared
+    // memory, CTA r sums its share of the tile's rows over the slices (slice
+    // order) through distributed shared memory and applies the epilogue
+    __syncwarp();
+    cluster_sync();
+    if (warp >= 2) {
+      const int S = static_cast<int>(gridDim.z);
+      const int r = static_cast<int>(cluster_ctarank());
+      const int rows = min(kBM, M - m0), nch = min(kBN, N - n0) / 32;
+      const int rpc = (rows + S - 1) / S;
+      const int r0 = r * rpc, r1 = min(rows, r0 + rpc);
+      const float* red = reinterpret_cast<const float*>(smem);
+      for (int item = threadIdx.x - 64; item < (r1 - r0) * nch; item += 128) {
+        const int rr = r0 + item / nch, c = item % nch;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+        for (int p = 0; p < S; ++p) {
+          const uint32_t src = mapa_shared(red + rr * kRedLd + c * 32, p);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 t = ld_cluster_f32x4(src + 16 * j);
+            v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+          }
+        }
+        epilogue_store32<MODE, T>(ep, m0 + rr, n0 + c * 32, v);
+      }
+    }
+    __syncwarp();
+    cluster_sync();  // the peers have read this CTA's slice
   }
 
   tc_fence_before();
@@ -211,43 +290,11 @@ __global__ void __launch_bounds__(192, 2)
   }
 }
 
-// Sum of the split-K slices: one warp per 32-column row chunk, lane j summing
-// column j over the slices (coalesced 128-byte reads), then lane 0 applies
-// the fused epilogue to the chunk and stores it.
-template <int MODE, class OutT>
-__global__ void __launch_bounds__(256) splitk_epilogue_kernel(const float* __restrict__ part,
-                                                              int splits, int M, int N,
-                                                              Epilogue ep) {
-  const int nch = N / 32;
-  const int64_t chunk = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (chunk >= static_cast<int64_t>(M) * nch) return;  // whole warps leave together
-  const int m = static_cast<int>(chunk / nch);
-  const int c = static_cast<int>(chunk - static_cast<int64_t>(m) * nch);
-  const float* p = part + static_cast<int64_t>(m) * N + c * 32 + lane;
-  const int64_t slice = static_cast<int64_t>(M) * N;
-  float acc = 0.0f;
-  int z = 0;
-  for (; z + 4 <= splits; z += 4) {
-    const float a0 = __ldg(p + z * slice), a1 = __ldg(p + (z + 1) * slice);
-    const float a2 = __ldg(p + (z + 2) * slice), a3 = __ldg(p + (z + 3) * slice);
-    acc += a0;
-    acc += a1;
-    acc += a2;
-    acc += a3;
-  }
-  for (; z < splits; ++z) acc += __ldg(p + z * slice);
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __shfl_sync(0xffffffffu, acc, i);
-  if (lane == 0) epilogue_store32<MODE, OutT>(ep, m, static_cast<int64_t>(c) * 32, v);
-}
-
 }  // namespace
 
 void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s4, const uint8_t* z4,
                   int64_t M, int64_t N, int64_t K, int mode, const Epilogue& ep, cudaStream_t stream,
-                  DevBuf* splitk_ws) {
+                  bool split_k) {
   LTM_REQUIRE(M >= 0 && N >= 0 && K >= 0, "negative size");
   LTM_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "size exceeds int32");
   if (M == 0 || N == 0) return;
@@ -267,74 +314,44 @@ void launch_w4a16(const void* a, ltm_dtype dt, const uint8_t* q4, const float* s
   const int tiles_n = static_cast<int>((N + kBN - 1) / kBN), tiles_m = static_cast<int>((M + kBM - 1) / kBM);
   const int nkb = static_cast<int>(K / kBKe);
   // split K when the tile grid leaves most SMs idle (two CTAs fit per SM),
-  // with at least 8 K-blocks per slice
+  // with at least 8 K-blocks per slice and at most one cluster of 8 slices
   int splits = 1;
-  if (splitk_ws != nullptr) {
+  if (split_k) {
     const int want = 2 * device_sm_count() / (tiles_n * tiles_m);
-    splits = std::max(1, std::min(want, nkb / 8));
+    splits = std::max(1, std::min(std::min(want, nkb / 8), kMaxSplits));
   }
   const int kps = (nkb + splits - 1) / splits;
   splits = (nkb + kps - 1) / kps;
-  dim3 grid(tiles_n, tiles_m, splits);
-  if (splits > 1) {
-    const size_t need = static_cast<size_t>(splits) * M * N * sizeof(float);
-    splitk_ws->ensure(need);
-    Epilogue pe;
-    pe.out = splitk_ws->ptr;
-    pe.ldo = N;
-    dispatch_dtype(dt, [&](auto tag) {
-      using T = decltype(tag);
-      if constexpr (!std::is_same<T, float>::value) {
-        auto kern = w4a16_tc_kernel<T, kEpiAccI32>;
-        LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          W4Smem::kBytes));
-        kern<<<grid, 192, W4Smem::kBytes, stream>>>(ta, tp, s4, z4, static_cast<int>(M),
-                                                     static_cast<int>(N), static_cast<int>(K), kps,
-                                                     pe, device_error_ptr());
-      }
-    });
-    check_launch("w4a16_tc_kernel/splitk", stream);
-    const int64_t threads = M * N;  // one warp per 32-column row chunk
-    dispatch_epilogue(mode, dt, [&](auto mode_c, auto out_tag) {
-      using OutT = decltype(out_tag);
-      constexpr int MODE = decltype(mode_c)::value;
-      if constexpr (MODE != kEpiAccI32 && !std::is_same<OutT, float>::value)
-        splitk_epilogue_kernel<MODE, OutT><<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
-                                             stream>>>(splitk_ws->as<float>(), splits,
-                                                       static_cast<int>(M), static_cast<int>(N), ep);
-    });
-    check_launch("splitk_epilogue_kernel", stream);
-    return;
-  }
+  const dim3 grid(tiles_n, tiles_m, splits);
   auto go = [&](auto tag, auto mode_c) {
     using T = decltype(tag);
     constexpr int MODE = decltype(mode_c)::value;
     auto kern = w4a16_tc_kernel<T, MODE>;
     LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, W4Smem::kBytes));
-    kern<<<grid, 192, W4Smem::kBytes, stream>>>(ta, tp, s4, z4, static_cast<int>(M),
-                                                 static_cast<int>(N), static_cast<int>(K), kps, ep,
-                                                 device_error_ptr());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = W4Smem::kBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = static_cast<unsigned>(splits);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LTM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tp, s4, z4, static_cast<int>(M),
+                                    static_cast<int>(N), static_cast<int>(K), kps, ep,
+                                    device_error_ptr()));
   };
   dispatch_epilogue(mode, dt, [&](auto mode_c, auto out_tag) {
     using OutT = decltype(out_tag);
     constexpr int MODE = decltype(mode_c)::value;
     if constexpr (MODE != kEpiAccI32 && !std::is_same<OutT, float>::value) go(OutT{}, mode_c);
   });
-  check_launch("w4a16_tc_kernel", stream);
+  check_launch(splits > 1 ? "w4a16_tc_kernel/splitk" : "w4a16_tc_kernel", stream);
 }
 
-namespace {
-// Per-device split-K partials of ltm_linear_w4a16 (grown on demand, held
-// until exit; calls whose GPU work overlaps on one device share it).
-DevBuf& splitk_scratch(int dev) {
-  static std::mutex mu;
-  static std::vector<std::unique_ptr<DevBuf>> per_dev;
-  std::lock_guard<std::mutex> lk(mu);
-  if (static_cast<int>(per_dev.size()) <= dev) per_dev.resize(dev + 1);
-  if (!per_dev[dev]) per_dev[dev] = std::make_unique<DevBuf>();
-  return *per_dev[dev];
-}
-}  // namespace
 
 }  // namespace ltm_b200
 
@@ -352,9 +369,6 @@ extern "C" ltm_status ltm_linear_w4a16(const void* a, ltm_dtype a_dtype, const u
     ep.bias = bias;
     ep.out = y;
     ep.ldo = N;
-    int dev = 0;
-    LTM_CUDA_TRY(cudaGetDevice(&dev));
-    launch_w4a16(a, a_dtype, packed, s, zp, M, N, K, kEpiPlain, ep, as_stream(stream),
-                 &splitk_scratch(dev));
+    launch_w4a16(a, a_dtype, packed, s, zp, M, N, K, kEpiPlain, ep, as_stream(stream), true);
   });
 }
