@@ -114,3 +114,80 @@ def test_tp2_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_wr
         ref2, _ = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S, memory=mem_ref)
         assert_close(y2.reshape(ref2.shape), ref2, *TOL[dt], what="tp2 second forward")
     blk.close()
+
+
+def _decode_worker(rank, n, uid, c, caches, xs, L0, out):
+    sys.path[:0] = [str(ROOT), str(ROOT / "obsidian-memory-transformer_b200")]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import ltm_b200 as ltm
+    from ltm_b200 import synthetic
+    try:
+        torch.cuda.set_device(rank)
+        comm = ltm.Comm(uid, n, rank, rank)
+        cfg, q, _ = _build(ltm, c, comm)
+        blk = ltm.TitanBlock(cfg, q, comm=comm)
+        blk.load_weights(synthetic.block_weights(c["H"], c["F"], c["Ms"], c["seed"]))
+        nhl = c["nh"] // n
+        k, v = (torch.from_numpy(a[:, rank * nhl:(rank + 1) * nhl].copy()).to(
+            torch.bfloat16 if c["dt"] == "bf16" else torch.float16).cuda() for a in caches)
+        ys = []
+        for i, x in enumerate(xs):
+            ys.append(as_f32(blk.decode_step(to_device(x, c["dt"]), k, v, L0 + i)))
+        torch.cuda.synchronize()
+        out.put((rank, ys, as_f32(blk.memory()), ltm.device_error()))
+        blk.close()
+        comm.close()
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        out.put((rank, repr(e), None, -1))
+
+
+@pytest.mark.parametrize("scheme,dt", [("w4a16", "bf16"), ("w8a8", "f16")])
+def test_tp2_decode_matches_oracle(ltm, orc, scheme, dt):
+    """Tensor-parallel decode steps with the memory write: each rank holds its
+    heads of the KV cache; every rank returns the same output, equal to the
+    oracle's decode steps within the dtype tolerance."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from ltm_b200 import synthetic
+    c = _case(scheme, dt, True)
+    H, nh, B, L0, P, steps = c["H"], c["nh"], 3, 40, 48, 3
+    dh = H // nh
+    rng = np.random.default_rng(5)
+    caches = [orc.round_to(rng.standard_normal((B, nh, P, dh)), orc_dtype(dt)) for _ in range(2)]
+    xs = [orc.round_to(synthetic.activations(B, H, 60 + i), orc_dtype(dt)) for i in range(steps)]
+    uid = ltm.comm_unique_id()
+    ctx = mp.get_context("spawn")
+    qu = ctx.Queue()
+    procs = [ctx.Process(target=_decode_worker, args=(r, 2, uid, c, caches, xs, L0, qu))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = {}
+        for _ in procs:
+            r, ys, mem, derr = qu.get(timeout=600)
+            assert not isinstance(ys, str), f"rank {r}: {ys}"
+            assert derr == 0
+            res[r] = (ys, mem)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for i in range(steps):
+        assert np.array_equal(res[0][0][i], res[1][0][i])
+    cfg, _, sch = _build(ltm, c)
+    ocfg = dict(H=H, F=c["F"], nh=nh, dh=dh, Ms=c["Ms"], scheme=sch, dtype=orc_dtype(dt),
+                memory_write=1, use_attention_scores=1, update_rate=cfg.memory_update_rate,
+                use_rotary=1, use_bias=1, use_layer_norm=1, use_memory_gating=1)
+    w = synthetic.block_weights(H, c["F"], c["Ms"], c["seed"])
+    mem = orc.round_to(w["memory"], orc_dtype(dt))
+    kvm = orc.block_kvm(ocfg, w, mem)
+    kh, vh = caches[0].copy(), caches[1].copy()
+    for i, x in enumerate(xs):
+        ref = orc.block_decode_step(ocfg, w, x, kh, vh, L0 + i, mem, kvm)
+        assert_close(res[0][0][i], ref, *TOL[dt], what=f"tp2 decode step {i}")
+    assert_close(res[0][1], mem, 2e-3, 1e-2, what="tp2 bank after the decode writes")
