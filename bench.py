@@ -564,7 +564,7 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False):
     all_ms = sum(ms for name, (n, ms) in kt.result.items())
     roofline = None
     if rank == 0 and not args.no_probe:
-        work = step_work_tp(L, ws, wl, "w4a16_tc_kernel" if w4a16 else "w8a8_tc_kernel")
+        work = step_work_tp(L, ws, wl, "gemm_f16_tc_kernel" if w4a16 else "w8a8_tc_kernel")
         roofline, i8 = roofline_of(kt.result, work, torch)
         if i8:
             kernels["int8_peak_tops_measured"] = round(i8, 1)

@@ -161,8 +161,14 @@ void QLinear::load_cols(const ltm_quant_config& q, const float* w_host, const fl
 
 // Runs y = epilogue(a W^T) for the block's scheme.  a_act: activation in the
 // act dtype (W8A32 / W4A16); aq/as: its per-token int8 codes (W8A8).
+// M from which a W4A16 linear dequantises its weight once into wdq and runs
+// the 16-bit persistent GEMM (every weight tile then serves M / 128 row
+// tiles without being dequantised again); below it the fused kernel
+// dequantises tiles on the fly and reads the packed weight once.
+constexpr int64_t kW4DequantM = 1024;
+
 void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode,
-                  ltm_dtype dt, Epilogue ep, cudaStream_t stream) const {
+                  ltm_dtype dt, Epilogue ep, cudaStream_t stream, DevBuf* wdq) const {
   ep.bias = bias.as<float>();
   if (scheme == LTM_SCHEME_W8A8) {
     ep.row_scale = as;
@@ -172,6 +178,13 @@ void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t 
     ep.row_scale = nullptr;
     ep.col_scale = s8.as<float>();
     launch_w8a32(static_cast<const float*>(a_act), q8.as<int8_t>(), M, N, K, mode, ep, stream);
+  } else if (wdq != nullptr && M >= kW4DequantM) {
+    ep.row_scale = nullptr;
+    ep.col_scale = nullptr;
+    wdq->ensure(static_cast<size_t>(N) * K * dtype_size(dt));
+    launch_int4_dequant_rows(q4.as<uint8_t>(), s4.as<float>(), z4.as<uint8_t>(), N, K, wdq->ptr, dt,
+                             stream);
+    launch_gemm_f16(a_act, wdq->ptr, M, N, K, mode, dt, ep, stream);
   } else {
     ep.row_scale = nullptr;
     ep.col_scale = nullptr;
@@ -212,6 +225,7 @@ struct ltm_block {
   // split-cache attention partials
   bool kvm_fresh = false;
   DevBuf crow, cq, cs, kcv, dpart;
+  DevBuf wdq;  // dequantised weight of the W4A16 GEMMs at large M (one at a time)
 
   size_t act_bytes() const { return dtype_size(dt); }
 
@@ -285,7 +299,7 @@ struct ltm_block {
     Epilogue ep;
     ep.out = kvmb.ptr;
     ep.ldo = 2 * Hl;
-    kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st);
+    kvm.run(memory.ptr, mq.as<int8_t>(), ms.as<float>(), Ms, kEpiPlain, dt, ep, st, &wdq);
     kvm_fresh = true;
   }
 
@@ -313,7 +327,7 @@ struct ltm_block {
     ep.seq_len = S;
     ep.head_dim = dh;
     qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
-             ep, st);
+             ep, st, &wdq);
   }
 
   // Memory attention of nb groups of sq query rows against K_M | V_M (the
@@ -352,9 +366,9 @@ struct ltm_block {
       Epilogue ep;
       ep.out = sp;
       ep.ldo = H;
-      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st);
+      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
       ep.out = mp;
-      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st);
+      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
     }
     // row-parallel partial sums of s and m (the biases were added by rank 0)
     if (tp > 1) comm_allreduce(comm, spm.ptr, spm.ptr, 2 * T * H, dt, false, st);
@@ -369,7 +383,7 @@ struct ltm_block {
       ep.aux2 = x;
       ep.ld_aux = H;
       if (q.memory_write) mw.prepare_gate_epilogue(ep, H, st);
-      g.run(x, xq.as<int8_t>(), xs.as<float>(), T, kEpiGateMix, dt, ep, st);
+      g.run(x, xq.as<int8_t>(), xs.as<float>(), T, kEpiGateMix, dt, ep, st, &wdq);
     } else {
       launch_add3(sp, mp, x, y.ptr, T * H, dt, st);
     }
@@ -387,7 +401,7 @@ struct ltm_block {
       ep.act = LTM_EPI_GELU;
       ep.out = u.ptr;
       ep.ldo = Fl;
-      w1.run(zin, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st);
+      w1.run(zin, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
     }
     if (w8a8) quant_rows(u.ptr, T, Fl, uq.as<int8_t>(), us.as<float>(), amax.as<float>(), st);
     {
@@ -399,7 +413,7 @@ struct ltm_block {
       ep.aux0 = y.ptr;
       ep.ld_aux = H;
       w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, tpr == 0 ? kEpiResid : kEpiPlain, dt, ep,
-             st);
+             st, &wdq);
     }
     if (tp > 1) comm_allreduce(comm, out, out, T * H, dt, false, st);
   }
@@ -437,7 +451,7 @@ struct ltm_block {
     Epilogue ep;
     ep.out = kcv.ptr;
     ep.ldo = 2 * Hl;
-    kvm.run(crow.ptr, cq.as<int8_t>(), cs.as<float>(), 1, kEpiPlain, dt, ep, st);
+    kvm.run(crow.ptr, cq.as<int8_t>(), cs.as<float>(), 1, kEpiPlain, dt, ep, st, &wdq);
     launch_rows_ema(kvmb.ptr, 2 * Hl, 2 * Hl, kcv.ptr, wslot, cfg.memory_update_rate, Ms, dt, st);
   }
 

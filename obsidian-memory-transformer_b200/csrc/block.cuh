@@ -45,8 +45,10 @@ struct QLinear {
   // weight's scales (row-parallel tensor-parallel layers).
   void load_cols(const ltm_quant_config& q, const float* w_host, const float* b_host, int64_t n,
                  int64_t k, int64_t c0, int64_t nc, cudaStream_t stream);
+  // wdq: scratch for the dequantised weight of the W4A16 path at large M
+  // (NULL: the fused dequantising kernel at every M).
   void run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode, ltm_dtype dt,
-           Epilogue ep, cudaStream_t stream) const;
+           Epilogue ep, cudaStream_t stream, DevBuf* wdq = nullptr) const;
 };
 
 struct AttnParams {
@@ -130,6 +132,13 @@ void launch_rowwise_int8_amax(const void* x, ltm_dtype dt, int64_t rows, int64_t
                               const float* amax, int8_t* q, float* s, cudaStream_t stream);
 void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
                  ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream);
+// 16-bit GEMM on the persistent tcgen05 kernels (operands a [M,K], w [N,K]
+// in dt, fp32 accumulation, fused epilogue, output in dt).
+void launch_gemm_f16(const void* a, const void* w, int64_t M, int64_t N, int64_t K, int mode,
+                     ltm_dtype dt, const Epilogue& ep, cudaStream_t stream);
+// INT4 group-128 weight [N,K] dequantised to dt (T((q - zp) * s)).
+void launch_int4_dequant_rows(const uint8_t* packed, const float* s, const uint8_t* zp, int64_t N,
+                              int64_t K, void* out, ltm_dtype dt, cudaStream_t st);
 void launch_w8a32(const float* a, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
                   const Epilogue& ep, cudaStream_t stream);
 // split_k: grids smaller than the GPU split K over a cluster of CTAs per

@@ -415,6 +415,18 @@ __device__ __forceinline__ void tc_mma_i8_pair(uint32_t d_tmem, uint64_t a_desc,
       : "memory");
 }
 
+// CTA-pair MMA (cta_group::2) of f16 / bf16 operands -> fp32, as
+// tc_mma_i8_pair.  Issued by the pair's even-rank CTA only.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A * B^T, f16/bf16 inputs -> fp32.
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {

@@ -492,19 +492,16 @@ struct TmaTileEpilogue {
         else v[i] = __uint_as_float(acc[cur][i]);
       }
       if constexpr (kMath) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= rs;
+        // (acc * rs) * cs + bs, the last two in one FMA
         const float4* cs4 = reinterpret_cast<const float4*>(cvec + c * 32);
         const float4* bs4 = reinterpret_cast<const float4*>(cvec + CW + c * 32);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 s = cs4[j];
-          v[4 * j] *= s.x; v[4 * j + 1] *= s.y; v[4 * j + 2] *= s.z; v[4 * j + 3] *= s.w;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 s = bs4[j];
-          v[4 * j] += s.x; v[4 * j + 1] += s.y; v[4 * j + 2] += s.z; v[4 * j + 3] += s.w;
+          const float4 s = cs4[j], b = bs4[j];
+          v[4 * j] = fmaf(v[4 * j] * rs, s.x, b.x);
+          v[4 * j + 1] = fmaf(v[4 * j + 1] * rs, s.y, b.y);
+          v[4 * j + 2] = fmaf(v[4 * j + 2] * rs, s.z, b.z);
+          v[4 * j + 3] = fmaf(v[4 * j + 3] * rs, s.w, b.w);
         }
         if (ep.act == LTM_EPI_GELU) {
 #pragma unroll

@@ -3,6 +3,12 @@
 //   acc[m,n] = sum_k qa[m,k] * qw[n,k]     int8 x int8 -> exact int32 in TMEM
 //   y        = epilogue(acc)                dequant, bias, act, rope/resid/gate-mix
 //
+// The same kernels, instantiated on 16-bit operands (kind::f16, fp32
+// accumulators; the stage tiling is in bytes, so a 128-byte K row holds 64
+// elements), are the GEMM of the W4A16 linear at large M: the INT4 weight is
+// dequantised once per call into a 16-bit scratch and contracted here
+// (launch_gemm_f16).
+//
 // Persistent kernel, one CTA per SM, static round-robin over 128 x BN output
 // tiles (N-tile fastest, so the CTAs in flight share activation rows and the
 // whole weight stays L2-resident).  Warp roles (320 threads):
@@ -47,12 +53,32 @@ struct W8A8Smem {
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
 };
 
-template <int BN, int STAGES, int MODE, class OutT>
+// MMA of one 32-byte K slice: int8 (kind::i8) or 16-bit (kind::f16) operands.
+template <class AT, bool PAIR>
+__device__ __forceinline__ void mma_k32(uint32_t tacc, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  if constexpr (sizeof(AT) == 1) {
+    if constexpr (PAIR) tc_mma_i8_pair(tacc, a, b, idesc, acc);
+    else tc_mma_i8(tacc, a, b, idesc, acc);
+  } else {
+    if constexpr (PAIR) tc_mma_f16_pair(tacc, a, b, idesc, acc);
+    else tc_mma_f16(tacc, a, b, idesc, acc);
+  }
+}
+
+template <class AT>
+__host__ __device__ constexpr uint32_t idesc_of(int M, int N) {
+  if constexpr (sizeof(AT) == 1) return idesc_i8(M, N);
+  else return idesc_f16(M, N, std::is_same<AT, __nv_bfloat16>::value);
+}
+
+template <int BN, int STAGES, int MODE, class OutT, class AT>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, int M, int N, int K, Epilogue ep,
                    int* err) {
   using L = W8A8Smem<BN, STAGES>;
+  constexpr int kKe = kBK / static_cast<int>(sizeof(AT));  // K elements per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -68,7 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN;
   const int tiles = ((M + kBM - 1) / kBM) * num_n;
-  const int nkb = (K + kBK - 1) / kBK;
+  const int nkb = (K + kKe - 1) / kKe;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -103,8 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait_bounded(empty + s, ph ^ 1, abort_flag, err, kErrWaitEmpty)) break;
           uint8_t* a_dst = smem + s * L::kStage;
           mbar_arrive_expect_tx(full + s, L::kStage);
-          tma_load_2d(a_dst, &tmA, full + s, kb * kBK, m0);
-          tma_load_2d(a_dst + L::kA, &tmB, full + s, kb * kBK, n0);
+          tma_load_2d(a_dst, &tmA, full + s, kb * kKe, m0);
+          tma_load_2d(a_dst + L::kA, &tmB, full + s, kb * kKe, n0);
           ++it;
         }
       }
@@ -117,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(kBM, BN);
+      constexpr uint32_t idesc = idesc_of<AT>(kBM, BN);
       int it = 0, lt = 0;
       for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++lt) {
         const int b = lt & 1;
@@ -138,8 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + L::kA;
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
-            tc_mma_i8(tacc, make_desc_kmajor_sw128(a_addr + k * 32),
-                      make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+            mma_k32<AT, false>(tacc, make_desc_kmajor_sw128(a_addr + k * 32),
+                               make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
           }
           tc_commit(empty + s);
           ++it;
@@ -160,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
     float* cvec = reinterpret_cast<float*>(smem + L::kColOff + (warp - 2) * L::kColWarp);
-    TmaTileEpilogue<MODE, OutT, BN / 2, true> epi;
+    TmaTileEpilogue<MODE, OutT, BN / 2, sizeof(AT) == 1> epi;
     auto rows_of = [&](int t) { return (t / num_n) * kBM + q * 32; };
     auto cols_of = [&](int t) { return (t % num_n) * BN + half * (BN / 2); };
     if (static_cast<int>(blockIdx.x) < tiles)
@@ -222,7 +248,7 @@ struct W8A8PairSmem {
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;
 };
 
-template <int MODE, class OutT>
+template <int MODE, class OutT, class AT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     w8a8_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -231,6 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   using L = W8A8PairSmem;
   constexpr int BN = kPairBN;
   constexpr int STAGES = kPairStages;
+  constexpr int kKe = kBK / static_cast<int>(sizeof(AT));  // K elements per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -250,7 +277,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int npairs = static_cast<int>(gridDim.x >> 1);
   const int num_n = (N + BN - 1) / BN;
   const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * num_n;
-  const int nkb = (K + kBK - 1) / kBK;
+  const int nkb = (K + kKe - 1) / kKe;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -288,8 +315,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* a_dst = smem + s * L::kStage;
           if (leader) mbar_arrive_expect_tx(full + s, 2 * L::kStage);
           const uint32_t fb = full0 + static_cast<uint32_t>(s) * 8u;
-          tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, m0);
-          tma_load_2d_pair(a_dst + L::kA, &tmB, fb, kb * kBK, n0);
+          tma_load_2d_pair(a_dst, &tmA, fb, kb * kKe, m0);
+          tma_load_2d_pair(a_dst + L::kA, &tmB, fb, kb * kKe, n0);
           ++it;
         }
       }
@@ -302,7 +329,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(2 * kBM, BN);
+      constexpr uint32_t idesc = idesc_of<AT>(2 * kBM, BN);
       int it = 0, lt = 0;
       for (int t = pair; t < tiles && !*abort_flag; t += npairs, ++lt) {
         const int b = lt % kPairAccBufs;
@@ -323,8 +350,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + L::kA;
 #pragma unroll
           for (int k = 0; k < kBK / 32; ++k) {
-            tc_mma_i8_pair(tacc, make_desc_kmajor_sw128(a_addr + k * 32),
-                           make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+            mma_k32<AT, true>(tacc, make_desc_kmajor_sw128(a_addr + k * 32),
+                              make_desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
           }
           tc_commit_pair_mc(empty + s, 0x3);
           ++it;
@@ -346,7 +373,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
     float* cvec = reinterpret_cast<float*>(smem + L::kColOff + (warp - 2) * L::kColWarp);
     const uint32_t acce0 = mapa_shared(acce, 0);  // the even CTA's acce[0]
-    TmaTileEpilogue<MODE, OutT, BN / 2, true, 128> epi;
+    TmaTileEpilogue<MODE, OutT, BN / 2, sizeof(AT) == 1, 128> epi;
     auto rows_of = [&](int t) {
       return (t / num_n) * (2 * kBM) + static_cast<int>(rank) * kBM + q * 32;
     };
@@ -381,59 +408,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int MODE, class OutT>
-void launch_w8a8_pair(const int8_t* qa, const int8_t* qw, int M, int N, int K, const Epilogue& ep,
+constexpr const char* kNamesI8[] = {"w8a8_tc_kernel/plain", "w8a8_tc_kernel/rope",
+                                     "w8a8_tc_kernel/resid", "w8a8_tc_kernel/gatemix",
+                                     "w8a8_tc_kernel/acc_i32"};
+constexpr const char* kNamesF16[] = {"gemm_f16_tc_kernel/plain", "gemm_f16_tc_kernel/rope",
+                                      "gemm_f16_tc_kernel/resid", "gemm_f16_tc_kernel/gatemix",
+                                      "gemm_f16_tc_kernel/acc"};
+
+template <class AT>
+void operand_maps(CUtensorMap* ta, CUtensorMap* tb, const void* qa, const void* qw, int M, int N,
+                  int K, int b_rows) {
+  constexpr int el = static_cast<int>(sizeof(AT));
+  make_tma_2d(ta, qa, tma_dtype_of<AT>(), el, M, K, K, kBK / el, kBM);
+  make_tma_2d(tb, qw, tma_dtype_of<AT>(), el, N, K, K, kBK / el, b_rows);
+}
+
+template <int MODE, class OutT, class AT>
+void launch_w8a8_pair(const void* qa, const void* qw, int M, int N, int K, const Epilogue& ep,
                       cudaStream_t stream) {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
   using L = W8A8PairSmem;
   static_assert(L::kBytes <= 232448, "shared memory budget exceeded");
   CUtensorMap ta, tb, to;
-  make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
-  make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, kPairBN / 2);
+  operand_maps<AT>(&ta, &tb, qa, qw, M, N, K, kPairBN / 2);
   constexpr int ob = static_cast<int>(sizeof(StoreT));
   make_tma_2d(&to, ep.out, tma_dtype_of<StoreT>(), ob, M, N, ep.ldo, 128 / ob, 32);
-  auto kern = w8a8_tc_pair_kernel<MODE, OutT>;
+  auto kern = w8a8_tc_pair_kernel<MODE, OutT, AT>;
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kPairBN - 1) / kPairBN);
   const int pairs_max = device_sm_count() / 2;
   const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
   kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, ep, device_error_ptr());
-  static const char* const kNames[] = {"w8a8_tc_kernel/plain", "w8a8_tc_kernel/rope",
-                                      "w8a8_tc_kernel/resid", "w8a8_tc_kernel/gatemix",
-                                      "w8a8_tc_kernel/acc_i32"};
-  check_launch(kNames[MODE], stream);
+  check_launch(sizeof(AT) == 1 ? kNamesI8[MODE] : kNamesF16[MODE], stream);
 }
 
-template <int BN, int STAGES, int MODE, class OutT>
-void launch_w8a8_inst(const int8_t* qa, const int8_t* qw, int M, int N, int K, const Epilogue& ep,
+template <int BN, int STAGES, int MODE, class OutT, class AT>
+void launch_w8a8_inst(const void* qa, const void* qw, int M, int N, int K, const Epilogue& ep,
                       cudaStream_t stream) {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
   using L = W8A8Smem<BN, STAGES>;
   static_assert(L::kBytes <= 232448, "shared memory budget exceeded");
   CUtensorMap ta, tb, to;
-  make_tma_2d(&ta, qa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, K, kBK, kBM);
-  make_tma_2d(&tb, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, K, kBK, BN);
+  operand_maps<AT>(&ta, &tb, qa, qw, M, N, K, BN);
   constexpr int ob = static_cast<int>(sizeof(StoreT));
   make_tma_2d(&to, ep.out, tma_dtype_of<StoreT>(), ob, M, N, ep.ldo, 128 / ob, 32);
-  auto kern = w8a8_tc_kernel<BN, STAGES, MODE, OutT>;
+  auto kern = w8a8_tc_kernel<BN, STAGES, MODE, OutT, AT>;
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
   kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, ep, device_error_ptr());
-  static const char* const kNames[] = {"w8a8_tc_kernel/plain", "w8a8_tc_kernel/rope",
-                                      "w8a8_tc_kernel/resid", "w8a8_tc_kernel/gatemix",
-                                      "w8a8_tc_kernel/acc_i32"};
-  check_launch(kNames[MODE], stream);
+  check_launch(sizeof(AT) == 1 ? kNamesI8[MODE] : kNamesF16[MODE], stream);
 }
 
-}  // namespace
-
-// Launches the W8A8 GEMM with the given epilogue. qa: [M,K], qw: [N,K].
-void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
-                 ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream) {
+void check_gemm_args(const void* qa, const void* qw, int64_t M, int64_t N, int64_t K, int mode,
+                     ltm_dtype out_dt, const Epilogue& ep) {
   LTM_REQUIRE(M >= 0 && N >= 0 && K >= 0, "negative size");
   LTM_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "size exceeds int32");
-  if (M == 0 || N == 0) return;
   LTM_REQUIRE(K > 0, "K must be positive");
   LTM_REQUIRE(K % 16 == 0, "K must be a multiple of 16");
   LTM_REQUIRE(N % 32 == 0, "N must be a multiple of 32");
@@ -447,17 +477,52 @@ void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64
   if (mode == kEpiResid || mode == kEpiGateMix) {
     LTM_REQUIRE((ep.ld_aux * osz) % 16 == 0, "aux row stride must be a multiple of 16 bytes");
   }
+}
+
+template <class AT>
+void launch_gemm_tc(const void* qa, const void* qw, int64_t M, int64_t N, int64_t K, int mode,
+                    ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream) {
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   dispatch_epilogue(mode, out_dt, [&](auto mode_c, auto out_tag) {
     constexpr int MODE = decltype(mode_c)::value;
     using OutT = decltype(out_tag);
-    if (N % 256 == 0 && M >= 2 * kBM)
-      launch_w8a8_pair<MODE, OutT>(qa, qw, m, n, k, ep, stream);
-    else if (N % 256 == 0)
-      launch_w8a8_inst<256, 3, MODE, OutT>(qa, qw, m, n, k, ep, stream);
-    else
-      launch_w8a8_inst<128, 4, MODE, OutT>(qa, qw, m, n, k, ep, stream);
+    if constexpr (sizeof(AT) == 1 || (MODE != kEpiAccI32 && !std::is_same<OutT, float>::value)) {
+      if (N % 256 == 0 && M >= 2 * kBM)
+        launch_w8a8_pair<MODE, OutT, AT>(qa, qw, m, n, k, ep, stream);
+      else if (N % 256 == 0)
+        launch_w8a8_inst<256, 3, MODE, OutT, AT>(qa, qw, m, n, k, ep, stream);
+      else
+        launch_w8a8_inst<128, 4, MODE, OutT, AT>(qa, qw, m, n, k, ep, stream);
+    } else {
+      LTM_REQUIRE(false, "16-bit GEMM stores 16-bit outputs");
+    }
   });
+}
+
+}  // namespace
+
+// Launches the W8A8 GEMM with the given epilogue. qa: [M,K], qw: [N,K].
+void launch_w8a8(const int8_t* qa, const int8_t* qw, int64_t M, int64_t N, int64_t K, int mode,
+                 ltm_dtype out_dt, const Epilogue& ep, cudaStream_t stream) {
+  if (M == 0 || N == 0) return;
+  check_gemm_args(qa, qw, M, N, K, mode, out_dt, ep);
+  launch_gemm_tc<int8_t>(qa, qw, M, N, K, mode, out_dt, ep, stream);
+}
+
+// 16-bit GEMM (f16 or bf16 operands a [M,K], w [N,K] of dtype dt; fp32
+// accumulation) with the fused epilogue, output in dt.
+void launch_gemm_f16(const void* a, const void* w, int64_t M, int64_t N, int64_t K, int mode,
+                     ltm_dtype dt, const Epilogue& ep, cudaStream_t stream) {
+  if (M == 0 || N == 0) return;
+  LTM_REQUIRE(dt == LTM_DTYPE_F16 || dt == LTM_DTYPE_BF16, "16-bit GEMM operands are f16 or bf16");
+  LTM_REQUIRE(mode != kEpiAccI32, "no raw accumulator mode on the 16-bit GEMM");
+  check_gemm_args(a, w, M, N, K, mode, dt, ep);
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
+              "operands must be 16-byte aligned");
+  if (dt == LTM_DTYPE_BF16)
+    launch_gemm_tc<__nv_bfloat16>(a, w, M, N, K, mode, dt, ep, stream);
+  else
+    launch_gemm_tc<__half>(a, w, M, N, K, mode, dt, ep, stream);
 }
 
 }  // namespace ltm_b200

@@ -236,6 +236,42 @@ __global__ void __launch_bounds__(256) int4_dequant_kernel(const uint8_t* __rest
   }
 }
 
+// int4_dequant_kernel on 32 weights (16 packed bytes, one group's quarter)
+// per thread: W[n,k] = T((q - zp) * s), the same arithmetic; K % 128 == 0.
+template <class T>
+__global__ void __launch_bounds__(256) int4_dequant_rows_kernel(const uint8_t* __restrict__ packed,
+                                                                const float* __restrict__ s,
+                                                                const uint8_t* __restrict__ zp,
+                                                                int64_t N, int K,
+                                                                T* __restrict__ out) {
+  const int cpr = K / 32;  // 32-weight chunks per row
+  const int64_t total = N * cpr;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t n = i / cpr;
+    const int c = static_cast<int>(i - n * cpr);
+    const int64_t gi = n * (K / 128) + c / 4;
+    const float sc = __ldg(s + gi);
+    const float z = static_cast<float>(__ldg(zp + gi));
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(packed + n * (K / 2)) + c);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint4 o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      T* e = reinterpret_cast<T*>(&o[j]);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t byte = (w[j] >> (8 * b)) & 0xFFu;
+        e[2 * b] = from_f32<T>((static_cast<float>(byte & 0xFu) - z) * sc);
+        e[2 * b + 1] = from_f32<T>((static_cast<float>(byte >> 4) - z) * sc);
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + n * K) + c * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = o[j];
+  }
+}
+
 int elementwise_grid(int64_t total) {
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
@@ -444,6 +480,24 @@ extern "C" ltm_status ltm_quantize_int4_grouped(const void* w, ltm_dtype w_dtype
     check_launch("int4_group_quant_kernel", as_stream(stream));
   });
 }
+
+namespace ltm_b200 {
+void launch_int4_dequant_rows(const uint8_t* packed, const float* s, const uint8_t* zp, int64_t N,
+                              int64_t K, void* out, ltm_dtype dt, cudaStream_t st) {
+  LTM_REQUIRE(K % 128 == 0 && K < (1ll << 31), "K must be a multiple of 128");
+  LTM_REQUIRE(dt != LTM_DTYPE_F32, "16-bit dequantised weights");
+  LTM_REQUIRE((reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(out)) % 16 == 0,
+              "packed weights and output must be 16-byte aligned");
+  const int64_t total = N * (K / 32);
+  const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, device_sm_count() * 16));
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    int4_dequant_rows_kernel<T><<<grid, 256, 0, st>>>(packed, s, zp, N, static_cast<int>(K),
+                                                      static_cast<T*>(out));
+  });
+  check_launch("int4_dequant_rows_kernel", st);
+}
+}  // namespace ltm_b200
 
 extern "C" ltm_status ltm_dequantize_int4_grouped(const uint8_t* packed, const float* s,
                                                   const uint8_t* zp, int64_t N, int64_t K,

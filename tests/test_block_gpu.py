@@ -161,3 +161,24 @@ def test_model_embedding_and_layers(ltm, orc, scheme, dt):
     ref = orc.model_forward(ocfg, layers, emb, tok, B, S)
     assert_close(as_f32(y).reshape(ref.shape), ref, *TOL[dt], what=f"model {scheme}")
     model.close()
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("H,nh,F", [(256, 4, 512), (384, 3, 768)])
+def test_block_w4a16_large_m(ltm, orc, dt, H, nh, F):
+    """W4A16 at M >= 1024 tokens: every linear dequantises its INT4 weight
+    once and runs the persistent 16-bit tcgen05 GEMM (CTA-pair tiles when N is
+    a multiple of 256, 128-wide tiles otherwise) with each fused epilogue;
+    1024 memory slots take the same path for K_M / V_M; the memory write and
+    a second forward over the written bank."""
+    blk, w, xd, y, ref, mem_ref, ocfg = run_block(ltm, orc, "w4a16", dt, H=H, nh=nh, F=F,
+                                                  Ms=1024, B=2, S=640, seed=4,
+                                                  memory_write=True)
+    assert_close(as_f32(y).reshape(ref.shape), ref, *TOL[dt], what=f"w4a16 large-M {dt} H{H}")
+    assert_close(as_f32(blk.memory()), mem_ref, 2e-3, 1e-2, what="bank after the write")
+    B, S = 2, 640
+    y2 = blk(xd)
+    ref2, _ = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S, memory=mem_ref)
+    assert_close(as_f32(y2).reshape(ref2.shape), ref2, *TOL[dt], what="second forward")
+    assert ltm.device_error() == 0
+    blk.close()
