@@ -62,7 +62,7 @@ def parse():
                     choices=["prefill", "tp", "w4a16", "decode"],
                     help="launch each kernel of one block once at the workload's shapes (for ncu); "
                          "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2; "
-                         "w4a16: the long-context layer's W4A16 GEMMs at 8192 tokens; decode: "
+                         "w4a16: one long-context block forward at 1 x 8192 tokens; decode: "
                          "one decode step of one block at batch 64, 2048 cached positions")
     return ap.parse_args()
 
@@ -387,18 +387,24 @@ def probe_tp_case(torch, ltm):
 
 
 def probe_w4a16_case(torch, ltm):
-    """One launch each of the long-context layer's W4A16 GEMM shapes at 8192
-    tokens (FFN up 11008 x 4096, FFN down 4096 x 11008), bf16."""
-    dev = torch.device("cuda")
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(0)
-    M = 8192
-    for N, K in ((11008, 4096), (4096, 11008)):
-        a = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
-        w = (torch.randn((N, K), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
-        packed, s, zp = ltm.quantize_int4_grouped(w)
-        ltm.linear_w4a16(a, packed, s, zp)
+    """One forward of one long-context block (hidden 4096, 32 heads, FFN 11008,
+    4096 slots, W4A16, bf16) at 1 x 8192 tokens, after a warm-up forward: the
+    weight dequantisation pre-pass and the 16-bit GEMMs at the workload's
+    per-sequence shapes (for ncu)."""
+    from ltm_b200 import synthetic
+    wl = W4_WL
+    H, F, Ms, nh, S = wl["H"], wl["F"], wl["Ms"], wl["nh"], wl["S"]
+    cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
+                               memory_slots=Ms)
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W4A16, act_dtype=ltm.DTYPE_BF16)
+    blk = ltm.TitanBlock(cfg, q)
+    blk.load_weights(synthetic.block_weights(H, F, Ms, 1000))
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.randn((1, S, H), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    blk(x)
+    blk(x)
     torch.cuda.synchronize()
+    blk.close()
 
 
 def int8_peak(torch):

@@ -11,7 +11,10 @@
 //
 // Persistent kernel, one CTA per SM, static round-robin over 128 x BN output
 // tiles (N-tile fastest, so the CTAs in flight share activation rows and the
-// whole weight stays L2-resident).  Warp roles (320 threads):
+// whole weight stays L2-resident; for weights too large for L2 -- the 16-bit
+// instantiation at hidden 4096 -- M-tile fastest inside groups of gm row
+// blocks, so a group's activation band stays L2-resident while the weight
+// streams once per group).  Warp roles (320 threads):
 //   warp 0      TMA producer: 128 x 128-byte tiles of qa and BN x 128-byte
 //               tiles of qw into a STAGES-deep ring (128-byte swizzle); runs
 //               ahead across tile boundaries
@@ -27,6 +30,7 @@
 //
 // Replaces the CUTLASS 2.x Sm80 half GEMM of the reference
 // (src/core/ops/mma_ops.cu:20-92) for the quantized linears.
+#include <algorithm>
 #include <type_traits>
 
 #include "block.cuh"
@@ -72,10 +76,26 @@ __host__ __device__ constexpr uint32_t idesc_of(int M, int N) {
   else return idesc_f16(M, N, std::is_same<AT, __nv_bfloat16>::value);
 }
 
+// Row / column block of tile t: N fastest when gm <= 0, else M fastest
+// inside groups of gm row blocks (the last group may be shorter).
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int gm, int& mb,
+                                            int& nb) {
+  if (gm <= 0) {
+    mb = t / num_n;
+    nb = t - mb * num_n;
+    return;
+  }
+  const int per = gm * num_n;
+  const int g = t / per, r = t - g * per;
+  const int mg = min(gm, num_m - g * gm);
+  mb = g * gm + r % mg;
+  nb = r / mg;
+}
+
 template <int BN, int STAGES, int MODE, class OutT, class AT>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, Epilogue ep,
+                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, int gm, Epilogue ep,
                    int* err) {
   using L = W8A8Smem<BN, STAGES>;
   constexpr int kKe = kBK / static_cast<int>(sizeof(AT));  // K elements per stage
@@ -93,7 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_n = (N + BN - 1) / BN;
-  const int tiles = ((M + kBM - 1) / kBM) * num_n;
+  const int num_m = (M + kBM - 1) / kBM;
+  const int tiles = num_m * num_n;
   const int nkb = (K + kKe - 1) / kKe;
 
   if (threadIdx.x == 0) {
@@ -122,7 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0;
       for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-        const int m0 = (t / num_n) * kBM, n0 = (t % num_n) * BN;
+        int mb, nb;
+        tile_coords(t, num_m, num_n, gm, mb, nb);
+        const int m0 = mb * kBM, n0 = nb * BN;
         for (int kb = 0; kb < nkb; ++kb) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -187,8 +210,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
     float* cvec = reinterpret_cast<float*>(smem + L::kColOff + (warp - 2) * L::kColWarp);
     TmaTileEpilogue<MODE, OutT, BN / 2, sizeof(AT) == 1> epi;
-    auto rows_of = [&](int t) { return (t / num_n) * kBM + q * 32; };
-    auto cols_of = [&](int t) { return (t % num_n) * BN + half * (BN / 2); };
+    auto rows_of = [&](int t) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, gm, mb, nb);
+      return mb * kBM + q * 32;
+    };
+    auto cols_of = [&](int t) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, gm, mb, nb);
+      return nb * BN + half * (BN / 2);
+    };
     if (static_cast<int>(blockIdx.x) < tiles)
       epi.prefetch(ep, rows_of(blockIdx.x) + lane, cols_of(blockIdx.x), M, N, lane);
     int lt = 0;
@@ -252,8 +283,8 @@ template <int MODE, class OutT, class AT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     w8a8_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmO, int M, int N, int K, Epilogue ep,
-                        int* err) {
+                        const __grid_constant__ CUtensorMap tmO, int M, int N, int K, int gm,
+                        Epilogue ep, int* err) {
   using L = W8A8PairSmem;
   constexpr int BN = kPairBN;
   constexpr int STAGES = kPairStages;
@@ -276,7 +307,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int npairs = static_cast<int>(gridDim.x >> 1);
   const int num_n = (N + BN - 1) / BN;
-  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * num_n;
+  const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  const int tiles = num_m * num_n;
   const int nkb = (K + kKe - 1) / kKe;
 
   if (threadIdx.x == 0) {
@@ -306,8 +338,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t full0 = mapa_shared(full, 0);  // the even CTA's full[0]
       int it = 0;
       for (int t = pair; t < tiles && !*abort_flag; t += npairs) {
-        const int m0 = (t / num_n) * (2 * kBM) + static_cast<int>(rank) * kBM;
-        const int n0 = (t % num_n) * BN + static_cast<int>(rank) * (BN / 2);
+        int mb, nb;
+        tile_coords(t, num_m, num_n, gm, mb, nb);
+        const int m0 = mb * (2 * kBM) + static_cast<int>(rank) * kBM;
+        const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < nkb; ++kb) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -375,9 +409,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t acce0 = mapa_shared(acce, 0);  // the even CTA's acce[0]
     TmaTileEpilogue<MODE, OutT, BN / 2, sizeof(AT) == 1, 128> epi;
     auto rows_of = [&](int t) {
-      return (t / num_n) * (2 * kBM) + static_cast<int>(rank) * kBM + q * 32;
+      int mb, nb;
+      tile_coords(t, num_m, num_n, gm, mb, nb);
+      return mb * (2 * kBM) + static_cast<int>(rank) * kBM + q * 32;
     };
-    auto cols_of = [&](int t) { return (t % num_n) * BN + half * (BN / 2); };
+    auto cols_of = [&](int t) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, gm, mb, nb);
+      return nb * BN + half * (BN / 2);
+    };
     if (pair < tiles) epi.prefetch(ep, rows_of(pair) + lane, cols_of(pair), M, N, lane);
     int lt = 0;
     for (int t = pair; t < tiles; t += npairs, ++lt) {
@@ -423,6 +463,17 @@ void operand_maps(CUtensorMap* ta, CUtensorMap* tb, const void* qa, const void* 
   make_tma_2d(tb, qw, tma_dtype_of<AT>(), el, N, K, K, kBK / el, b_rows);
 }
 
+// Row-block group of the rasterization: N fastest (0) while the weight fits
+// a third of L2; else the number of row blocks whose activation band fits a
+// 48 MiB share of L2.
+template <class AT>
+int raster_group(int rows_per_block, int N, int K) {
+  const int64_t el = sizeof(AT);
+  if (static_cast<int64_t>(N) * K * el <= (42ll << 20)) return 0;
+  const int64_t band = static_cast<int64_t>(rows_per_block) * K * el;
+  return static_cast<int>(std::max<int64_t>(1, (48ll << 20) / band));
+}
+
 template <int MODE, class OutT, class AT>
 void launch_w8a8_pair(const void* qa, const void* qw, int M, int N, int K, const Epilogue& ep,
                       cudaStream_t stream) {
@@ -438,7 +489,8 @@ void launch_w8a8_pair(const void* qa, const void* qw, int M, int N, int K, const
   const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kPairBN - 1) / kPairBN);
   const int pairs_max = device_sm_count() / 2;
   const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
-  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, ep, device_error_ptr());
+  const int gm = raster_group<AT>(2 * kBM, N, K);
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, gm, ep, device_error_ptr());
   check_launch(sizeof(AT) == 1 ? kNamesI8[MODE] : kNamesF16[MODE], stream);
 }
 
@@ -456,7 +508,8 @@ void launch_w8a8_inst(const void* qa, const void* qw, int M, int N, int K, const
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
-  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, ep, device_error_ptr());
+  const int gm = raster_group<AT>(kBM, N, K);
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, gm, ep, device_error_ptr());
   check_launch(sizeof(AT) == 1 ? kNamesI8[MODE] : kNamesF16[MODE], stream);
 }
 
