@@ -130,19 +130,28 @@ __device__ __forceinline__ float recip_or_zero(float s) { return s == 0.0f ? 0.0
 
 // Warp-cooperative form of quant_i8_exact for V values per lane; must be
 // called by all 32 lanes (lanes without data pass zeros).  Off the rounding
-// ties round-half-even (cvt.rni) equals round-half-away, so the common path is
-// one multiply and one convert; only when some lane of the warp holds a value
-// near a tie does the warp evaluate the IEEE quotients (warp-uniform branch).
+// ties round-half-even equals round-half-away, so the common path rounds with
+// the 1.5 * 2^23 shift (for |t| < 2^22, t + 1.5 * 2^23 holds round-half-even(t)
+// in its low mantissa bits, whose low byte is the two's-complement int8 code)
+// -- about five instructions per value, none on the conversion unit.  Its
+// near-tie test is wider than quant_i8_exact's: |t| <= 127.5 makes
+// |t| * 2^-20 <= 1.22e-4, so every value within 2^-20 |t| of a tie is within
+// 1.22e-4 of it; a warp holding such a value takes the IEEE quotients of
+// quant_i8_exact, so the codes equal quant_i8_exact's.  Requires
+// |v| <= 127 |s| (s is the row's, or a larger, absmax / 127), so that codes
+// stay within [-127, 127] without a clamp; s = 0 gives inv_s = 0 and code 0.
 template <int V>
 __device__ __forceinline__ void quant_i8_exact_warp(const float (&v)[V], float s, float inv_s,
                                                     int8_t (&out)[V]) {
-  float t[V];
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kTie = 0.5f - 1.220703125e-4f;  // 0.5 - 2^-13
+  float big[V];
   bool near_tie = false;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    t[i] = v[i] * inv_s;
-    const float a = fabsf(t[i]);
-    near_tie |= fabsf((a - floorf(a)) - 0.5f) <= a * 9.5367431640625e-07f;  // 2^-20
+    const float t = v[i] * inv_s;
+    big[i] = __fadd_rn(t, kShift);
+    near_tie |= fabsf(__fsub_rn(t, __fsub_rn(big[i], kShift))) >= kTie;
   }
   if (__any_sync(0xffffffffu, near_tie)) {
 #pragma unroll
@@ -150,11 +159,7 @@ __device__ __forceinline__ void quant_i8_exact_warp(const float (&v)[V], float s
     return;
   }
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    int q = __float2int_rn(t[i]);
-    q = max(-127, min(127, q));
-    out[i] = static_cast<int8_t>(s == 0.0f ? 0 : q);
-  }
+  for (int i = 0; i < V; ++i) out[i] = static_cast<int8_t>(__float_as_uint(big[i]) & 0xFFu);
 }
 
 // 2^x with the hardware approximation (MUFU.EX2, flush-to-zero); 2^-inf = 0.
