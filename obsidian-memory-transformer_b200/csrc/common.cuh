@@ -128,6 +128,32 @@ __device__ __forceinline__ int8_t quant_i8_exact(float v, float s, float inv_s) 
 
 __device__ __forceinline__ float recip_or_zero(float s) { return s == 0.0f ? 0.0f : __frcp_rn(s); }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions: two IEEE round-to-nearest
+// operations per instruction, lane by lane).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // Warp-cooperative form of quant_i8_exact for V values per lane; must be
 // called by all 32 lanes (lanes without data pass zeros).  Off the rounding
 // ties round-half-even equals round-half-away, so the common path rounds with
@@ -145,13 +171,18 @@ __device__ __forceinline__ void quant_i8_exact_warp(const float (&v)[V], float s
                                                     int8_t (&out)[V]) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   constexpr float kTie = 0.5f - 1.220703125e-4f;  // 0.5 - 2^-13
+  static_assert(V % 2 == 0, "values in pairs");
   float big[V];
   bool near_tie = false;
+  const uint64_t inv2 = f2_pack(inv_s, inv_s), shift2 = f2_pack(kShift, kShift);
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const float t = v[i] * inv_s;
-    big[i] = __fadd_rn(t, kShift);
-    near_tie |= fabsf(__fsub_rn(t, __fsub_rn(big[i], kShift))) >= kTie;
+  for (int i = 0; i < V; i += 2) {  // the same per-value operations, two values per instruction
+    const uint64_t t = f2_mul(f2_pack(v[i], v[i + 1]), inv2);
+    const uint64_t b = f2_add(t, shift2);
+    float d0, d1;
+    f2_unpack(f2_sub(t, f2_sub(b, shift2)), d0, d1);
+    f2_unpack(b, big[i], big[i + 1]);
+    near_tie |= (fabsf(d0) >= kTie) | (fabsf(d1) >= kTie);
   }
   if (__any_sync(0xffffffffu, near_tie)) {
 #pragma unroll
