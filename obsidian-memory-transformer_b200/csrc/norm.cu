@@ -276,39 +276,50 @@ __global__ void __launch_bounds__(256) ln_x2_warp_kernel(const T* __restrict__ x
     if (lane == 0) xs[row] = s;
   }
   if (do_norm) {
-    float sum = 0.0f;
+    // the LN arithmetic on packed fp32 pairs (two IEEE operations per
+    // instruction); the sums run as two interleaved partial sums per lane
+    static_assert(V % 2 == 0, "values in pairs");
+    uint64_t in2[NV][V / 2];
+    uint64_t sum2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
     for (int j = 0; j < NV; ++j)
 #pragma unroll
-      for (int i = 0; i < V; ++i) sum += lnin(j, i);
-    const float mean = rr_.sum(sum) / static_cast<float>(H);
-    float sq = 0.0f;
+      for (int i = 0; i < V; i += 2) {
+        in2[j][i / 2] = f2_pack(lnin(j, i), lnin(j, i + 1));
+        sum2 = f2_add(sum2, in2[j][i / 2]);
+      }
+    float s0, s1;
+    f2_unpack(sum2, s0, s1);
+    const float mean = rr_.sum(s0 + s1) / static_cast<float>(H);
+    const uint64_t mean2 = f2_pack(mean, mean);
+    uint64_t sq2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       if (lane + STRIDE * j < nvec) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          const float d = lnin(j, i) - mean;
-          sq += d * d;
+        for (int i = 0; i < V / 2; ++i) {
+          const uint64_t d = f2_sub(in2[j][i], mean2);
+          sq2 = f2_fma(d, d, sq2);
         }
       }
     }
-    const float var = rr_.sum(sq) / static_cast<float>(H);
+    f2_unpack(sq2, s0, s1);
+    const float var = rr_.sum(s0 + s1) / static_cast<float>(H);
     const float rstd = rsqrtf(var + 1e-5f);
+    const uint64_t rstd2 = f2_pack(rstd, rstd);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int vi = lane + STRIDE * j;
       const int c0 = vi < nvec ? vi * V : 0;
-      float gv[V], bv[V];
 #pragma unroll
       for (int i = 0; i < V; i += 4) {  // gamma / beta are 16-byte aligned (checked by the launcher)
         const float4 g4 = __ldg(reinterpret_cast<const float4*>(gamma + c0 + i));
         const float4 b4 = __ldg(reinterpret_cast<const float4*>(beta + c0 + i));
-        gv[i] = g4.x; gv[i + 1] = g4.y; gv[i + 2] = g4.z; gv[i + 3] = g4.w;
-        bv[i] = b4.x; bv[i + 1] = b4.y; bv[i + 2] = b4.z; bv[i + 3] = b4.w;
+        const uint64_t n0 = f2_mul(f2_sub(in2[j][i / 2], mean2), rstd2);
+        const uint64_t n1 = f2_mul(f2_sub(in2[j][i / 2 + 1], mean2), rstd2);
+        f2_unpack(f2_fma(n0, f2_pack(g4.x, g4.y), f2_pack(b4.x, b4.y)), xv[j][i], xv[j][i + 1]);
+        f2_unpack(f2_fma(n1, f2_pack(g4.z, g4.w), f2_pack(b4.z, b4.w)), xv[j][i + 2], xv[j][i + 3]);
       }
-#pragma unroll
-      for (int i = 0; i < V; ++i) xv[j][i] = (lnin(j, i) - mean) * rstd * gv[i] + bv[i];
     }
   } else if constexpr (!SAME) {
 #pragma unroll
