@@ -143,7 +143,11 @@ LTM_API ltm_status ltm_linear_w8a8_acc_i32(const int8_t* qa, const int8_t* qw, i
 /* W4A16: y = act(a @ dequant(W)^T + bias), a: [M,K] f16/bf16; the weight is
  * dequantized to a_dtype (as Quantizer::dequantize writes T) and contracted
  * on tcgen05 kind::f16 with fp32 accumulation; y stored as a_dtype.
- * Requires K % 128 == 0 (group 128), N % 32 == 0. */
+ * Requires K % 128 == 0 (group 128), N % 32 == 0.  This entry point
+ * dequantises weight tiles in shared memory at every M (K split over a
+ * thread-block cluster when the tile grid is small) and allocates nothing;
+ * a W4A16 Titan block at M >= 1024 tokens instead dequantises each weight once
+ * into its own workspace and runs the persistent 16-bit GEMM. */
 LTM_API ltm_status ltm_linear_w4a16(const void* a, ltm_dtype a_dtype, const uint8_t* packed,
                             const float* s, const uint8_t* zp, const float* bias,
                             ltm_epilogue act, void* y, int64_t M, int64_t N, int64_t K,
