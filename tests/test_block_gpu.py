@@ -182,3 +182,27 @@ def test_block_w4a16_large_m(ltm, orc, dt, H, nh, F):
     assert_close(as_f32(y2).reshape(ref2.shape), ref2, *TOL[dt], what="second forward")
     assert ltm.device_error() == 0
     blk.close()
+
+
+def test_empty_batches_are_no_ops(ltm):
+    """B = 0 or S = 0 forwards, a B = 0 decode step and M = 0 linears return
+    OK without touching their outputs."""
+    import torch
+    from ltm_b200 import synthetic
+    H, nh, F, Ms = 256, 4, 512, 64
+    cfg, q, _ = make(ltm, "w4a16", "bf16", H, nh, F, Ms)
+    blk = ltm.TitanBlock(cfg, q)
+    blk.load_weights(synthetic.block_weights(H, F, Ms, 23))
+    for shape in ((0, 16, H), (2, 0, H)):
+        x = torch.zeros(shape, dtype=torch.bfloat16, device="cuda")
+        y = torch.full(shape, 7.0, dtype=torch.bfloat16, device="cuda")
+        blk.forward(x, out=y)
+        assert torch.all(y == 7.0)
+    x = torch.zeros((0, H), dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros((0, nh, 8, H // nh), dtype=torch.bfloat16, device="cuda")
+    assert blk.decode_step(x, kc, torch.zeros_like(kc), 0).shape == (0, H)
+    packed, s, zp = ltm.quantize_int4_grouped(torch.zeros((64, 256), device="cuda"))
+    y = ltm.linear_w4a16(torch.zeros((0, 256), dtype=torch.bfloat16, device="cuda"), packed, s, zp)
+    assert y.shape == (0, 64)
+    assert ltm.device_error() == 0
+    blk.close()

@@ -49,6 +49,28 @@ def test_int8_rounding_ties_and_clamp(ltm, orc):
     assert qo.max() == 127 and qo.min() == -127
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("K", [768, 3072])
+def test_act_per_token_rounding_ties(ltm, orc, dt, K):
+    """Per-token activation codes at exact .5 boundaries (row absmax 127, so
+    s = 1 and every k + 0.5 is a tie) and just off them: the warp quantizer's
+    fast path must hand every near-tie to the exact IEEE quotient and round
+    half away from zero.  Rows mix ties, near-ties, zeros and plain values."""
+    rng = np.random.default_rng(K)
+    k = rng.integers(-126, 126, size=(64, K)).astype(np.float32)
+    a = k + 0.5
+    a[:, 0] = 127.0                                  # absmax 127 -> s = 1
+    a[1::4] = k[1::4] + 0.5 + np.float32(2e-3)      # just above a tie in f32 (f16 / bf16 storage rounds it onto the tie)
+    a[2::4] = rng.standard_normal((16, K)).astype(np.float32) * 40.0
+    a[2::4, 0] = 127.0
+    a[3, :] = 0.0                                    # all-zero row: s = 0, codes 0
+    ad = to_device(a, dt)
+    q, s = ltm.quantize_act_int8_per_token(ad)
+    qo, so = orc.quant_int8_rows(as_f32(ad))
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 def test_act_per_token_bit_exact(ltm, orc, dt):
     a = np.random.default_rng(3).standard_normal((2048, 768)).astype(np.float32)
