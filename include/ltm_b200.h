@@ -73,6 +73,10 @@ LTM_API ltm_status ltm_device_error(int* code_out);
 /* Number of kernels this library has launched in this process (all devices). */
 LTM_API ltm_status ltm_launch_count(uint64_t* count_out);
 
+/* Number of device allocations (cudaMalloc) the library has made in this
+ * process (all devices): workspaces, weights, banks, scratch. */
+LTM_API ltm_status ltm_device_alloc_count(uint64_t* count_out);
+
 /* In-library kernel timer.  Between begin and end, every kernel the library
  * launches on `stream` is followed by a CUDA event; end synchronizes the
  * stream and writes one line per kernel name, "name launches total_ms\n", in
@@ -206,11 +210,15 @@ LTM_API ltm_status ltm_memory_store(void* memory, const void* keys, int64_t ldk,
  * device memory itself, a server whose device footprint must stay fixed after
  * start-up, a latency-critical loop where cudaMalloc would stall the device.
  * Its scratch is one fixed 256 KiB device array per GPU that loads the library
- * (held until exit), so hidden_dim rounded up to 64 plus memory_slots must not
- * exceed 65536 (else LTM_ERR_INVALID_ARG).  All calls share that array and
- * clear it at their start: calls whose GPU work overlaps (other streams or
- * unordered host threads) race.  The first call on a device looks up the
- * array's device address; make it before any stream capture. */
+ * (held until exit), so with use_attention_scores != 0, hidden_dim rounded up
+ * to 64 plus memory_slots must not exceed 65536 (else LTM_ERR_INVALID_ARG);
+ * rate-only calls (use_attention_scores == 0) use no scratch and have no such
+ * limit.  All calls share that array and clear it at their start: calls whose
+ * GPU work overlaps (other streams or unordered host threads) race.  The first
+ * call on a device looks up the array's device address in the device's
+ * primary context and caches it; make it before any stream capture, and do
+ * not call this entry point again after cudaDeviceReset in the same process
+ * (the cached address is then stale). */
 LTM_API ltm_status ltm_memory_store_noalloc(void* memory, const void* keys, int64_t ldk,
                                             const void* queries, int64_t ldq, int64_t T,
                                             const float* state, int memory_slots,
@@ -331,6 +339,21 @@ LTM_API ltm_status ltm_block_memory_write(ltm_block* blk, const float* state, co
 /* Copies the memory bank [Ms,H] (act_dtype) to a device buffer
  * (getMemoryBank(), titan_inspired_block.cuh:133). */
 LTM_API ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stream);
+
+/* Stage-by-stage inspection (no counterpart in the reference, whose block
+ * keeps its intermediates private): the shape of one intermediate of the last
+ * forward / decode step on this handle and, when out is not NULL, a copy of it
+ * into out (device memory, rows x cols packed, on stream).  kind: 0 =
+ * activation in act_dtype, 1 = int8 codes, 2 = fp32 per-row scales
+ * ([rows, 1]).  Names: "qkvm" [T, 4H] (post-RoPE
+ * Q|K|V|Qm), "kvm" [Ms, 2H] (K_M|V_M), "attn_self", "attn_mem" [T, H], "s",
+ * "m" [T, H] (output projections), "y" [T, H] (gated integration),
+ * "ffn_hidden" [T, F] (GELU output); W8A8 adds the per-token int8 codes and
+ * scales "ln1_q"/"ln1_s", "x_q"/"x_s", "attn_self_q"/"_s", "attn_mem_q"/"_s",
+ * "ln2_q"/"ln2_s", "ffn_hidden_q"/"_s"; the other schemes "ln1", "ln2".
+ * Under tensor parallelism H and F are this rank's widths (s, m: full H). */
+LTM_API ltm_status ltm_block_intermediate(ltm_block* blk, const char* name, void* out,
+                                          void* stream, int64_t* rows, int64_t* cols, int* kind);
 LTM_API ltm_status ltm_block_destroy(ltm_block* blk);
 
 /* ------------------------------------------------------ tensor parallel -- */

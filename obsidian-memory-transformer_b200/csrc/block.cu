@@ -30,6 +30,7 @@ void DevBuf::ensure(size_t n) {
   if (n <= bytes) return;
   release();
   LTM_CUDA_TRY(cudaMalloc(&ptr, n));
+  note_device_alloc();
   bytes = n;
 }
 
@@ -215,8 +216,9 @@ struct ltm_block {
   DevBuf memory;  // [Ms, H] act dtype
   DevBuf rope;    // [rope_S, dh/2] float2
   int rope_S = 0;
-  // workspace
-  int64_t ws_T = 0;
+  // workspace (ws_T rows of capacity; last_T rows written by the last
+  // forward or decode step)
+  int64_t ws_T = 0, last_T = 0;
   DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, spm, y, zq, zs, z,
       u, uq, us, amax;
   MemoryWriteState mw;
@@ -478,6 +480,7 @@ struct ltm_block {
   void forward(const void* x, void* out, int B, int S, cudaStream_t st) {
     const int64_t T = static_cast<int64_t>(B) * S;
     ensure_ws(T);
+    last_T = T;
     if (cfg.use_rotary) ensure_rope(S);
     const void* hin = ln1(x, T, st);
     // 2. memory keys / values from the bank
@@ -513,6 +516,7 @@ struct ltm_block {
               cudaStream_t st) {
     const int64_t T = B;
     ensure_ws(T);
+    last_T = T;
     if (cfg.use_rotary) ensure_rope(L + 1);
     if (!kvm_fresh) compute_kvm(st);
     const void* hin = ln1(x, T, st);
@@ -796,6 +800,67 @@ extern "C" ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stre
     LTM_CUDA_TRY(cudaMemcpyAsync(out, blk->memory.ptr,
                                  static_cast<size_t>(blk->Ms) * blk->H * dtype_size(blk->dt),
                                  cudaMemcpyDeviceToDevice, as_stream(stream)));
+  });
+}
+
+extern "C" ltm_status ltm_block_intermediate(ltm_block* blk, const char* name, void* out,
+                                             void* stream, int64_t* rows, int64_t* cols,
+                                             int* kind) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded && name && rows && cols && kind, "bad argument");
+    LTM_REQUIRE(blk->last_T > 0, "no forward or decode step has run on this block");
+    const std::string n(name);
+    const int64_t T = blk->last_T;
+    const int64_t H = blk->H, Hl = blk->Hl, Fl = blk->Fl;
+    const size_t a = dtype_size(blk->dt);
+    const bool w8a8 = blk->q.scheme == LTM_SCHEME_W8A8;
+    const bool ln = blk->cfg.use_layer_norm != 0;
+    struct View {
+      const char* name;
+      bool present;
+      const void* p;
+      int64_t r, c, ld;
+      int kind;
+    };
+    const View views[] = {
+        {"ln1_q", w8a8, blk->hq.ptr, T, H, H, 1},
+        {"ln1_s", w8a8, blk->hs.ptr, T, 1, 1, 2},
+        {"x_q", w8a8, blk->xq.ptr, T, H, H, 1},
+        {"x_s", w8a8, blk->xs.ptr, T, 1, 1, 2},
+        {"ln1", !w8a8 && ln, blk->h.ptr, T, H, H, 0},
+        {"qkvm", true, blk->qkv.ptr, T, 4 * Hl, 4 * Hl, 0},
+        {"kvm", true, blk->kvmb.ptr, blk->Ms, 2 * Hl, 2 * Hl, 0},
+        {"attn_self", true, blk->os.ptr, T, Hl, Hl, 0},
+        {"attn_mem", true, blk->om_.ptr, T, Hl, Hl, 0},
+        {"attn_self_q", w8a8, blk->osq.ptr, T, Hl, Hl, 1},
+        {"attn_self_s", w8a8, blk->oss.ptr, T, 1, 1, 2},
+        {"attn_mem_q", w8a8, blk->omq.ptr, T, Hl, Hl, 1},
+        {"attn_mem_s", w8a8, blk->oms.ptr, T, 1, 1, 2},
+        {"s", true, blk->spm.ptr, T, H, H, 0},
+        {"m", true, static_cast<const char*>(blk->spm.ptr) + T * H * a, T, H, H, 0},
+        {"y", true, blk->y.ptr, T, H, H, 0},
+        {"ln2_q", w8a8, blk->zq.ptr, T, H, H, 1},
+        {"ln2_s", w8a8, blk->zs.ptr, T, 1, 1, 2},
+        {"ln2", !w8a8 && ln, blk->z.ptr, T, H, H, 0},
+        {"ffn_hidden", true, blk->u.ptr, T, Fl, Fl, 0},
+        {"ffn_hidden_q", w8a8, blk->uq.ptr, T, Fl, Fl, 1},
+        {"ffn_hidden_s", w8a8, blk->us.ptr, T, 1, 1, 2},
+    };
+    for (const View& v : views) {
+      if (n != v.name) continue;
+      LTM_REQUIRE(v.present && v.p, "this block's scheme has no such intermediate");
+      *rows = v.r;
+      *cols = v.c;
+      *kind = v.kind;
+      if (out) {
+        const size_t es = v.kind == 0 ? a : (v.kind == 1 ? 1 : sizeof(float));
+        DeviceGuard g(blk->device);
+        LTM_CUDA_TRY(cudaMemcpy2DAsync(out, v.c * es, v.p, v.ld * es, v.c * es, v.r,
+                                       cudaMemcpyDeviceToDevice, as_stream(stream)));
+      }
+      return;
+    }
+    LTM_REQUIRE(false, "unknown intermediate name");
   });
 }
 

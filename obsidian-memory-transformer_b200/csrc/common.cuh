@@ -80,6 +80,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // Counts a launch and, while the kernel timer is on for `stream`, records an
 // event after it (the kernel's end; its start is the previous mark).
 void note_launch(const char* what, cudaStream_t stream);
+// Counts one device allocation made by the library (every cudaMalloc goes
+// through DevBuf::ensure, which calls this).
+void note_device_alloc();
 
 inline void check_launch(const char* what, cudaStream_t stream = nullptr) {
   note_launch(what, stream);

@@ -13,14 +13,19 @@
 // Limits and behaviour:
 //   * the array holds kNoAllocScratchFloats fp32 values (256 KiB) on every GPU
 //     that loads the library, until the process exits;
-//   * it fits round_up(hidden_dim, 64) + memory_slots <= kNoAllocScratchFloats;
-//     larger sizes are rejected with LTM_ERR_INVALID_ARG;
+//   * with use_attention_scores != 0 it fits round_up(hidden_dim, 64) +
+//     memory_slots <= kNoAllocScratchFloats; larger sizes are rejected with
+//     LTM_ERR_INVALID_ARG.  Rate-only calls (use_attention_scores == 0) use no
+//     scratch and take any size ltm_memory_store takes;
 //   * every call shares the one array and clears the parts it uses at its
 //     start (in stream order), so calls whose GPU work overlaps -- different
 //     streams, or different host threads without ordering -- race on it;
 //   * the first call on a device looks the array's device address up
 //     (cudaGetSymbolAddress, with that device current) and caches it; make that
-//     first call before any stream capture.
+//     first call before any stream capture.  The cached address belongs to the
+//     device's primary context: after cudaDeviceReset (or anything else that
+//     destroys that context) it is stale, so do not call this entry point
+//     again in that process.
 #include <mutex>
 
 #include "block.cuh"
@@ -73,13 +78,15 @@ extern "C" ltm_status ltm_memory_store_noalloc(void* memory, const void* keys, i
     validate_memory_store(memory, keys, ldk, queries, ldq, T, state, memory_slots, hidden_dim,
                           num_heads, scores);
     const int64_t qsum_floats = (static_cast<int64_t>(hidden_dim) + 63) / 64 * 64;
-    LTM_REQUIRE(qsum_floats + memory_slots <= kNoAllocScratchFloats,
+    LTM_REQUIRE(!scores || qsum_floats + memory_slots <= kNoAllocScratchFloats,
                 "hidden_dim (rounded up to 64) + memory_slots exceeds the 65536-float "
                 "allocation-free scratch; use ltm_memory_store");
     if (memory_slots == 0 || hidden_dim == 0) return;
-    float* scratch = scratch_address();
+    // Rate-only updates read no scratch (the bank update takes the constant
+    // rate), so they need no device address either.
+    float* scratch = scores ? scratch_address() : nullptr;
     launch_memory_store(memory, keys, ldk, queries, ldq, T, state, 1.0f, memory_slots, hidden_dim,
-                        num_heads, update_rate, scores, dtype, scratch, scratch + qsum_floats,
-                        as_stream(stream));
+                        num_heads, update_rate, scores, dtype, scratch,
+                        scores ? scratch + qsum_floats : nullptr, as_stream(stream));
   });
 }

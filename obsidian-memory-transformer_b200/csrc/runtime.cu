@@ -34,6 +34,7 @@ int* device_error_ptr() {
 namespace {
 thread_local std::string t_last_error;
 std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_device_allocs{0};
 }  // namespace
 
 // Kernel timer: while on, every launch on the timed stream is followed by an
@@ -71,6 +72,8 @@ void note_launch(const char* what, cudaStream_t stream) {
   cudaEvent_t e = t.get();
   if (e && cudaEventRecord(e, stream) == cudaSuccess) t.marks.emplace_back(what, e);
 }
+
+void note_device_alloc() { g_device_allocs.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 void clear_error() { t_last_error.clear(); }
@@ -158,6 +161,13 @@ extern "C" ltm_status ltm_launch_count(uint64_t* count_out) {
   return guarded([&] {
     LTM_REQUIRE(count_out != nullptr, "count_out is NULL");
     *count_out = g_launches.load(std::memory_order_relaxed);
+  });
+}
+
+extern "C" ltm_status ltm_device_alloc_count(uint64_t* count_out) {
+  return guarded([&] {
+    LTM_REQUIRE(count_out != nullptr, "count_out is NULL");
+    *count_out = g_device_allocs.load(std::memory_order_relaxed);
   });
 }
 

@@ -73,6 +73,7 @@ def _declare(L):
         "ltm_last_error_string": ([], C.c_char_p),
         "ltm_device_error": ([C.POINTER(C.c_int)], ci),
         "ltm_launch_count": ([C.POINTER(C.c_uint64)], ci),
+        "ltm_device_alloc_count": ([C.POINTER(C.c_uint64)], ci),
         "ltm_kernel_timer_begin": ([vp], ci),
         "ltm_kernel_timer_end": ([C.c_char_p, C.c_size_t], ci),
         "ltm_quantize_int8_per_channel": ([vp, ci, i64, i64, vp, vp, vp], ci),
@@ -96,6 +97,8 @@ def _declare(L):
         "ltm_block_load_weights": ([vp, C.POINTER(BlockWeightsC)], ci),
         "ltm_block_forward": ([vp, vp, vp, vp, ci, ci, vp], ci),
         "ltm_block_get_memory": ([vp, vp, vp], ci),
+        "ltm_block_intermediate": ([vp, C.c_char_p, vp, vp, C.POINTER(i64), C.POINTER(i64),
+                                    C.POINTER(ci)], ci),
         "ltm_block_decode_step": ([vp, vp, vp, vp, vp, i64, ci, ci, vp], ci),
         "ltm_block_memory_write": ([vp, vp, vp, i64, i64, vp], ci),
         "ltm_block_destroy": ([vp], ci),
@@ -150,6 +153,13 @@ def launch_count() -> int:
     """Kernels launched by the library in this process."""
     n = C.c_uint64(0)
     _check(lib().ltm_launch_count(C.byref(n)))
+    return n.value
+
+
+def device_alloc_count() -> int:
+    """Device allocations (cudaMalloc) the library has made in this process."""
+    n = C.c_uint64(0)
+    _check(lib().ltm_device_alloc_count(C.byref(n)))
     return n.value
 
 
@@ -569,6 +579,20 @@ class TitanBlock:
                           dtype=torch_dtype(self.quant.act_dtype), device=f"cuda:{self.device}")
         _check(lib().ltm_block_get_memory(self._h, _ptr(out), _stream(stream)))
         return out
+
+    def intermediate(self, name: str, stream=None):
+        """A copy of one intermediate of the last forward / decode step
+        (ltm_block_intermediate): activations in the act dtype, int8 codes,
+        or fp32 per-row scales as a 1-D tensor."""
+        torch = _torch()
+        r, c, kind = C.c_int64(), C.c_int64(), C.c_int()
+        _check(lib().ltm_block_intermediate(self._h, name.encode(), None, None, C.byref(r),
+                                            C.byref(c), C.byref(kind)))
+        dt = {0: torch_dtype(self.quant.act_dtype), 1: torch.int8, 2: torch.float32}[kind.value]
+        out = torch.empty((r.value, c.value), dtype=dt, device=f"cuda:{self.device}")
+        _check(lib().ltm_block_intermediate(self._h, name.encode(), _ptr(out), _stream(stream),
+                                            C.byref(r), C.byref(c), C.byref(kind)))
+        return out.reshape(-1) if kind.value == 2 else out
 
     def close(self) -> None:
         if getattr(self, "_h", None):
