@@ -1,19 +1,27 @@
 #!/usr/bin/env python
-"""Headline benchmark: Titan-block tokens/s of the quantized prefill.
+"""Headline benchmark: Titan-block tokens/s of the quantized prefill, tensor
+parallel over the N GPUs.
 
-Workload (one step): a 12-layer Titan model prefill with W8A8 linears and
-fp16 activations -- hidden 768, 12 heads (head_dim 64), FFN 3072, 512 memory
-slots, vocab 32000, batch 8, seq 2048, per-token dynamic INT8 activations --
-embedding gather + 12 TB-v1 blocks on synthetic seeded tokens / weights.
+Workload (one step, the default): an 8-layer Titan prefill with W8A8 linears
+and bf16 activations -- hidden 8192, 64 heads (head_dim 128), FFN 28672, 8192
+memory slots, batch 16, seq 4096, per-token dynamic INT8 activations --
+sharded by heads, memory slots' K_M / V_M and FFN columns over the N GPUs
+with an NCCL allreduce after the output and FFN-down projections.  The job is
+fixed as N grows (strong scaling), so `python bench.py --gpus N` for N = 1, 2,
+4, 8 measures the tensor-parallel scaling of one workload.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config tp|prefill|w4a16|decode]
 
-N > 1 runs under torchrun as N independent replicas (one process per GPU, no
-data-path collective: the prefill of independent batches does not shard), so
-`value` is the aggregate over all ranks and scaling is weak.  Rank 0 prints one
-JSON line.  `--impl reference` times the CPU restatement of the reference's
-algorithm (the oracle; the reference itself does not compile) on the host
-cores with the same metric.
+At N = 1 the line also carries `side_workloads`: the 12-layer hidden-768
+W8A8 prefill (batch 8 x 2048), the 4-layer hidden-4096 W4A16 long-context
+prefill (batch 4 x 8192) and the 32-layer W4A16 batched decode step (batch
+64 against 32768 cached positions), each measured the same way with fewer
+steps.  `--config` runs one of them as the headline instead (prefill and
+decode: N independent replicas, weak scaling).  Rank 0 prints one JSON line.
+`--impl reference` times the CPU restatement of the reference's algorithm
+(the oracle; the reference itself does not compile) on all host cores with
+the same metric and workload.
 """
 from __future__ import annotations
 
@@ -50,11 +58,13 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
+    ap.add_argument("--no-side", action="store_true",
+                    help="skip the side workloads measured after the headline at N = 1")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
-    ap.add_argument("--config", choices=["prefill", "tp", "w4a16", "decode"], default="prefill",
-                    help="prefill: the 12-layer W8A8 prefill (default; N>1 = data-parallel "
-                         "replicas); tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel "
-                         "over the N GPUs; w4a16: the 4-layer hidden-4096 W4A16 long-context "
+    ap.add_argument("--config", choices=["prefill", "tp", "w4a16", "decode"], default="tp",
+                    help="tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel over the N "
+                         "GPUs (default); prefill: the 12-layer W8A8 prefill (N>1 = data-parallel "
+                         "replicas); w4a16: the 4-layer hidden-4096 W4A16 long-context "
                          "prefill (tensor-parallel when N > 1); decode: the 32-layer hidden-4096 "
                          "W4A16 batched decode step against a 32768-position KV cache (N > 1 = "
                          "replicas)")
@@ -99,7 +109,7 @@ class ClockSampler:
             self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.out, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -449,8 +459,7 @@ def cpu_baseline(threads_hint=None):
     layers at the full batch (tokens/s scaled by 1/12)."""
     from ltm_b200 import synthetic
     from oracle import oracle as orc
-    if threads_hint:
-        orc.set_threads(threads_hint)
+    orc.set_threads(threads_hint or host_threads())
     H, nh, F, Ms, V = WL["H"], WL["nh"], WL["F"], WL["Ms"], WL["vocab"]
     cfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W8A8, dtype=orc.F16)
     w = synthetic.block_weights(H, F, Ms, 1000)
@@ -466,12 +475,13 @@ def cpu_baseline(threads_hint=None):
                       f"{dt:.1f} s; tokens/s scaled to {WL['layers']} layers"}
 
 
-def run_tp(args, wl: dict = TP_WL, w4a16: bool = False):
+def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     """The tensor-parallel prefill: one block per rank (its head / FFN shard of
     one random-init block, built from the same seeded full weights on every
     rank) applied at each of the layers; the input hidden states are the full
     [B,S,H] on every rank.  Strong scaling: the job is fixed, N GPUs share it.
-    With w4a16 the same driver runs the W4A16 long-context prefill."""
+    With w4a16 the same driver runs the W4A16 long-context prefill.  Returns
+    the result line on rank 0 (None elsewhere); side: no CPU baseline."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -494,7 +504,9 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False):
     blk = ltm.TitanBlock(cfg, q, comm=comm)
     w = synthetic.block_weights(H, F, Ms, 1000)
     blk.load_weights(w)
-    del w
+    want_cpu = rank == 0 and ws == 1 and not args.no_cpu_baseline and not side
+    if not want_cpu:
+        del w
     gen = torch.Generator(device=dev).manual_seed(7)
     x = (torch.randn((B, S, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
     bufs = (torch.empty_like(x), torch.empty_like(x))
@@ -590,19 +602,77 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False):
                        "l2": "inputs (1 GiB per activation tensor) larger than L2"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x_host.numel() * 2),
-                    "d2h_bytes_per_step": int(last_host.numel() * 2)},
+                    "d2h_bytes_per_step": int(last_host.numel() * 2),
+                    "copies": "H2D of the [B,S,H] input hidden states from pinned memory; D2H "
+                              "of each sequence's last output hidden state (what the next "
+                              "step of a prefill needs); the [B,S,H] output stays on the device"},
             "gpu_launches": int(launches),
             "clocks": clocks,
             "roofline": roofline,
             "cpu_baseline": None,
             "kernels": kernels,
         }
-        emit(line)
     blk.close()
     comm.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if rank == 0 and want_cpu:
+        line["cpu_baseline"] = cpu_sample_block(wl, w4a16, w, L, samples=2)
+    return line if rank == 0 else None
+
+
+def cpu_sample_block(wl: dict, w4a16: bool, w: dict, layers: int, samples: int,
+                     warmup: int = 0, tokens: int = 64):
+    """The oracle's block forward on the host cores, bounded sample of a
+    prefill workload: K_M | V_M of the bank made once (the per-forward cost of
+    one layer, timed), then `samples` forwards of one sequence's first
+    `tokens` tokens with those K_M | V_M (per-token cost, timed); the job's
+    time is layers x (K_M|V_M time + B*S x per-token time).  The sample's
+    causal self-attention spans `tokens` positions, fewer than the workload's
+    sequence, so it under-counts the attention share of the per-token work.
+    Returns the cpu_baseline entry plus the per-sample times."""
+    import numpy as np
+    from oracle import oracle as orc
+    threads = host_threads()
+    orc.set_threads(threads)
+    B, S, H, F, Ms, nh = (wl[k] for k in ("B", "S", "H", "F", "Ms", "nh"))
+    dt = orc.BF16
+    ocfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W4A16 if w4a16 else orc.W8A8,
+                dtype=dt)
+    pb = orc.PreparedBlock(ocfg, w)
+    mem = orc.round_to(w["memory"], dt)
+    t0 = time.perf_counter()
+    kvm = pb.kvm(mem)
+    t_kvm = time.perf_counter() - t0
+    rng = np.random.default_rng(7)
+    x = orc.round_to(rng.standard_normal((tokens, H), dtype=np.float32) * 0.02, dt)
+    for _ in range(warmup):
+        pb.forward(x, 1, tokens, mem, kvm)
+    times = []
+    for _ in range(max(samples, 1)):
+        t0 = time.perf_counter()
+        pb.forward(x, 1, tokens, mem, kvm)
+        times.append(time.perf_counter() - t0)
+    pb.close()
+    per_tok = statistics.median(times) / tokens
+    job_s = layers * (t_kvm + B * S * per_tok)
+    return {"value": B * S / job_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"oracle TB-v1 block on {threads} host threads: K_M|V_M of the "
+                      f"{Ms}-slot bank once ({t_kvm:.1f} s), then {len(times)} forwards of one "
+                      f"sequence's first {tokens} tokens ({statistics.median(times):.2f} s "
+                      f"each); job time = {layers} layers x (K_M|V_M + {B}x{S} tokens x "
+                      f"per-token time); the sample's causal attention spans {tokens} positions",
+            "per_sample_s": times, "kvm_s": t_kvm}
+
+
+def host_threads() -> int:
+    """Host cores this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its workers; the CPU baselines use every core they are given)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # not Linux
+        return os.cpu_count() or 1
 
 
 def cpu_baseline_decode(wl: dict = DEC_WL, budget_s: float = 12.0):
@@ -616,6 +686,7 @@ def cpu_baseline_decode(wl: dict = DEC_WL, budget_s: float = 12.0):
     ocfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W4A16, dtype=orc.BF16,
                 memory_write=1, use_attention_scores=1, update_rate=0.9)
     w = synthetic.block_weights(H, F, Ms, 1000)
+    orc.set_threads(host_threads())
     pb = orc.PreparedBlock(ocfg, w)
     rng = np.random.default_rng(5)
     kc = orc.round_to(rng.standard_normal((1, nh, P, H // nh), dtype=np.float32), orc.BF16)
@@ -636,7 +707,7 @@ def cpu_baseline_decode(wl: dict = DEC_WL, budget_s: float = 12.0):
                       f"scaled to {wl['layers']} layers"}
 
 
-def run_decode(args, wl: dict = DEC_WL):
+def run_decode(args, wl: dict = DEC_WL, side: bool = False):
     """The batched decode step: one block per layer (each its own copy of the
     same seeded weights, bank and resident K_M | V_M), one shared KV-cache
     buffer for all layers (per-layer caches would need 1.1 TB), every step at
@@ -755,7 +826,7 @@ def run_decode(args, wl: dict = DEC_WL):
         work = {"decode_attn_kernel": {"amount": lb["kv"] * L, "unit": "byte"}}
         roofline, _ = roofline_of(kt.result, work, torch)
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not side:
         cpu = cpu_baseline_decode(wl)
     if rank == 0:
         step_gbs = lb["total"] * L / (step_ms * 1e-3) / 1e9
@@ -784,12 +855,14 @@ def run_decode(args, wl: dict = DEC_WL):
             "cpu_baseline": cpu,
             "kernels": kernels,
         }
-        emit(line)
+        result = line
     for b in blocks:
         b.close()
+    cache.clear()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return result if rank == 0 else None
 
 
 def probe_decode_case(torch, ltm):
@@ -816,7 +889,7 @@ def probe_decode_case(torch, ltm):
     blk.close()
 
 
-def run_ours(args):
+def run_ours(args, side: bool = False):
     import torch
     import torch.distributed as dist
     import ltm_b200 as ltm
@@ -910,7 +983,7 @@ def run_ours(args):
             kernels["int8_peak_tops_measured"] = round(i8, 1)
 
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not side:
         cpu = cpu_baseline()
 
     if rank == 0:
@@ -933,51 +1006,120 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "kernels": kernels,
         }
-        emit(line)
+        result = line
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
     model.close()
+    return result if rank == 0 else None
 
 
 # ---------------------------------------------------------- reference path --
 def run_reference(args):
+    """The reference arm: the CPU restatement of the reference's algorithm
+    (the oracle; the reference's own CUDA sources do not compile) timed on all
+    host cores the process may use, for the same workload, metric and unit as
+    our arm.  Each timed step is one bounded sample of the workload; the line's
+    value is the whole job's tokens/s extrapolated from the samples.  Under
+    torchrun only rank 0 runs."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
     from ltm_b200 import synthetic
     from oracle import oracle as orc
-    H, nh, F, Ms, V = WL["H"], WL["nh"], WL["F"], WL["Ms"], WL["vocab"]
-    cfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W8A8, dtype=orc.F16)
-    w = synthetic.block_weights(H, F, Ms, 1000)
-    emb = synthetic.embedding(V, H, 7)
-    Bs, S = 1, WL["S"]  # each step: 1 layer of 12, one sequence of the batch
-    tok = synthetic.tokens(Bs, S, V, 3)
-    for _ in range(args.warmup):
-        orc.model_forward(cfg, [w], emb, tok, Bs, S)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        orc.model_forward(cfg, [w], emb, tok, Bs, S)
-    dt = time.perf_counter() - t0
-    value = args.steps * Bs * S / dt / WL["layers"]
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "impl": "reference",
-        "data": "synthetic (seeded tokens U[0,32000), weights N(0,0.02), random init)",
-        "config": {"workload": WORKLOAD_NAME, "layers": WL["layers"], "global_batch": WL["B"],
-                   "seq_len": S, "act_dtype": "f16", "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": orc.num_threads(),
-                         "kind": "port",
-                         "sample": f"each step: 1 of {WL['layers']} layers, 1 sequence of "
-                                   f"{S} tokens; tokens/s scaled to {WL['layers']} layers"},
-        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-        "note": "the reference's CUDA sources do not compile; this arm times the CPU "
-                "restatement of its algorithm (oracle/) on all host cores",
-    }
+    threads = host_threads()
+    orc.set_threads(threads)
+    base = {"metric": METRIC, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+            "impl": "reference",
+            "note": "the reference's CUDA sources do not compile; this arm times the CPU "
+                    "restatement of its algorithm (oracle/) on all host cores"}
+    if args.config in ("tp", "w4a16"):
+        w4 = args.config == "w4a16"
+        wl = W4_WL if w4 else TP_WL
+        L = args.layers or wl["layers"]
+        w = synthetic.block_weights(wl["H"], wl["F"], wl["Ms"], 1000)
+        cpu = cpu_sample_block(wl, w4, w, L, samples=args.steps, warmup=args.warmup)
+        step_s = statistics.median(cpu.pop("per_sample_s"))
+        cpu.pop("kvm_s")
+        line = dict(base, value=round(cpu["value"], 3), ms_per_step=round(step_s * 1e3, 2),
+                    scaling="strong", dtype="int4xbf16" if w4 else "int8",
+                    data="synthetic (hidden states N(0,0.02^2), weights N(0,0.02), random init)",
+                    config={"workload": W4_WORKLOAD_NAME if w4 else TP_WORKLOAD_NAME,
+                            "layers": L, "global_batch": wl["B"], "seq_len": wl["S"],
+                            "act_dtype": "bf16", "parallelism": "host cores",
+                            "same_config": False,
+                            "sampling": "each timed step: 1 layer, one sequence's first 64 "
+                                        "tokens with K_M|V_M made once; the job's tokens/s "
+                                        "extrapolated (see cpu_baseline.sample)"})
+    elif args.config == "decode":
+        cpu = cpu_baseline_decode(DEC_WL)
+        line = dict(base, value=round(cpu["value"], 4), ms_per_step=None, scaling="weak",
+                    dtype="int4xbf16",
+                    data="synthetic (KV cache N(0,1), hidden states N(0,0.02^2), weights "
+                         "N(0,0.02), random init)",
+                    config={"workload": DEC_WORKLOAD_NAME, "layers": DEC_WL["layers"],
+                            "global_batch": DEC_WL["B"], "kv_positions": DEC_WL["P"],
+                            "act_dtype": "bf16", "parallelism": "host cores",
+                            "same_config": False,
+                            "sampling": "1 layer, 1 sequence per sample (see "
+                                        "cpu_baseline.sample)"})
+    else:
+        H, nh, F, Ms, V = WL["H"], WL["nh"], WL["F"], WL["Ms"], WL["vocab"]
+        cfg = dict(H=H, F=F, nh=nh, dh=H // nh, Ms=Ms, scheme=orc.W8A8, dtype=orc.F16)
+        w = synthetic.block_weights(H, F, Ms, 1000)
+        emb = synthetic.embedding(V, H, 7)
+        Bs, S = 1, WL["S"]  # each step: 1 layer of 12, one sequence of the batch
+        tok = synthetic.tokens(Bs, S, V, 3)
+        for _ in range(args.warmup):
+            orc.model_forward(cfg, [w], emb, tok, Bs, S)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            orc.model_forward(cfg, [w], emb, tok, Bs, S)
+        dt = time.perf_counter() - t0
+        value = args.steps * Bs * S / dt / WL["layers"]
+        cpu = {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"each step: 1 of {WL['layers']} layers, 1 sequence of {S} tokens; "
+                         f"tokens/s scaled to {WL['layers']} layers"}
+        line = dict(base, value=round(value, 2), ms_per_step=round(dt / args.steps * 1e3, 2),
+                    scaling="weak", dtype="int8",
+                    data="synthetic (seeded tokens U[0,32000), weights N(0,0.02), random init)",
+                    config={"workload": WORKLOAD_NAME, "layers": WL["layers"],
+                            "global_batch": WL["B"], "seq_len": S, "act_dtype": "f16",
+                            "parallelism": "host cores", "same_config": False,
+                            "sampling": "each step: 1 of 12 layers, 1 of 8 sequences"})
+    cpu["value"] = line["value"]
+    line["cpu_baseline"] = cpu
+    line["e2e"] = {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}
     emit(line)
+
+
+def run_side_workloads(args) -> dict:
+    """At N = 1, after the headline: the other single-GPU workloads, each
+    measured like the headline (device-timed value, e2e, roofline of its
+    dominant kernel class, clocks) with fewer steps and no CPU baseline."""
+    import gc
+    import torch
+    side = {}
+    steps = max(3, min(args.steps, 10))
+    plans = [("prefill_12layer_w8a8", lambda a: run_ours(a, side=True)),
+             ("prefill_4layer_w4a16_long_context", lambda a: run_tp(a, W4_WL, True, side=True)),
+             ("decode_32layer_w4a16", lambda a: run_decode(a, side=True))]
+    for name, fn in plans:
+        a = argparse.Namespace(**vars(args))
+        a.steps, a.warmup = steps, 3
+        a.layers = WL["layers"] if name.startswith("prefill_12") else None
+        try:
+            line = fn(a)
+            keep = ("value", "unit", "ms_per_step", "steps", "warmup", "dtype", "config", "e2e",
+                    "roofline", "clocks", "gpu_launches", "scaling")
+            side[name] = {k: line.get(k) for k in keep}
+        except Exception as e:  # noqa: BLE001 - a side workload must not lose the headline
+            side[name] = {"error": f"{type(e).__name__}: {e}"}
+        gc.collect()
+        torch.cuda.empty_cache()
+    return side
 
 
 _JSON_FD = 1
@@ -1011,16 +1153,22 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args)
-    elif args.config == "tp":
-        run_tp(args)
+        return
+    if args.config == "tp":
+        line = run_tp(args)
     elif args.config == "w4a16":
-        run_tp(args, W4_WL, w4a16=True)
+        line = run_tp(args, W4_WL, w4a16=True)
     elif args.config == "decode":
-        run_decode(args)
+        line = run_decode(args)
     else:
         if args.layers is None:
             args.layers = WL["layers"]
-        run_ours(args)
+        line = run_ours(args)
+    if line is None:
+        return
+    if args.config == "tp" and args.gpus == 1 and not args.no_side:
+        line["side_workloads"] = run_side_workloads(args)
+    emit(line)
 
 
 if __name__ == "__main__":

@@ -70,6 +70,8 @@ def _declare(L):
         "orc_rope_table": ([ci, ci, f], None),
         "orc_attention": ([f, i64, f, f, i64, ci, ci, ci, ci, ci, ci, ci, ci, f, i64], None),
         "orc_memory_store": ([f, f, i64, f, i64, i64, f, ci, ci, ci, C.c_float, ci, ci], None),
+        "orc_activation": ([f, i64, ci, f], None),
+        "orc_ema_rows": ([f, ci, i64, f, f, ci], None),
         "orc_block_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci], ci),
         "orc_block_forward_kv": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci, f], ci),
         "orc_block_kvm": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f], ci),
@@ -77,6 +79,9 @@ def _declare(L):
                                    ci, f], ci),
         "orc_block_prepare": ([_p(OrcBlockCfg), _p(OrcBlockWeights)], C.c_void_p),
         "orc_block_release": ([C.c_void_p], None),
+        "orc_block_forward_prepared": ([C.c_void_p, _p(OrcBlockCfg), _p(OrcBlockWeights), f, f,
+                                        f, f, ci, ci], ci),
+        "orc_block_kvm_prepared": ([C.c_void_p, _p(OrcBlockCfg), f, f], ci),
         "orc_block_decode_step_prepared": ([C.c_void_p, _p(OrcBlockCfg), _p(OrcBlockWeights), f, f,
                                             f, f, f, i64, ci, ci, f], ci),
         "orc_model_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), _p(f), ci, f, ci, i32, f, ci,
@@ -218,6 +223,22 @@ def attention(q, k, v, B, Sq, Skv, nh, dh, causal, dtype, kv_shared=False):
     return out
 
 
+def activation(x, act: int):
+    """act(x) elementwise in fp32 (GELU-tanh or sigmoid)."""
+    x = _f32(x)
+    y = np.empty_like(x)
+    lib().orc_activation(_ptr(x), x.size, act, _ptr(y))
+    return y
+
+
+def ema_rows(rows, v, w, dtype: int):
+    """rows [Ms, n] (updated copy returned): (1 - w[s]) rows[s] + w[s] v, rounded."""
+    rows = np.array(rows, dtype=np.float32, copy=True, order="C")
+    lib().orc_ema_rows(_ptr(rows), rows.shape[0], rows.shape[1], _ptr(_f32(v)), _ptr(_f32(w)),
+                       dtype)
+    return rows
+
+
 def memory_store(memory, keys, queries, state, nh: int, rate: float, use_scores: bool, dtype: int):
     """memory [Ms,H] (returned updated copy); keys [Ms, >=H]; queries [T, >=H]; state [H]."""
     mem = np.array(memory, dtype=np.float32, copy=True, order="C")
@@ -309,6 +330,29 @@ class PreparedBlock:
                                                  x.shape[0], _ptr(y))
         if r != 0:
             raise RuntimeError(f"orc_block_decode_step failed ({r})")
+        return y
+
+    def kvm(self, memory):
+        """K_M | V_M [Ms, 2H] of a bank (rounded to the block's dtype)."""
+        memory = _f32(memory)
+        out = np.empty((memory.shape[0], 2 * memory.shape[1]), np.float32)
+        r = lib().orc_block_kvm_prepared(self.h, C.byref(self.c), _ptr(memory), _ptr(out))
+        if r != 0:
+            raise RuntimeError(f"orc_block_kvm failed ({r})")
+        return out
+
+    def forward(self, x, B: int, S: int, memory, kvm=None):
+        """Block forward with the prepared linears; kvm (K_M | V_M of the bank)
+        is used as given when passed.  memory is updated in place when the
+        block writes."""
+        x = _f32(x)
+        assert memory.dtype == np.float32 and memory.flags.c_contiguous
+        y = np.empty_like(x)
+        r = lib().orc_block_forward_prepared(self.h, C.byref(self.c), C.byref(self.st),
+                                             _ptr(memory), _ptr(None if kvm is None else _f32(kvm)),
+                                             _ptr(x), _ptr(y), B, S)
+        if r != 0:
+            raise RuntimeError(f"orc_block_forward_prepared failed ({r})")
         return y
 
     def close(self):

@@ -393,6 +393,18 @@ void ema_rows(float* rows, int Ms, int64_t n, const float* v, const std::vector<
 
 }  // namespace
 
+extern "C" void orc_activation(const float* x, int64_t n, int act, float* y) {
+  // the epilogue activations: GELU-tanh (src/core/ops/fused_ops.cu:136-142), sigmoid
+  for (int64_t i = 0; i < n; ++i) y[i] = act_fn(x[i], act);
+}
+
+extern "C" void orc_ema_rows(float* rows, int Ms, int64_t n, const float* v, const float* w,
+                             int dtype) {
+  // rows[s, :] = (1 - w[s]) rows[s, :] + w[s] v (storeStateKernel,
+  // src/core/ltm/memory_bank.cu:56-67), rounded to dtype
+  ema_rows(rows, Ms, n, v, std::vector<float>(w, w + Ms), dtype);
+}
+
 extern "C" void orc_memory_store(float* memory, const float* keys, int64_t ldk,
                                  const float* queries, int64_t ldq, int64_t T, const float* state,
                                  int Ms, int H, int nh, float rate, int use_scores, int dtype) {
@@ -535,21 +547,26 @@ void block_write(const orc_block_cfg* c, const OrcLins& L, float* memory, float*
 
 }  // namespace
 
-extern "C" int orc_block_forward_kv(const orc_block_cfg* c, const orc_block_weights* w,
-                                    float* memory_inout, const float* x, float* y, int B, int S,
-                                    float* kv_out) {
+namespace {
+
+// One TB-v1 forward with the block's quantized linears L; kvm_in (K_M | V_M
+// of the current bank, [Ms, 2H]) is used as given when not NULL, else made
+// from the bank.
+int forward_impl(const orc_block_cfg* c, const orc_block_weights* w, const OrcLins& L,
+                 float* memory_inout, const float* kvm_in, const float* x, float* y, int B, int S,
+                 float* kv_out) {
   const int H = c->H, nh = c->nh, dh = c->dh, Ms = c->Ms;
   const int dt = c->dtype;
   if (nh * dh != H) return 1;
   const int64_t T = static_cast<int64_t>(B) * S;
-  OrcLins L(c, w);
   // 1-2. LN1, fused Q | K | V | Qm projection, RoPE on Q and K
   std::vector<float> qkvm = qkvm_rows(c, w, L, x, T, S, 0);
   if (kv_out)
     for (int64_t t = 0; t < T; ++t)
       std::memcpy(kv_out + t * 2 * H, qkvm.data() + t * 4 * H + H, sizeof(float) * 2 * H);
   // 3. memory keys/values from the bank
-  std::vector<float> kvm = kvm_rows(c, L, memory_inout);
+  std::vector<float> kvm = kvm_in ? std::vector<float>(kvm_in, kvm_in + static_cast<int64_t>(Ms) * 2 * H)
+                                  : kvm_rows(c, L, memory_inout);
   // 4. causal self-attention and memory attention
   std::vector<float> os(T * H), om(T * H);
   orc_attention(qkvm.data(), 4 * H, qkvm.data() + H, qkvm.data() + 2 * H, 4 * H, B, S, S, S, nh,
@@ -562,6 +579,15 @@ extern "C" int orc_block_forward_kv(const orc_block_cfg* c, const orc_block_weig
   if (c->memory_write && c->use_memory_gating)
     block_write(c, L, memory_inout, kvm.data(), qkvm.data() + 3 * H, 4 * H, g, x, T, false);
   return 0;
+}
+
+}  // namespace
+
+extern "C" int orc_block_forward_kv(const orc_block_cfg* c, const orc_block_weights* w,
+                                    float* memory_inout, const float* x, float* y, int B, int S,
+                                    float* kv_out) {
+  OrcLins L(c, w);
+  return forward_impl(c, w, L, memory_inout, nullptr, x, y, B, S, kv_out);
 }
 
 extern "C" int orc_block_forward(const orc_block_cfg* c, const orc_block_weights* w,
@@ -647,6 +673,22 @@ extern "C" int orc_block_decode_step_prepared(const void* prepared, const orc_bl
                                               int cache_len, int B, float* y) {
   return decode_step(c, w, *static_cast<const OrcLins*>(prepared), memory_inout, kvm_inout, x,
                      k_cache, v_cache, max_positions, cache_len, B, y);
+}
+
+extern "C" int orc_block_forward_prepared(const void* prepared, const orc_block_cfg* c,
+                                          const orc_block_weights* w, float* memory_inout,
+                                          const float* kvm_in, const float* x, float* y, int B,
+                                          int S) {
+  return forward_impl(c, w, *static_cast<const OrcLins*>(prepared), memory_inout, kvm_in, x, y, B,
+                      S, nullptr);
+}
+
+extern "C" int orc_block_kvm_prepared(const void* prepared, const orc_block_cfg* c,
+                                      const float* memory, float* kvm_out) {
+  if (c->nh * c->dh != c->H) return 1;
+  const std::vector<float> kvm = kvm_rows(c, *static_cast<const OrcLins*>(prepared), memory);
+  std::memcpy(kvm_out, kvm.data(), sizeof(float) * kvm.size());
+  return 0;
 }
 
 extern "C" int orc_model_forward(const orc_block_cfg* c, const orc_block_weights* w, float** banks,

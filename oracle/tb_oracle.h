@@ -69,6 +69,10 @@ void orc_attention(const float* q, int64_t ldq, const float* k, const float* v, 
 /* memory-bank store: slot weights from the mean query row against the keys
  * (use_scores) or update_rate; memory[s,:] = (1-w_s) memory[s,:] + w_s state,
  * rounded to dtype.  keys rows of stride ldk, queries [T, ldq], state [H]. */
+// y = act(x) elementwise (ORC_ACT_GELU: tanh form; ORC_ACT_SIGMOID)
+void orc_activation(const float* x, int64_t n, int act, float* y);
+// rows[s, :] = (1 - w[s]) rows[s, :] + w[s] v, rounded to dtype (rows [Ms, n])
+void orc_ema_rows(float* rows, int Ms, int64_t n, const float* v, const float* w, int dtype);
 void orc_memory_store(float* memory, const float* keys, int64_t ldk, const float* queries,
                       int64_t ldq, int64_t T, const float* state, int Ms, int H, int nh,
                       float rate, int use_scores, int dtype);
@@ -125,6 +129,13 @@ int orc_block_decode_step_prepared(const void* prepared, const orc_block_cfg* c,
                                    float* y);
 
 /* Embedding gather + n_layers blocks (weights[l], banks[l]).  tokens [B*S]. */
+// Forward with a prepared block; kvm_in ([Ms, 2H] K_M | V_M of the bank) is
+// used as given when not NULL (else made from the bank).
+int orc_block_forward_prepared(const void* prepared, const orc_block_cfg* c,
+                               const orc_block_weights* w, float* memory_inout,
+                               const float* kvm_in, const float* x, float* y, int B, int S);
+int orc_block_kvm_prepared(const void* prepared, const orc_block_cfg* c, const float* memory,
+                           float* kvm_out);
 int orc_model_forward(const orc_block_cfg* c, const orc_block_weights* w, float** banks,
                       int n_layers, const float* embedding, int vocab, const int32_t* tokens,
                       float* y, int B, int S);
