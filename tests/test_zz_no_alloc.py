@@ -68,14 +68,17 @@ def test_noalloc_store_matches_allocating_store_twice(ltm, dt):
 
 
 def test_noalloc_store_rejects_sizes_beyond_its_scratch(ltm):
+    """With attention-score slot weights the scratch holds round_up(H, 64) +
+    Ms floats: 15360 + 51200 = 66560 > 65536 is refused (51200 slots is the
+    slot-weight kernel's own limit, so the scratch is what refuses)."""
     import torch
-    H, Ms = 4096, 65536 - 4096 + 1  # round_up(H, 64) + Ms = 65537 > 65536
+    H, Ms = 15360, 51200
     mem = torch.zeros((Ms, H), dtype=torch.bfloat16, device="cuda")
     keys = torch.zeros((Ms, H), dtype=torch.bfloat16, device="cuda")
     q = torch.zeros((4, H), dtype=torch.bfloat16, device="cuda")
     state = torch.zeros(H, dtype=torch.float32, device="cuda")
     with pytest.raises(ltm.LtmError) as e:
-        ltm.memory_store_noalloc(mem, keys, q, state, 32, 0.9, False)
+        ltm.memory_store_noalloc(mem, keys, q, state, 32, 0.9, True)
     assert e.value.status == ltm.ERR_INVALID_ARG
     assert "scratch" in str(e.value)
 
