@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the side workloads measured after the headline at N = 1")
+    ap.add_argument("--no-sp", action="store_true",
+                    help="tensor parallel without sequence parallelism (every rank holds the "
+                         "full activations; allreduce after the row-parallel projections)")
     ap.add_argument("--layers", type=int, default=None, help=argparse.SUPPRESS)
     ap.add_argument("--config", choices=["prefill", "tp", "w4a16", "decode"], default="tp",
                     help="tp: the 8-layer hidden-8192 W8A8 prefill, tensor-parallel over the N "
@@ -509,6 +512,12 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
         del w
     gen = torch.Generator(device=dev).manual_seed(7)
     x = (torch.randn((B, S, H), generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    # sequence parallelism: each rank holds its B*S/N consecutive rows of the
+    # activations between layers (the rows of whole sequences when N divides B)
+    sp = ws > 1 and not args.no_sp
+    Tr = B * S // ws
+    if sp:
+        x = x.reshape(B * S, H)[rank * Tr:(rank + 1) * Tr].contiguous()
     bufs = (torch.empty_like(x), torch.empty_like(x))
     stream = torch.cuda.current_stream()
 
@@ -516,7 +525,10 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
         a = inp
         for i in range(L):
             o = bufs[i % 2]
-            blk.forward(a, out=o)
+            if sp:
+                blk.forward_sp(a, B, S, out=o)
+            else:
+                blk.forward(a, out=o)
             a = o
         return a
 
@@ -551,10 +563,16 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     total_ms = float(t.item())
     value = B * S * args.steps / (total_ms * 1e-3)
 
-    # end to end: pinned H2D of the input hidden states, the layers, D2H of
-    # each sequence's last hidden state
+    # end to end: pinned H2D of the input hidden states (this rank's rows
+    # under sequence parallelism), the layers, D2H of the last hidden state
+    # of each sequence (that this rank holds)
     x_host = x.cpu().pin_memory()
-    last_host = torch.empty((B, H), dtype=torch.bfloat16).pin_memory()
+    if sp:
+        rows = torch.arange(rank * Tr, (rank + 1) * Tr, device=dev)
+        last_idx = (rows[(rows + 1) % S == 0] - rank * Tr).contiguous()
+    else:
+        last_idx = torch.arange(S - 1, B * S, S, device=dev)
+    last_host = torch.empty((last_idx.numel(), H), dtype=torch.bfloat16).pin_memory()
     barrier()
     e2e_evs = []
     for _ in range(args.steps):
@@ -562,7 +580,7 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
         s_.record(stream)
         x.copy_(x_host, non_blocking=True)
         y = forward_all(x)
-        last_host.copy_(y[:, -1, :], non_blocking=True)
+        last_host.copy_(y.reshape(-1, H).index_select(0, last_idx), non_blocking=True)
         e_.record(stream)
         e2e_evs.append((s_, e_))
     torch.cuda.synchronize()
@@ -595,7 +613,8 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
             "data": "synthetic (hidden states N(0,0.02^2), weights N(0,0.02), random init)",
             "config": {"workload": W4_WORKLOAD_NAME if w4a16 else TP_WORKLOAD_NAME, "layers": L,
                        "global_batch": B,
-                       "seq_len": S, "act_dtype": "bf16", "parallelism": f"tp{ws}",
+                       "seq_len": S, "act_dtype": "bf16",
+                       "parallelism": f"tp{ws}" + ("-sp" if sp else ""),
                        "tokens_per_s_per_gpu": round(value / ws, 1),
                        "comm_fraction_of_rank0_step": round(comm_ms / all_ms, 4) if all_ms else None,
                        "weights": "one random-init block's shard applied at every layer",
@@ -603,9 +622,10 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x_host.numel() * 2),
                     "d2h_bytes_per_step": int(last_host.numel() * 2),
-                    "copies": "H2D of the [B,S,H] input hidden states from pinned memory; D2H "
-                              "of each sequence's last output hidden state (what the next "
-                              "step of a prefill needs); the [B,S,H] output stays on the device"},
+                    "copies": "H2D of the input hidden states from pinned memory (per rank: "
+                              "its rows under sequence parallelism, else all [B,S,H]); D2H of "
+                              "each sequence's last output hidden state (what the next step "
+                              "of a prefill needs); the rest of the output stays on the device"},
             "gpu_launches": int(launches),
             "clocks": clocks,
             "roofline": roofline,

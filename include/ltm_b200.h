@@ -126,6 +126,42 @@ LTM_API ltm_status ltm_dequantize_int4_grouped(const uint8_t* packed, const floa
                                        int64_t N, int64_t K, int group_size, void* out,
                                        ltm_dtype out_dtype, void* stream);
 
+/* ----------------------------------------------------------- calibration -- */
+/* Activation-range calibrators for static INT8 scales: QuantizationCalibrator
+ * and its MinMax / Percentile / MSE subclasses
+ * (include/core/quantization/quantizer.cuh:124-175,
+ * src/core/quantization/calibrator.cu:61-264), on the device.
+ *   MINMAX      min and max of everything collected;
+ *   PERCENTILE  the sorted values at lo = (size_t)((100 - p) * n / 100) and
+ *               hi = (size_t)(p * n / 100) (fp32 arithmetic, hi <= n - 1),
+ *               exact (radix select, no sort);
+ *   MSE         [-c a, c a] for the c in {1/100, ..., 100/100} (a = max |x|)
+ *               whose symmetric INT8 quantize-dequantize has the least
+ *               squared error over the collected values (first minimum).
+ * compute_range writes host floats (it synchronizes the stream); with nothing
+ * collected it gives [0, 0].  A static symmetric scale is then
+ * max(|min|, |max|) / 127. */
+typedef enum ltm_calibration {
+  LTM_CALIB_MINMAX = 0,
+  LTM_CALIB_PERCENTILE = 1,
+  LTM_CALIB_MSE = 2
+} ltm_calibration;
+typedef struct ltm_calibrator ltm_calibrator;
+LTM_API ltm_status ltm_calibrator_create(int method, float percentile, int device,
+                                         ltm_calibrator** out);
+LTM_API ltm_status ltm_calibrator_collect(ltm_calibrator* c, const void* data, ltm_dtype dtype,
+                                          int64_t n, void* stream);
+LTM_API ltm_status ltm_calibrator_compute_range(ltm_calibrator* c, float* min_val,
+                                                float* max_val, void* stream);
+LTM_API ltm_status ltm_calibrator_reset(ltm_calibrator* c);
+LTM_API ltm_status ltm_calibrator_destroy(ltm_calibrator* c);
+/* Static per-tensor INT8 with a calibrated scale (symmetricQuantizeKernel,
+ * src/core/quantization/quantizer.cu:93-105, plus the clamp):
+ *   q = clamp(round_half_away(x / scale), -127, 127), IEEE division;
+ *   scale == 0 => q = 0. */
+LTM_API ltm_status ltm_quantize_int8_static(const void* x, ltm_dtype dtype, int64_t n, float scale,
+                                            int8_t* q, void* stream);
+
 /* --------------------------------------------------------------- linears -- */
 /* Quantized replacements of ops::matmul + bias add (src/core/ops/mma_ops.cu:59-92,
  * src/core/ops/fused_ops.cu:187-210) and of the per-token FFN kernel
@@ -327,6 +363,29 @@ LTM_API ltm_status ltm_block_decode_step(ltm_block* blk, const void* x, void* y,
                                          void* v_cache, int64_t max_positions, int cache_len, int B,
                                          void* stream);
 
+/* The decode step with a cache length per sequence (the continuous-batching
+ * form of the CacheManager stubs, python_bindings/src/main.cpp:101-135):
+ * cache_lens is a device int32 [B]; sequence b's new token sits at position
+ * cache_lens[b], is written there and attends positions [0, cache_lens[b]].
+ * The launches depend only on B and max_positions, not on the lengths, so
+ * one step can be captured in a CUDA graph once (after a first, uncaptured
+ * call has sized the workspace) and replayed while the lengths move on the
+ * device.  A length outside [0, max_positions) skips that sequence's cache
+ * write and attention (its attention output is 0) and sets the device error
+ * word (ltm_device_error: 5). */
+LTM_API ltm_status ltm_block_decode_step_ragged(ltm_block* blk, const void* x, void* y,
+                                                void* k_cache, void* v_cache,
+                                                int64_t max_positions, const int32_t* cache_lens,
+                                                int B, void* stream);
+
+/* Prefill that also fills the decode KV caches: ltm_block_forward plus the
+ * post-RoPE K and V of positions [0, S) of every sequence written to the
+ * head-major caches [B, heads, max_positions, head_dim] (this rank's heads
+ * under tensor parallelism), so decode steps can follow at cache_len = S. */
+LTM_API ltm_status ltm_block_forward_with_cache(ltm_block* blk, const void* x, void* y, int B,
+                                                int S, void* k_cache, void* v_cache,
+                                                int64_t max_positions, void* stream);
+
 /* Memory write of the block's own bank: MemoryBank<T>::store
  * (src/core/ltm/memory_bank.cu:242-274) with a caller-given state (fp32 [H],
  * device) and, with use_attention_scores, slot weights from the mean of the T
@@ -354,6 +413,23 @@ LTM_API ltm_status ltm_block_get_memory(ltm_block* blk, void* out, void* stream)
  * Under tensor parallelism H and F are this rank's widths (s, m: full H). */
 LTM_API ltm_status ltm_block_intermediate(ltm_block* blk, const char* name, void* out,
                                           void* stream, int64_t* rows, int64_t* cols, int* kind);
+/* Quantized checkpoints: TitanBlock<T>::save / load
+ * (include/core/transformer/titan_inspired_block.cuh:147-154) and
+ * MemoryBank<T>::save / load (include/core/ltm/memory_bank.cuh:152-159),
+ * declared but never defined in the reference.  A versioned little-endian
+ * file: a header (magic "LTMB200", format version, kind, the writer's block
+ * and quantization configs, tensor-parallel size / rank, FNV-1a 64 header
+ * checksum) and one checksummed section per device buffer -- the quantized
+ * codes, scales, zero-points and biases of every linear, the LayerNorm
+ * parameters and the bank.  load restores the exact codes (no requantizing)
+ * into a block created with the same dimensions, scheme, dtype and
+ * tensor-parallel rank (LTM_ERR_INVALID_ARG otherwise, or on a checksum
+ * mismatch); after it the block is ready without ltm_block_load_weights.
+ * The *_memory pair saves / loads the bank [Ms, H] alone. */
+LTM_API ltm_status ltm_block_save(ltm_block* blk, const char* path);
+LTM_API ltm_status ltm_block_load(ltm_block* blk, const char* path);
+LTM_API ltm_status ltm_block_save_memory(ltm_block* blk, const char* path);
+LTM_API ltm_status ltm_block_load_memory(ltm_block* blk, const char* path);
 LTM_API ltm_status ltm_block_destroy(ltm_block* blk);
 
 /* ------------------------------------------------------ tensor parallel -- */
@@ -384,11 +460,24 @@ LTM_API ltm_status ltm_comm_destroy(ltm_comm* comm);
  * block. */
 LTM_API ltm_status ltm_block_create_tp(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
                                ltm_comm* comm, ltm_block** out);
+/* Sequence-parallel forward of a tensor-parallel block (f16 / bf16): x_local
+ * and y_local are this rank's B*S / nranks consecutive rows [T / nranks, H]
+ * of the [B*S, H] activations (B*S a multiple of nranks).  The LayerNorms,
+ * the gate and the gated integration run on the local rows; the LayerNorm
+ * outputs (int8 codes + scales for W8A8) are all-gathered for the
+ * column-parallel projections and the row-parallel partial sums are
+ * reduce-scattered to the rows' owners, so no rank repeats another's row
+ * work.  Consecutive layers chain y_local -> x_local with no gather. */
+LTM_API ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, void* y_local, int B,
+                                        int S, void* stream);
 
 /* ----------------------------------------------------------------- model -- */
 /* Multi-layer model (token embedding gather + n_layers Titan blocks), the
- * forward of TitanModel (python_bindings/ltm/model.py:159-215) without the
- * LM head. */
+ * forward of TitanModel (python_bindings/ltm/model.py:159-215), plus the LM
+ * head of TitanForCausalLM (python_bindings/ltm/model.py:217-231,261) and a
+ * prefill / decode-step pair over per-layer KV caches (the generation loop
+ * of python_bindings/ltm/inference.py:131-260 with its CacheManager stubs,
+ * python_bindings/src/main.cpp:101-135). */
 typedef struct ltm_model ltm_model;
 LTM_API ltm_status ltm_model_create(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
                             int n_layers, int vocab_size, int device, ltm_model** out);
@@ -398,6 +487,40 @@ LTM_API ltm_status ltm_model_load_layer(ltm_model* m, int layer, const ltm_block
 /* tokens: device int32 [B,S]; hidden_out: device [B,S,H] act_dtype. */
 LTM_API ltm_status ltm_model_forward(ltm_model* m, const int32_t* tokens, void* hidden_out, int B, int S,
                              void* stream);
+/* LM head weight: host fp32 [vocab, H] (nn.Linear(H, vocab, bias=False)),
+ * quantized like the blocks' linears (W8A8: int8 per row, the hidden rows
+ * quantized per token; W4A16: int4 group 128; W8A32: int8, fp32 rows). */
+LTM_API ltm_status ltm_model_load_lm_head(ltm_model* m, const float* weight);
+/* logits [rows, vocab] (act_dtype, device) = hidden rows (device, row stride
+ * row_stride elements, e.g. S * H for the last position of each sequence)
+ * times the LM head weight. */
+LTM_API ltm_status ltm_model_lm_head(ltm_model* m, const void* hidden, int64_t rows,
+                                     int64_t row_stride, void* logits, void* stream);
+/* Prefill of B prompts of S tokens (device int32 [B,S]): the model forward
+ * with every layer writing the post-RoPE K / V of positions [0, S) into its
+ * caches k_caches[l] / v_caches[l] (host arrays of n_layers device pointers to
+ * [B, heads, max_positions, head_dim] act_dtype); hidden_out ([B,S,H], or
+ * NULL) receives the last layer's output, logits_last ([B, vocab], or NULL)
+ * the LM head of each sequence's last position. */
+LTM_API ltm_status ltm_model_prefill(ltm_model* m, const int32_t* tokens, int B, int S,
+                                     void* const* k_caches, void* const* v_caches,
+                                     int64_t max_positions, void* hidden_out, void* logits_last,
+                                     void* stream);
+/* One decode step of the model: tokens (device int32 [B]) at positions
+ * cache_lens[b] (device int32 [B]; ltm_block_decode_step_ragged for every
+ * layer), hidden_out ([B, H] or NULL), logits ([B, vocab] or NULL).  The
+ * launches depend on B and max_positions only: after one uncaptured call the
+ * step (with ltm_greedy_next_tokens) can be captured in a CUDA graph and
+ * replayed for a whole greedy generation. */
+LTM_API ltm_status ltm_model_decode_step(ltm_model* m, const int32_t* tokens,
+                                         const int32_t* cache_lens, int B, void* const* k_caches,
+                                         void* const* v_caches, int64_t max_positions,
+                                         void* hidden_out, void* logits, void* stream);
+/* Greedy next tokens: tokens_out[b] = argmax of logits row b ([B, vocab],
+ * dtype; lowest index on ties); cache_lens[b] += 1 when cache_lens is not
+ * NULL (device int32 [B]). */
+LTM_API ltm_status ltm_greedy_next_tokens(const void* logits, ltm_dtype dtype, int B, int vocab,
+                                          int32_t* tokens_out, int32_t* cache_lens, void* stream);
 LTM_API ltm_status ltm_model_destroy(ltm_model* m);
 
 #ifdef __cplusplus

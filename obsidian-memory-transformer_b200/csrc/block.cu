@@ -48,7 +48,7 @@ __global__ void add3_kernel(const T* __restrict__ a, const T* __restrict__ b,
                             const T* __restrict__ c, T* __restrict__ y, int64_t n) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    y[i] = from_f32<T>(to_f32(a[i]) + to_f32(b[i]) + to_f32(c[i]));
+    y[i] = from_f32<T>(to_f32(a[i]) + to_f32(b[i]) + (c ? to_f32(c[i]) : 0.0f));
 }
 
 int grid_for(int64_t n) {
@@ -221,6 +221,7 @@ struct ltm_block {
   int64_t ws_T = 0, last_T = 0;
   DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, spm, y, zq, zs, z,
       u, uq, us, amax;
+  DevBuf sploc;  // sequence parallel: this rank's rows of s | m [2, T/tp, H]
   MemoryWriteState mw;
   // decode: K_M | V_M kept resident between steps (kvm_fresh: kvmb holds them
   // for the current bank), the state row of the write and its projection,
@@ -319,15 +320,18 @@ struct ltm_block {
   }
 
   // 3. fused Q | K | V | Qm projection with RoPE on Q, K at position
-  // pos0 + (row % S)
-  void qkv_proj(const void* hin, int64_t T, int S, int pos0, cudaStream_t st) {
+  // pos0 + (row % S), or at row_pos[row] when given (device [T])
+  void qkv_proj(const void* hin, int64_t T, int S, int pos0, cudaStream_t st,
+                const int* row_pos = nullptr) {
     Epilogue ep;
     ep.out = qkv.ptr;
     ep.ldo = 4 * Hl;
-    ep.rope = rope.as<float2>() + static_cast<int64_t>(pos0) * (dh / 2);
+    ep.rope = rope.as<float2>() + (row_pos ? 0 : static_cast<int64_t>(pos0) * (dh / 2));
     ep.rope_cols = cfg.use_rotary ? 2 * Hl : 0;
     ep.seq_len = S;
     ep.head_dim = dh;
+    ep.row_pos = row_pos;
+    ep.rope_rows = rope_S;
     qkvm.run(hin, hq.as<int8_t>(), hs.as<float>(), T, cfg.use_rotary ? kEpiRope : kEpiPlain, dt,
              ep, st, &wdq);
   }
@@ -457,6 +461,146 @@ struct ltm_block {
     launch_rows_ema(kvmb.ptr, 2 * Hl, 2 * Hl, kcv.ptr, wslot, cfg.memory_update_rate, Ms, dt, st);
   }
 
+  // Sequence-parallel tensor-parallel forward (Megatron sequence
+  // parallelism): x_loc / out_loc are this rank's T / tp consecutive rows of
+  // the [B*S, H] activations.  LayerNorms, the gate and the gated
+  // integration run on the local rows only; the LayerNorm outputs (int8
+  // codes and scales for W8A8) are all-gathered for the column-parallel
+  // projections, and the row-parallel output / FFN-down partial sums are
+  // reduce-scattered back to the rows' owners, so no rank repeats another's
+  // row work and the bytes on NVLink are the reduce-scatter + all-gather of
+  // the collectives they replace (the LayerNorm all-gathers in int8).
+  void forward_sp(const void* x_loc, void* out_loc, int B, int S, cudaStream_t st) {
+    const int64_t T = static_cast<int64_t>(B) * S;
+    const int64_t Tr = T / tp, r0 = static_cast<int64_t>(tpr) * Tr;
+    ensure_ws(T);
+    last_T = T;
+    const size_t a = act_bytes();
+    sploc.ensure(static_cast<size_t>(2 * Tr) * H * a);
+    if (cfg.use_rotary) ensure_rope(S);
+    const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
+    // 1. LN1 of the local rows into rows [r0, r0 + Tr) of the full buffers
+    //    (+ the int8 of x's local rows for the gate), then all-gather
+    if (w8a8) {
+      launch_ln_x2(x_loc, dt, Tr, H, ln1_g.as<float>(), ln1_b.as<float>(), nullptr,
+                   hq.as<int8_t>() + r0 * H, hs.as<float>() + r0, xq.as<int8_t>(), xs.as<float>(),
+                   cfg.use_layer_norm != 0, st);
+      comm_group_start();
+      comm_allgather_bytes(comm, hq.as<int8_t>() + r0 * H, hq.ptr, Tr * H, st);
+      comm_allgather_bytes(comm, hs.as<float>() + r0, hs.ptr, Tr * sizeof(float), st);
+      comm_group_end("nccl_allgather", st);
+    } else {
+      char* hl = static_cast<char*>(h.ptr) + r0 * H * a;
+      if (cfg.use_layer_norm)
+        launch_ln_x2(x_loc, dt, Tr, H, ln1_g.as<float>(), ln1_b.as<float>(), hl, nullptr, nullptr,
+                     nullptr, nullptr, true, st);
+      else
+        LTM_CUDA_TRY(cudaMemcpyAsync(hl, x_loc, Tr * H * a, cudaMemcpyDeviceToDevice, st));
+      comm_allgather_bytes(comm, hl, h.ptr, Tr * H * a, st);
+    }
+    // 2-4. K_M | V_M, Q | K | V | Qm of all T rows for this rank's heads, the
+    //      two attentions
+    compute_kvm(st);
+    qkv_proj(h.ptr, T, S, 0, st);
+    {
+      AttnParams p{};
+      p.q = qkv.ptr;
+      p.k = static_cast<const char*>(qkv.ptr) + Hl * a;
+      p.v = static_cast<const char*>(qkv.ptr) + 2 * Hl * a;
+      p.o = os.ptr;
+      p.ldq = p.ldk = p.ldv = 4 * Hl;
+      p.ldo = Hl;
+      p.q_batch_rows = S;
+      p.kv_batch_rows = S;
+      p.Sq = S;
+      p.Skv = S;
+      p.nh = nhl;
+      p.causal_offset = 0;
+      launch_attention(p, B, dh, true, dt, st);
+      mem_attention(B, S, st);
+    }
+    // 5. output projections: partial sums of all rows, reduce-scattered to
+    //    the rows' owners (rank 0's partial carries the biases)
+    if (w8a8) {
+      quant_rows(os.ptr, T, Hl, osq.as<int8_t>(), oss.as<float>(), amax.as<float>(), st);
+      quant_rows(om_.ptr, T, Hl, omq.as<int8_t>(), oms.as<float>(), amax.as<float>() + T, st);
+    }
+    void* sp = spm.ptr;
+    void* mp = static_cast<char*>(spm.ptr) + T * H * a;
+    void* s_loc = sploc.ptr;
+    void* m_loc = static_cast<char*>(sploc.ptr) + Tr * H * a;
+    {
+      Epilogue ep;
+      ep.out = sp;
+      ep.ldo = H;
+      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+      ep.out = mp;
+      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+    }
+    comm_group_start();
+    comm_reduce_scatter(comm, sp, s_loc, Tr * H, dt, st);
+    comm_reduce_scatter(comm, mp, m_loc, Tr * H, dt, st);
+    comm_group_end("nccl_reduce_scatter", st);
+    // 6. gate and gated integration of the local rows
+    if (cfg.use_memory_gating) {
+      Epilogue ep;
+      ep.act = LTM_EPI_SIGMOID;
+      ep.out = y.ptr;
+      ep.ldo = H;
+      ep.aux0 = s_loc;
+      ep.aux1 = m_loc;
+      ep.aux2 = x_loc;
+      ep.ld_aux = H;
+      if (q.memory_write) mw.prepare_gate_epilogue(ep, H, st);
+      g.run(x_loc, xq.as<int8_t>(), xs.as<float>(), Tr, kEpiGateMix, dt, ep, st, &wdq);
+    } else {
+      launch_add3(s_loc, m_loc, x_loc, y.ptr, Tr * H, dt, st);
+    }
+    // 7. LN2 of the local rows, all-gathered for the column-parallel FFN-up
+    if (w8a8) {
+      launch_ln_x2(y.ptr, dt, Tr, H, ln2_g.as<float>(), ln2_b.as<float>(), nullptr,
+                   zq.as<int8_t>() + r0 * H, zs.as<float>() + r0, nullptr, nullptr,
+                   cfg.use_layer_norm != 0, st);
+      comm_group_start();
+      comm_allgather_bytes(comm, zq.as<int8_t>() + r0 * H, zq.ptr, Tr * H, st);
+      comm_allgather_bytes(comm, zs.as<float>() + r0, zs.ptr, Tr * sizeof(float), st);
+      comm_group_end("nccl_allgather", st);
+    } else {
+      char* zl = static_cast<char*>(z.ptr) + r0 * H * a;
+      if (cfg.use_layer_norm)
+        launch_ln_x2(y.ptr, dt, Tr, H, ln2_g.as<float>(), ln2_b.as<float>(), zl, nullptr, nullptr,
+                     nullptr, nullptr, true, st);
+      else
+        LTM_CUDA_TRY(cudaMemcpyAsync(zl, y.ptr, Tr * H * a, cudaMemcpyDeviceToDevice, st));
+      comm_allgather_bytes(comm, zl, z.ptr, Tr * H * a, st);
+    }
+    {
+      Epilogue ep;
+      ep.act = LTM_EPI_GELU;
+      ep.out = u.ptr;
+      ep.ldo = Fl;
+      w1.run(z.ptr, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+    }
+    if (w8a8) quant_rows(u.ptr, T, Fl, uq.as<int8_t>(), us.as<float>(), amax.as<float>(), st);
+    // 8. FFN-down partial sums of all rows (rank 0's carry b2), reduce-
+    //    scattered; the owner adds its rows' residual
+    {
+      Epilogue ep;
+      ep.out = sp;
+      ep.ldo = H;
+      w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+    }
+    comm_reduce_scatter(comm, sp, out_loc, Tr * H, dt, st);
+    launch_add3(out_loc, y.ptr, nullptr, out_loc, Tr * H, dt, st);
+    // 9. memory write: column sums of the local rows, summed over the ranks
+    if (q.memory_write && cfg.use_memory_gating) {
+      mw.update_bank(memory.ptr, kvmb.ptr, 2 * Hl, static_cast<const char*>(qkv.ptr) + 3 * Hl * a,
+                     4 * Hl, T, H, nhl, nh, dh, Ms, cfg.memory_update_rate,
+                     q.use_attention_scores != 0, dt, comm, st, /*colsum_partial=*/true);
+      kvm_fresh = false;
+    }
+  }
+
   // Memory write of a caller-given state (fp32 [H]) with slot weights from
   // the mean of T memory-query rows (this rank's heads' columns, stride ldq)
   // against the current K_M; K_M | V_M follow when they are resident.
@@ -477,7 +621,10 @@ struct ltm_block {
     if (kvm_fresh) follow_kvm(state, 1.0f, wslot, st);
   }
 
-  void forward(const void* x, void* out, int B, int S, cudaStream_t st) {
+  // kc / vc (optional): head-major caches [B, nhl, P, dh] that receive the
+  // post-RoPE keys / values of positions [0, S) of every sequence.
+  void forward(const void* x, void* out, int B, int S, cudaStream_t st, void* kc = nullptr,
+               void* vc = nullptr, int64_t P = 0) {
     const int64_t T = static_cast<int64_t>(B) * S;
     ensure_ws(T);
     last_T = T;
@@ -486,6 +633,7 @@ struct ltm_block {
     // 2. memory keys / values from the bank
     compute_kvm(st);
     qkv_proj(hin, T, S, 0, st);
+    if (kc) launch_kv_fill(qkv.ptr, 4 * Hl, Hl, dh, kc, vc, P, B, S, dt, st);
     // 4. causal self-attention, memory attention
     {
       const size_t a = act_bytes();
@@ -512,25 +660,127 @@ struct ltm_block {
   // One decode step: x, out [B, H], every sequence's new token at position L;
   // k_cache / v_cache [B, nhl, P, dh] hold positions [0, L) and receive
   // position L.
+  // cache_lens (optional, device [B]): sequence b's new token sits at
+  // position cache_lens[b] (L is ignored); its launches then depend on P and
+  // B only, so the step can be captured once and replayed as the lengths move.
   void decode(const void* x, void* out, void* kc, void* vc, int64_t P, int L, int B,
-              cudaStream_t st) {
+              cudaStream_t st, const int* cache_lens = nullptr) {
     const int64_t T = B;
     ensure_ws(T);
     last_T = T;
-    if (cfg.use_rotary) ensure_rope(L + 1);
+    if (cfg.use_rotary) ensure_rope(cache_lens ? static_cast<int>(P) : L + 1);
     if (!kvm_fresh) compute_kvm(st);
     const void* hin = ln1(x, T, st);
-    qkv_proj(hin, T, 1, L, st);
-    launch_kv_append(qkv.ptr, 4 * Hl, Hl, dh, kc, vc, P, L, B, dt, st);
+    qkv_proj(hin, T, 1, L, st, cache_lens);
+    launch_kv_append(qkv.ptr, 4 * Hl, Hl, dh, kc, vc, P, L, B, dt, st, cache_lens);
     const size_t pb = decode_partials_bytes(B, nhl, dh, P);
     if (pb > dpart.bytes) dpart.ensure(pb);
-    launch_decode_attention(qkv.ptr, 4 * Hl, kc, vc, P, L + 1, B, nhl, dh, dt, dpart.as<float>(),
-                            os.ptr, Hl, st);
+    launch_decode_attention(qkv.ptr, 4 * Hl, kc, vc, P, cache_lens ? static_cast<int>(P) : L + 1,
+                            B, nhl, dh, dt, dpart.as<float>(), os.ptr, Hl, st, cache_lens);
     mem_attention(1, B, st);  // the batch's rows share the bank: one group of B queries
     tail(x, out, T, st);
     if (q.memory_write && cfg.use_memory_gating) write(T, true, st);
   }
 };
+
+namespace ltm_b200 {
+
+// Sizes of a QLinear's buffers for an [n, k] weight of `scheme`, with or
+// without a bias; the buffers are made to hold them.
+static void shape_linear(QLinear& l, int scheme, int64_t n, int64_t k, bool with_bias) {
+  l.N = n;
+  l.K = k;
+  l.scheme = scheme;
+  if (scheme == LTM_SCHEME_W4A16) {
+    l.q4.ensure(n * k / 2);
+    l.s4.ensure(n * (k / 128) * sizeof(float));
+    l.z4.ensure(n * (k / 128));
+  } else {
+    l.q8.ensure(n * k);
+    l.s8.ensure(n * sizeof(float));
+  }
+  if (with_bias)
+    l.bias.ensure(n * sizeof(float));
+  else
+    l.bias.release();
+}
+
+static void linear_sections(std::vector<StateSection>& out, const std::string& name,
+                            const QLinear& l) {
+  const int64_t n = l.N, k = l.K;
+  if (l.scheme == LTM_SCHEME_W4A16) {
+    out.push_back({name + ".q4", l.q4.ptr, static_cast<size_t>(n * k / 2)});
+    out.push_back({name + ".s4", l.s4.ptr, static_cast<size_t>(n * (k / 128) * sizeof(float))});
+    out.push_back({name + ".z4", l.z4.ptr, static_cast<size_t>(n * (k / 128))});
+  } else {
+    out.push_back({name + ".q8", l.q8.ptr, static_cast<size_t>(n * k)});
+    out.push_back({name + ".s8", l.s8.ptr, static_cast<size_t>(n * sizeof(float))});
+  }
+  if (l.bias.ptr) out.push_back({name + ".bias", l.bias.ptr, static_cast<size_t>(n * sizeof(float))});
+}
+
+std::vector<StateSection> block_state(ltm_block* b, bool weights, bool bank, bool allocate) {
+  const int H = b->H, F = b->F, Hl = b->Hl, Fl = b->Fl;
+  const bool ub = b->cfg.use_bias != 0, lead = b->tpr == 0, tp1 = b->tp == 1;
+  const int sc = b->q.scheme;
+  if (allocate) {
+    if (weights) {
+      shape_linear(b->qkvm, sc, 4 * Hl, H, ub);
+      shape_linear(b->kvm, sc, 2 * Hl, H, ub);
+      shape_linear(b->o, sc, H, tp1 ? H : Hl, ub && (tp1 || lead));
+      shape_linear(b->om, sc, H, tp1 ? H : Hl, ub && (tp1 || lead));
+      shape_linear(b->g, sc, H, H, ub);
+      shape_linear(b->w1, sc, Fl, H, ub);
+      shape_linear(b->w2, sc, H, tp1 ? F : Fl, ub && (tp1 || lead));
+      if (b->cfg.use_layer_norm)
+        for (DevBuf* d : {&b->ln1_g, &b->ln1_b, &b->ln2_g, &b->ln2_b}) d->ensure(H * sizeof(float));
+    }
+    if (bank) b->memory.ensure(static_cast<size_t>(b->Ms) * H * dtype_size(b->dt));
+  }
+  std::vector<StateSection> out;
+  if (weights) {
+    linear_sections(out, "qkvm", b->qkvm);
+    linear_sections(out, "kvm", b->kvm);
+    linear_sections(out, "o", b->o);
+    linear_sections(out, "om", b->om);
+    linear_sections(out, "gate", b->g);
+    linear_sections(out, "ffn_up", b->w1);
+    linear_sections(out, "ffn_down", b->w2);
+    if (b->cfg.use_layer_norm) {
+      out.push_back({"ln1.gamma", b->ln1_g.ptr, H * sizeof(float)});
+      out.push_back({"ln1.beta", b->ln1_b.ptr, H * sizeof(float)});
+      out.push_back({"ln2.gamma", b->ln2_g.ptr, H * sizeof(float)});
+      out.push_back({"ln2.beta", b->ln2_b.ptr, H * sizeof(float)});
+    }
+  }
+  if (bank)
+    out.push_back({"memory", b->memory.ptr, static_cast<size_t>(b->Ms) * H * dtype_size(b->dt)});
+  return out;
+}
+
+void block_state_loaded(ltm_block* b, bool weights) {
+  if (weights) {
+    b->kvmb.ensure(static_cast<size_t>(b->Ms) * 2 * b->Hl * dtype_size(b->dt));
+    if (b->q.scheme == LTM_SCHEME_W8A8) {
+      b->mq.ensure(static_cast<size_t>(b->Ms) * b->H);
+      b->ms.ensure(static_cast<size_t>(b->Ms) * sizeof(float));
+    }
+    b->loaded = true;
+  }
+  b->kvm_fresh = false;  // K_M | V_M follow the (new) bank at the next use
+}
+
+void block_identity(const ltm_block* b, ltm_block_config* cfg, ltm_quant_config* q, int* tp,
+                    int* tpr, int* device, bool* loaded) {
+  *cfg = b->cfg;
+  *q = b->q;
+  *tp = b->tp;
+  *tpr = b->tpr;
+  *device = b->device;
+  *loaded = b->loaded;
+}
+
+}  // namespace ltm_b200
 
 namespace {
 
@@ -776,6 +1026,61 @@ extern "C" ltm_status ltm_block_decode_step(ltm_block* blk, const void* x, void*
   });
 }
 
+extern "C" ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, void* y_local,
+                                           int B, int S, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded, "block not created or weights not loaded");
+    LTM_REQUIRE(blk->tp > 1 && blk->comm, "sequence parallelism needs a tensor-parallel block");
+    LTM_REQUIRE(B >= 0 && S >= 0, "negative batch or sequence length");
+    if (B == 0 || S == 0) return;
+    const int64_t T = static_cast<int64_t>(B) * S;
+    LTM_REQUIRE(T % blk->tp == 0, "B * S must be a multiple of the tensor-parallel size");
+    LTM_REQUIRE(x_local && y_local && x_local != y_local, "x and y must be distinct device buffers");
+    LTM_REQUIRE(blk->dt != LTM_DTYPE_F32, "sequence parallelism needs f16 or bf16 activations");
+    DeviceGuard g(blk->device);
+    blk->forward_sp(x_local, y_local, B, S, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_block_forward_with_cache(ltm_block* blk, const void* x, void* y, int B,
+                                                   int S, void* k_cache, void* v_cache,
+                                                   int64_t max_positions, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded, "block not created or weights not loaded");
+    LTM_REQUIRE(B >= 0 && S >= 0, "negative batch or sequence length");
+    if (B == 0 || S == 0) return;
+    LTM_REQUIRE(x && y && x != y, "x and y must be distinct device buffers");
+    LTM_REQUIRE(k_cache && v_cache && k_cache != v_cache, "NULL or aliased KV cache");
+    LTM_REQUIRE(blk->dt != LTM_DTYPE_F32, "KV caches hold f16 or bf16 (W8A8 / W4A16)");
+    LTM_REQUIRE(S <= max_positions, "the prompt is longer than the cache");
+    LTM_REQUIRE((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 == 0,
+                "KV cache must be 16-byte aligned");
+    DeviceGuard g(blk->device);
+    blk->forward(x, y, B, S, as_stream(stream), k_cache, v_cache, max_positions);
+  });
+}
+
+extern "C" ltm_status ltm_block_decode_step_ragged(ltm_block* blk, const void* x, void* y,
+                                                   void* k_cache, void* v_cache,
+                                                   int64_t max_positions,
+                                                   const int32_t* cache_lens, int B,
+                                                   void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(blk && blk->loaded, "block not created or weights not loaded");
+    LTM_REQUIRE(B >= 0, "negative batch");
+    if (B == 0) return;
+    LTM_REQUIRE(x && y && x != y, "x and y must be distinct device buffers");
+    LTM_REQUIRE(k_cache && v_cache && k_cache != v_cache, "NULL or aliased KV cache");
+    LTM_REQUIRE(cache_lens, "NULL cache_lens");
+    LTM_REQUIRE(blk->dt != LTM_DTYPE_F32, "decode needs f16 or bf16 activations (W8A8 / W4A16)");
+    LTM_REQUIRE(max_positions >= 1 && max_positions < (1ll << 31), "max_positions out of range");
+    LTM_REQUIRE((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 == 0,
+                "KV cache must be 16-byte aligned");
+    DeviceGuard g(blk->device);
+    blk->decode(x, y, k_cache, v_cache, max_positions, 0, B, as_stream(stream), cache_lens);
+  });
+}
+
 extern "C" ltm_status ltm_block_memory_write(ltm_block* blk, const float* state,
                                              const void* queries, int64_t ldq, int64_t T,
                                              void* stream) {
@@ -881,6 +1186,65 @@ struct ltm_model {
   int device = 0, vocab = 0;
   DevBuf emb, a, b;
   int64_t ws_T = 0;
+  // LM head (TitanForCausalLM.lm_head, no bias): weight rows padded to a
+  // multiple of 32 (vocab_p); rows of hidden states gathered contiguously,
+  // their int8 codes / scales (W8A8), logits of the padded vocabulary when
+  // vocab != vocab_p
+  QLinear head;
+  bool head_loaded = false;
+  int vocab_p = 0;
+  DevBuf hrows, hq, hs, hlog, wdq;
+  int64_t head_rows = 0;
+
+  ltm_dtype dt() const { return q.act_dtype; }
+
+  // Makes sure the layer ping-pong buffers hold T rows.
+  void ensure_ws(int64_t T) {
+    if (T <= ws_T) return;
+    const size_t bytes = static_cast<size_t>(T) * cfg.hidden_dim * dtype_size(dt());
+    a.ensure(bytes);
+    b.ensure(bytes);
+    ws_T = T;
+  }
+
+  // logits [rows, vocab] (stride ld_logits) of `rows` hidden rows of stride
+  // ld_hidden elements.
+  void lm_head(const void* hidden, int64_t rows, int64_t ld_hidden, void* logits, int64_t ld_logits,
+               cudaStream_t st) {
+    const int H = cfg.hidden_dim;
+    const size_t es = dtype_size(dt());
+    if (rows > head_rows) {
+      hrows.ensure(static_cast<size_t>(rows) * H * es);
+      if (q.scheme == LTM_SCHEME_W8A8) {
+        hq.ensure(static_cast<size_t>(rows) * H);
+        hs.ensure(static_cast<size_t>(rows) * sizeof(float));
+      }
+      if (vocab_p != vocab) hlog.ensure(static_cast<size_t>(rows) * vocab_p * es);
+      head_rows = rows;
+    }
+    const void* in = hidden;
+    if (ld_hidden != H) {
+      LTM_CUDA_TRY(cudaMemcpy2DAsync(hrows.ptr, H * es, hidden, ld_hidden * es, H * es, rows,
+                                     cudaMemcpyDeviceToDevice, st));
+      in = hrows.ptr;
+    }
+    if (q.scheme == LTM_SCHEME_W8A8)
+      launch_rowwise_int8(in, dt(), rows, H, hq.as<int8_t>(), hs.as<float>(), st);
+    Epilogue ep;
+    const bool direct = vocab_p == vocab;
+    ep.out = direct ? logits : hlog.ptr;
+    ep.ldo = direct ? ld_logits : vocab_p;
+    head.run(in, hq.as<int8_t>(), hs.as<float>(), rows, kEpiPlain, dt(), ep, st, &wdq);
+    if (!direct)
+      LTM_CUDA_TRY(cudaMemcpy2DAsync(logits, ld_logits * es, hlog.ptr, vocab_p * es, vocab * es,
+                                     rows, cudaMemcpyDeviceToDevice, st));
+  }
+
+  void require_ready(bool need_head) const {
+    LTM_REQUIRE(emb.ptr, "model not created or embedding not loaded");
+    for (auto& l : layers) LTM_REQUIRE(l->loaded, "a layer has no weights");
+    if (need_head) LTM_REQUIRE(head_loaded, "LM head not loaded");
+  }
 };
 
 extern "C" ltm_status ltm_model_create(const ltm_block_config* cfg, const ltm_quant_config* qcfg,
@@ -927,12 +1291,7 @@ extern "C" ltm_status ltm_model_forward(ltm_model* m, const int32_t* tokens, voi
     cudaStream_t st = as_stream(stream);
     const int64_t T = static_cast<int64_t>(B) * S;
     const int H = m->cfg.hidden_dim;
-    const size_t bytes = T * H * dtype_size(m->q.act_dtype);
-    if (T > m->ws_T) {
-      m->a.ensure(bytes);
-      m->b.ensure(bytes);
-      m->ws_T = T;
-    }
+    m->ensure_ws(T);
     launch_embed_gather(m->emb.ptr, m->q.act_dtype, m->vocab, H, tokens, T, m->a.ptr, st);
     const void* cur = m->a.ptr;
     const size_t L = m->layers.size();
@@ -941,6 +1300,113 @@ extern "C" ltm_status ltm_model_forward(ltm_model* m, const int32_t* tokens, voi
       m->layers[i]->forward(cur, dst, B, S, st);
       cur = dst;
     }
+  });
+}
+
+extern "C" ltm_status ltm_model_load_lm_head(ltm_model* m, const float* weight) {
+  return guarded([&] {
+    LTM_REQUIRE(m && weight, "bad argument");
+    DeviceGuard g(m->device);
+    const int H = m->cfg.hidden_dim;
+    m->vocab_p = (m->vocab + 31) / 32 * 32;
+    std::vector<float> wp;
+    const float* w = weight;
+    if (m->vocab_p != m->vocab) {  // zero rows up to a multiple of 32
+      wp.assign(static_cast<size_t>(m->vocab_p) * H, 0.0f);
+      std::memcpy(wp.data(), weight, sizeof(float) * static_cast<size_t>(m->vocab) * H);
+      w = wp.data();
+    }
+    m->head.load(m->q, w, nullptr, m->vocab_p, H, nullptr);
+    m->head_loaded = true;
+  });
+}
+
+extern "C" ltm_status ltm_model_lm_head(ltm_model* m, const void* hidden, int64_t rows,
+                                        int64_t row_stride, void* logits, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(m && m->head_loaded, "model not created or LM head not loaded");
+    LTM_REQUIRE(rows >= 0 && row_stride >= m->cfg.hidden_dim, "bad rows / row stride");
+    if (rows == 0) return;
+    LTM_REQUIRE(hidden && logits, "NULL pointer");
+    DeviceGuard g(m->device);
+    m->lm_head(hidden, rows, row_stride, logits, m->vocab, as_stream(stream));
+  });
+}
+
+namespace {
+
+void check_caches(ltm_model* m, void* const* kc, void* const* vc, int64_t P) {
+  LTM_REQUIRE(kc && vc, "NULL cache pointer arrays");
+  LTM_REQUIRE(m->q.act_dtype != LTM_DTYPE_F32, "KV caches hold f16 or bf16 (W8A8 / W4A16)");
+  LTM_REQUIRE(P >= 1 && P < (1ll << 31), "max_positions out of range");
+  for (size_t i = 0; i < m->layers.size(); ++i) {
+    LTM_REQUIRE(kc[i] && vc[i] && kc[i] != vc[i], "NULL or aliased KV cache");
+    LTM_REQUIRE((reinterpret_cast<uintptr_t>(kc[i]) | reinterpret_cast<uintptr_t>(vc[i])) % 16 == 0,
+                "KV cache must be 16-byte aligned");
+  }
+}
+
+}  // namespace
+
+extern "C" ltm_status ltm_model_prefill(ltm_model* m, const int32_t* tokens, int B, int S,
+                                        void* const* k_caches, void* const* v_caches,
+                                        int64_t max_positions, void* hidden_out,
+                                        void* logits_last, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(m, "NULL model");
+    m->require_ready(logits_last != nullptr);
+    LTM_REQUIRE(B >= 0 && S >= 0, "negative batch or sequence length");
+    if (B == 0 || S == 0) return;
+    LTM_REQUIRE(tokens, "NULL tokens");
+    LTM_REQUIRE(S <= max_positions, "the prompt is longer than the cache");
+    check_caches(m, k_caches, v_caches, max_positions);
+    DeviceGuard g(m->device);
+    cudaStream_t st = as_stream(stream);
+    const int64_t T = static_cast<int64_t>(B) * S;
+    const int H = m->cfg.hidden_dim;
+    m->ensure_ws(T);
+    launch_embed_gather(m->emb.ptr, m->dt(), m->vocab, H, tokens, T, m->a.ptr, st);
+    const void* cur = m->a.ptr;
+    const size_t L = m->layers.size();
+    for (size_t i = 0; i < L; ++i) {
+      void* dst = (i + 1 == L && hidden_out) ? hidden_out : (cur == m->a.ptr ? m->b.ptr : m->a.ptr);
+      m->layers[i]->forward(cur, dst, B, S, st, k_caches[i], v_caches[i], max_positions);
+      cur = dst;
+    }
+    if (logits_last) {  // the last position of every sequence
+      const char* last = static_cast<const char*>(cur) +
+                         static_cast<size_t>(S - 1) * H * dtype_size(m->dt());
+      m->lm_head(last, B, static_cast<int64_t>(S) * H, logits_last, m->vocab, st);
+    }
+  });
+}
+
+extern "C" ltm_status ltm_model_decode_step(ltm_model* m, const int32_t* tokens,
+                                            const int32_t* cache_lens, int B,
+                                            void* const* k_caches, void* const* v_caches,
+                                            int64_t max_positions, void* hidden_out,
+                                            void* logits, void* stream) {
+  return guarded([&] {
+    LTM_REQUIRE(m, "NULL model");
+    m->require_ready(logits != nullptr);
+    LTM_REQUIRE(B >= 0, "negative batch");
+    if (B == 0) return;
+    LTM_REQUIRE(tokens && cache_lens, "NULL tokens / cache_lens");
+    check_caches(m, k_caches, v_caches, max_positions);
+    DeviceGuard g(m->device);
+    cudaStream_t st = as_stream(stream);
+    const int H = m->cfg.hidden_dim;
+    m->ensure_ws(B);
+    launch_embed_gather(m->emb.ptr, m->dt(), m->vocab, H, tokens, B, m->a.ptr, st);
+    const void* cur = m->a.ptr;
+    const size_t L = m->layers.size();
+    for (size_t i = 0; i < L; ++i) {
+      void* dst = (i + 1 == L && hidden_out) ? hidden_out : (cur == m->a.ptr ? m->b.ptr : m->a.ptr);
+      m->layers[i]->decode(cur, dst, k_caches[i], v_caches[i], max_positions, 0, B, st,
+                           cache_lens);
+      cur = dst;
+    }
+    if (logits) m->lm_head(cur, B, H, logits, m->vocab, st);
   });
 }
 

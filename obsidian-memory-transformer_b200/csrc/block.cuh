@@ -2,6 +2,9 @@
 // orchestration (device buffers, quantized weights, launchers).
 #pragma once
 
+#include <string>
+#include <vector>
+
 #include "common.cuh"
 #include "epilogue.cuh"
 
@@ -17,6 +20,18 @@ namespace ltm_b200 {
 // In-stream allreduce (sum, or max) over the communicator; send == recv allowed.
 void comm_allreduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dtype dt,
                     bool max_op, cudaStream_t st);
+// All-gather of bytes_per_rank bytes from every rank into recv (rank order);
+// in place when send == recv + rank * bytes_per_rank.
+void comm_allgather_bytes(ltm_comm* c, const void* send, void* recv, size_t bytes_per_rank,
+                          cudaStream_t st);
+// Reduce-scatter (sum): rank r receives the sum of every rank's block r of
+// count_per_rank elements of send.
+void comm_reduce_scatter(ltm_comm* c, const void* send, void* recv, size_t count_per_rank,
+                         ltm_dtype dt, cudaStream_t st);
+// NCCL group brackets: the collectives between them launch as one (at the
+// end, which marks them for the kernel timer under `what` on stream st).
+void comm_group_start();
+void comm_group_end(const char* what, cudaStream_t st);
 
 // Owning device allocation (grow-only).
 struct DevBuf {
@@ -51,6 +66,30 @@ struct QLinear {
            Epilogue ep, cudaStream_t stream, DevBuf* wdq = nullptr) const;
 };
 
+// One device buffer of a block's state (a checkpoint section).
+struct StateSection {
+  std::string name;
+  void* ptr;
+  size_t bytes;
+};
+
+}  // namespace ltm_b200
+
+struct ltm_block;
+
+namespace ltm_b200 {
+
+// The device buffers of a block's weights (quantized codes, scales,
+// zero-points, biases, LayerNorm parameters) and / or its bank, in a fixed
+// order; with allocate they are sized for the block's config first (before
+// a load from a checkpoint).
+std::vector<StateSection> block_state(ltm_block* b, bool weights, bool bank, bool allocate);
+// After the sections were written: the block counts as loaded (weights) and
+// its resident K_M | V_M are recomputed at the next use.
+void block_state_loaded(ltm_block* b, bool weights);
+void block_identity(const ltm_block* b, ltm_block_config* cfg, ltm_quant_config* q, int* tp,
+                    int* tpr, int* device, bool* loaded);
+
 struct AttnParams {
   const void* q;
   const void* k;
@@ -76,9 +115,12 @@ struct MemoryWriteState {
   // sums the slot weights over the ranks when given).
   // Returns the factor that turns colsum into the state c (1 / T, and the
   // mean over the ranks under tensor parallelism).
+  // colsum_partial: each rank's column sums cover only its own rows
+  // (sequence-parallel gate), so the ranks' sums add up to the total.
   float update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm, int64_t ldq,
                     int64_t T, int H, int heads, int nh_total, int dh, int Ms, float rate,
-                    bool use_scores, ltm_dtype dt, ltm_comm* comm, cudaStream_t st);
+                    bool use_scores, ltm_dtype dt, ltm_comm* comm, cudaStream_t st,
+                    bool colsum_partial = false);
 };
 
 // The state c = state * scale as one row [H] in the activation dtype.
@@ -93,15 +135,25 @@ void launch_rows_ema(void* rows, int64_t ld, int width, const void* v, const flo
 // Decode step, head-major caches [B, width / dh, P, dh]: the new token's K | V
 // rows (columns [width, 3 width) of the fused projection rows, stride ldq) to
 // position pos of every head of its sequence.
+// pos_arr (device [B], optional): a position per sequence instead of pos;
+// positions outside [0, P) write nothing and set the device error word.
 void launch_kv_append(const void* qkv, int64_t ldq, int width, int dh, void* kc, void* vc,
-                      int64_t P, int64_t pos, int B, ltm_dtype dt, cudaStream_t st);
+                      int64_t P, int64_t pos, int B, ltm_dtype dt, cudaStream_t st,
+                      const int* pos_arr = nullptr);
+// Prefill: the K | V rows of all B * S rows (positions 0 .. S-1 of each
+// sequence) into the head-major caches.
+void launch_kv_fill(const void* qkv, int64_t ldq, int width, int dh, void* kc, void* vc, int64_t P,
+                    int B, int S, ltm_dtype dt, cudaStream_t st);
 // Self-attention of one query row per (sequence, head) over the first L of
 // the P cached positions (split into chunks, partials in `part`, then merged
 // into o).
 size_t decode_partials_bytes(int B, int nh, int D, int64_t L);
+// cache_lens (device [B], optional): sequence b attends cache_lens[b] + 1
+// positions (L is then the upper bound max_positions).
 void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const void* vc,
                              int64_t P, int L, int B, int nh, int D, ltm_dtype dt, float* part,
-                             void* o, int64_t ldo, cudaStream_t st);
+                             void* o, int64_t ldo, cudaStream_t st,
+                             const int* cache_lens = nullptr);
 
 // Slot weights of `heads` heads (rate / nh_total per head, summed into wslot;
 // qsum [heads*dh] and wslot [Ms] are cleared here) and the bank EMA.
@@ -155,6 +207,10 @@ void launch_attention(const AttnParams& p, int B, int D, bool causal, ltm_dtype 
                       cudaStream_t stream);
 void launch_attention_tc(const AttnParams& p, int B, int D, bool causal, ltm_dtype dt,
                          cudaStream_t stream);
+// Next token of each of B rows of logits (stride ld): argmax (lowest index
+// on ties); lens[b] += 1 when lens is given.
+void launch_greedy_next(const void* logits, int64_t ld, ltm_dtype dt, int B, int vocab,
+                        int32_t* tokens, int32_t* lens, cudaStream_t st);
 void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n, ltm_dtype dt,
                  cudaStream_t stream);
 void upload_f32_as(const float* host, int64_t n, ltm_dtype dt, void* dev, cudaStream_t stream);

@@ -19,12 +19,26 @@
 namespace ltm_b200 {
 namespace {
 
+// Inside ncclGroupStart / End the collectives launch at the End: the kernel
+// timer marks the group once there.
+thread_local int t_group_depth = 0;
+
+void note_collective(const char* what, cudaStream_t st) {
+  if (t_group_depth == 0) note_launch(what, st);
+}
+
 struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                                 ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   ncclResult_t (*get_version)(int*) = nullptr;
   bool ok = false;
@@ -41,9 +55,15 @@ const NcclApi& nccl() {
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.reduce_scatter =
+        reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+    api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
+    api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
     api.get_version = reinterpret_cast<decltype(api.get_version)>(dlsym(h, "ncclGetVersion"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce &&
+             api.all_gather && api.reduce_scatter && api.group_start && api.group_end &&
              api.error_string;
   });
   if (!api.ok) {
@@ -79,7 +99,38 @@ void comm_allreduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm
   nccl_check(nccl().all_reduce(send, recv, count, nccl_type(dt), max_op ? ncclMax : ncclSum,
                                static_cast<ncclComm_t>(c->handle), st),
              "ncclAllReduce");
-  note_launch(max_op ? "nccl_allreduce/max" : "nccl_allreduce/sum", st);  // timer entry of its own
+  note_collective(max_op ? "nccl_allreduce/max" : "nccl_allreduce/sum", st);
+}
+
+void comm_allgather_bytes(ltm_comm* c, const void* send, void* recv, size_t bytes_per_rank,
+                          cudaStream_t st) {
+  LTM_REQUIRE(c != nullptr, "NULL communicator");
+  if (bytes_per_rank == 0) return;
+  nccl_check(nccl().all_gather(send, recv, bytes_per_rank, ncclInt8,
+                               static_cast<ncclComm_t>(c->handle), st),
+             "ncclAllGather");
+  note_collective("nccl_allgather", st);
+}
+
+void comm_reduce_scatter(ltm_comm* c, const void* send, void* recv, size_t count_per_rank,
+                         ltm_dtype dt, cudaStream_t st) {
+  LTM_REQUIRE(c != nullptr, "NULL communicator");
+  if (count_per_rank == 0) return;
+  nccl_check(nccl().reduce_scatter(send, recv, count_per_rank, nccl_type(dt), ncclSum,
+                                   static_cast<ncclComm_t>(c->handle), st),
+             "ncclReduceScatter");
+  note_collective("nccl_reduce_scatter", st);
+}
+
+void comm_group_start() {
+  nccl_check(nccl().group_start(), "ncclGroupStart");
+  ++t_group_depth;
+}
+
+void comm_group_end(const char* what, cudaStream_t st) {
+  --t_group_depth;
+  nccl_check(nccl().group_end(), "ncclGroupEnd");
+  if (what) note_collective(what, st);
 }
 
 }  // namespace ltm_b200

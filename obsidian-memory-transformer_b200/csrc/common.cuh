@@ -35,6 +35,7 @@ enum DeviceErrorCode : int {
   kErrWaitEmpty = 2,    // producer waited too long for a free stage
   kErrWaitAccum = 3,    // epilogue waited too long for the accumulator
   kErrWaitOther = 4,
+  kErrBadCacheLen = 5,  // a per-sequence cache length outside [0, max_positions)
 };
 
 #define LTM_CUDA_TRY(expr)                                                              \

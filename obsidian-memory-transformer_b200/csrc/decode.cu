@@ -67,13 +67,24 @@ __device__ __forceinline__ void load_row_part(const T* row, int gl, float (&v)[D
 __device__ __forceinline__ int part_dim(int gl, int i) { return (i >> 3) * 64 + gl * 8 + (i & 7); }
 
 // K | V rows of the new token (columns [width, 3 width) of its fused
-// projection row) into position pos of every head of its sequence.
+// projection row) into position pos (or pos_arr[b]) of every head of its
+// sequence.  A per-sequence position outside [0, P) writes nothing and sets
+// the device error word.
 template <class T>
 __global__ void __launch_bounds__(256) kv_append_kernel(const T* __restrict__ qkv, int64_t ldq,
                                                         int width, int dh, T* __restrict__ kc,
                                                         T* __restrict__ vc, int64_t P,
-                                                        int64_t pos) {
+                                                        int64_t pos,
+                                                        const int* __restrict__ pos_arr,
+                                                        int* err) {
   const int b = blockIdx.x;
+  if (pos_arr != nullptr) {
+    pos = pos_arr[b];
+    if (pos < 0 || pos >= P) {
+      if (threadIdx.x == 0) atomicExch(err, kErrBadCacheLen);
+      return;
+    }
+  }
   const int nv = width / 8, vph = dh / 8;  // 16-byte vectors per row / per head
   const int heads = width / dh;
   const uint4* ks = reinterpret_cast<const uint4*>(qkv + b * ldq + width);
@@ -86,6 +97,34 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const T* __restrict__ qk
   }
 }
 
+// K | V rows of all T = B * S prefill rows (row t at position t % S of
+// sequence t / S) into the head-major caches: one block per row.
+template <class T>
+__global__ void __launch_bounds__(256) kv_fill_kernel(const T* __restrict__ qkv, int64_t ldq,
+                                                      int width, int dh, T* __restrict__ kc,
+                                                      T* __restrict__ vc, int64_t P, int S) {
+  const int64_t t = blockIdx.x;
+  const int64_t b = t / S, p = t - b * S;
+  const int nv = width / 8, vph = dh / 8;
+  const int heads = width / dh;
+  const uint4* ks = reinterpret_cast<const uint4*>(qkv + t * ldq + width);
+  const uint4* vs = reinterpret_cast<const uint4*>(qkv + t * ldq + 2 * static_cast<int64_t>(width));
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    const int h = i / vph, c = i - h * vph;
+    const int64_t dst = ((b * heads + h) * P + p) * dh;
+    reinterpret_cast<uint4*>(kc + dst)[c] = ks[i];
+    reinterpret_cast<uint4*>(vc + dst)[c] = vs[i];
+  }
+}
+
+// Positions attended by sequence b: L, or cache_lens[b] + 1 (0 when that
+// length is outside [0, P): the sequence was skipped by the append).
+__device__ __forceinline__ int seq_positions(const int* cache_lens, int b, int L, int P) {
+  if (cache_lens == nullptr) return L;
+  const int c = cache_lens[b];
+  return (c >= 0 && c < P) ? c + 1 : 0;
+}
+
 __device__ __forceinline__ void consumer_bar_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kDCons * 32) : "memory");
 }
@@ -94,7 +133,7 @@ template <class T, int D>
 __global__ void __launch_bounds__(32 * (kDCons + 1), 1) decode_attn_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     const T* __restrict__ q, int64_t ldq, int L, int P, int nh, int nchunk, int items, float sl2,
-    float* __restrict__ part, int* err) {
+    float* __restrict__ part, const int* __restrict__ cache_lens, int* err) {
   using S = DecSmem<D>;
   constexpr int DL = D / 8;  // dims per lane
   constexpr int NS = S::kStages;
@@ -126,8 +165,9 @@ __global__ void __launch_bounds__(32 * (kDCons + 1), 1) decode_attn_kernel(
       bool ok = true;
       for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
         const int c = w % nchunk, bh = w / nchunk;
-        const int c0 = c * kDChunk, c1 = min(L, c0 + kDChunk);
-        const int nt = (c1 - c0 + kDTile - 1) / kDTile;
+        const int Lb = seq_positions(cache_lens, bh / nh, L, P);
+        const int c0 = c * kDChunk, c1 = min(Lb, c0 + kDChunk);
+        const int nt = c1 > c0 ? (c1 - c0 + kDTile - 1) / kDTile : 0;
         for (int t = 0; t < nt; ++t, ++it) {
           const int st = it % NS;
           if (!mbar_wait_bounded(empty + st, ((it / NS) & 1) ^ 1, abort_flag, err, kErrWaitEmpty)) {
@@ -157,8 +197,9 @@ __global__ void __launch_bounds__(32 * (kDCons + 1), 1) decode_attn_kernel(
   for (int w = blockIdx.x; w < items; w += gridDim.x, parity ^= 1) {
     const int c = w % nchunk, bh = w / nchunk;
     const int h = bh % nh, b = bh / nh;
-    const int c0 = c * kDChunk, c1 = min(L, c0 + kDChunk);
-    const int nt = (c1 - c0 + kDTile - 1) / kDTile;
+    const int Lb = seq_positions(cache_lens, b, L, P);
+    const int c0 = c * kDChunk, c1 = min(Lb, c0 + kDChunk);
+    const int nt = c1 > c0 ? (c1 - c0 + kDTile - 1) / kDTile : 0;
     float qv[DL];
     load_row_part<T, DL>(q + b * ldq + h * D, gl, qv);
     float m = -INFINITY, l = 0.0f, o[DL];
@@ -298,20 +339,39 @@ size_t decode_partials_bytes(int B, int nh, int D, int64_t L) {
 }
 
 void launch_kv_append(const void* qkv, int64_t ldq, int width, int dh, void* kc, void* vc,
-                      int64_t P, int64_t pos, int B, ltm_dtype dt, cudaStream_t st) {
+                      int64_t P, int64_t pos, int B, ltm_dtype dt, cudaStream_t st,
+                      const int* pos_arr) {
   LTM_REQUIRE(dt != LTM_DTYPE_F32 && dh % 8 == 0 && width % dh == 0,
               "KV append needs 16-bit rows of whole heads");
   dispatch_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     kv_append_kernel<T><<<B, 256, 0, st>>>(static_cast<const T*>(qkv), ldq, width, dh,
-                                            static_cast<T*>(kc), static_cast<T*>(vc), P, pos);
+                                            static_cast<T*>(kc), static_cast<T*>(vc), P, pos,
+                                            pos_arr, device_error_ptr());
   });
   check_launch("kv_append_kernel", st);
 }
 
+void launch_kv_fill(const void* qkv, int64_t ldq, int width, int dh, void* kc, void* vc, int64_t P,
+                    int B, int S, ltm_dtype dt, cudaStream_t st) {
+  LTM_REQUIRE(dt != LTM_DTYPE_F32 && dh % 8 == 0 && width % dh == 0,
+              "KV fill needs 16-bit rows of whole heads");
+  LTM_REQUIRE(S <= P, "the prompt is longer than the cache");
+  const int64_t T = static_cast<int64_t>(B) * S;
+  if (T == 0) return;
+  LTM_REQUIRE(T < (1ll << 31), "too many rows");
+  dispatch_dtype(dt, [&](auto tag) {
+    using T_ = decltype(tag);
+    kv_fill_kernel<T_><<<static_cast<unsigned>(T), 256, 0, st>>>(
+        static_cast<const T_*>(qkv), ldq, width, dh, static_cast<T_*>(kc), static_cast<T_*>(vc),
+        P, S);
+  });
+  check_launch("kv_fill_kernel", st);
+}
+
 void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const void* vc,
                              int64_t P, int L, int B, int nh, int D, ltm_dtype dt, float* part,
-                             void* o, int64_t ldo, cudaStream_t st) {
+                             void* o, int64_t ldo, cudaStream_t st, const int* cache_lens) {
   LTM_REQUIRE(D == 64 || D == 128, "decode attention head_dim must be 64 or 128");
   LTM_REQUIRE(L >= 1 && L <= P, "cache length outside [1, max_positions]");
   LTM_REQUIRE(dt != LTM_DTYPE_F32, "decode attention needs 16-bit activations");
@@ -336,7 +396,7 @@ void launch_decode_attention(const void* q, int64_t ldq, const void* kc, const v
         const int grid = persistent_grid(kern, 32 * (kDCons + 1), smem, items);
         kern<<<grid, 32 * (kDCons + 1), smem, st>>>(tk, tv, static_cast<const T*>(q), ldq, L,
                                                     static_cast<int>(P), nh, nchunk, items, sl2,
-                                                    part, device_error_ptr());
+                                                    part, cache_lens, device_error_ptr());
         check_launch("decode_attn_kernel", st);
         decode_combine_kernel<T, DD><<<dim3(nh, B), DD, 0, st>>>(part, nchunk, sl2,
                                                                  static_cast<T*>(o), ldo);

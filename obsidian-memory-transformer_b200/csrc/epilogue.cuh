@@ -35,6 +35,11 @@ struct Epilogue {
   int rope_cols = 0;
   int seq_len = 1;
   int head_dim = 64;
+  // per-row positions (decode with a cache length per sequence): row m at
+  // position row_pos[m] of the table, which holds rope_rows positions (a
+  // position outside [0, rope_rows) is clamped; the launchers flag it)
+  const int* row_pos = nullptr;
+  int rope_rows = 0;
   // RESID (aux0 = R) / GATEMIX (aux0 = s, aux1 = mem, aux2 = x); all use ld_aux
   const void* aux0 = nullptr;
   const void* aux1 = nullptr;
@@ -43,6 +48,15 @@ struct Epilogue {
   // GATEMIX: optional column sums of g*x over the rows (memory write), fp32 [N]
   float* colsum = nullptr;
 };
+
+// RoPE table row of output row m.
+__device__ __forceinline__ int rope_row(const Epilogue& ep, int64_t m, bool row_ok) {
+  if (ep.row_pos != nullptr) {
+    const int p = row_ok ? __ldg(ep.row_pos + m) : 0;
+    return min(max(p, 0), ep.rope_rows - 1);
+  }
+  return static_cast<int>(static_cast<uint32_t>(m) % static_cast<uint32_t>(ep.seq_len));
+}
 
 // Sum over the warp's 32 rows of v[c]; lane c receives column c (31 shuffles,
 // recursive halving).  Must be called by all 32 lanes.
@@ -138,7 +152,7 @@ __device__ __forceinline__ void epilogue_math32(const Epilogue& ep, int64_t m, i
       if (n0 < ep.rope_cols) {
         // a 32-column chunk never crosses a head (head_dim is a multiple of 32)
         const int half = ep.head_dim >> 1;
-        const int pos = static_cast<int>(static_cast<uint32_t>(m) % static_cast<uint32_t>(ep.seq_len));
+        const int pos = rope_row(ep, m, true);
         const int d0 = static_cast<int>(static_cast<uint32_t>(n0) % static_cast<uint32_t>(ep.head_dim));
         const float2* tab = ep.rope + static_cast<int64_t>(pos) * half + (d0 >> 1);
 #pragma unroll
@@ -461,8 +475,7 @@ struct TmaTileEpilogue {
     }
     const bool row_ok = m < M;
     int pos = 0;
-    if constexpr (MODE == kEpiRope)
-      pos = static_cast<int>(static_cast<uint32_t>(m) % static_cast<uint32_t>(ep.seq_len));
+    if constexpr (MODE == kEpiRope) pos = rope_row(ep, m, row_ok);
 
     using Aux = EpiChunkAux<MODE, OutT>;
     constexpr int kAuxSets = Aux::kAhead ? 2 : 1;

@@ -338,7 +338,7 @@ void validate_memory_store(const void* memory, const void* keys, int64_t ldk, co
 float MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, const void* qm,
                                     int64_t ldq, int64_t T, int H, int heads, int nh_total, int dh,
                                     int Ms, float rate, bool use_scores, ltm_dtype dt,
-                                    ltm_comm* comm, cudaStream_t st) {
+                                    ltm_comm* comm, cudaStream_t st, bool colsum_partial) {
   if (T == 0 || Ms == 0) return 0.0f;
   const int Hq = heads * dh;
   if (use_scores) {
@@ -352,11 +352,12 @@ float MemoryWriteState::update_bank(void* memory, const void* kvm, int64_t ldk, 
   }
   float state_scale = 1.0f / static_cast<float>(T);
   if (comm && comm->nranks > 1) {
-    // Every rank accumulated the same column sums (replicated gate), in its
-    // own atomic order; their mean makes the state, and so the bank, identical
-    // on all ranks.
+    // Replicated gate: every rank accumulated the same column sums, in its
+    // own atomic order, and their mean makes the state -- and so the bank --
+    // identical on all ranks.  Sequence-parallel gate: each rank summed its
+    // own rows, and the sum over the ranks is the total.
     comm_allreduce(comm, colsum.ptr, colsum.ptr, H, LTM_DTYPE_F32, false, st);
-    state_scale /= static_cast<float>(comm->nranks);
+    if (!colsum_partial) state_scale /= static_cast<float>(comm->nranks);
   }
   launch_bank_update(memory, colsum.as<float>(), state_scale,
                      use_scores ? wslot.as<float>() : nullptr, rate, Ms, H, dt, st);

@@ -107,6 +107,26 @@ def _declare(L):
         "ltm_model_load_embedding": ([vp, vp], ci),
         "ltm_model_load_layer": ([vp, ci, C.POINTER(BlockWeightsC)], ci),
         "ltm_model_forward": ([vp, vp, vp, ci, ci, vp], ci),
+        "ltm_model_load_lm_head": ([vp, vp], ci),
+        "ltm_model_lm_head": ([vp, vp, i64, i64, vp, vp], ci),
+        "ltm_model_prefill": ([vp, vp, ci, ci, C.POINTER(vp), C.POINTER(vp), i64, vp, vp, vp], ci),
+        "ltm_model_decode_step": ([vp, vp, vp, ci, C.POINTER(vp), C.POINTER(vp), i64, vp, vp,
+                                   vp], ci),
+        "ltm_greedy_next_tokens": ([vp, ci, ci, ci, vp, vp, vp], ci),
+        "ltm_block_forward_with_cache": ([vp, vp, vp, ci, ci, vp, vp, i64, vp], ci),
+        "ltm_block_forward_sp": ([vp, vp, vp, ci, ci, vp], ci),
+        "ltm_calibrator_create": ([ci, C.c_float, ci, C.POINTER(vp)], ci),
+        "ltm_calibrator_collect": ([vp, vp, ci, i64, vp], ci),
+        "ltm_calibrator_compute_range": ([vp, C.POINTER(C.c_float), C.POINTER(C.c_float), vp],
+                                         ci),
+        "ltm_calibrator_reset": ([vp], ci),
+        "ltm_calibrator_destroy": ([vp], ci),
+        "ltm_quantize_int8_static": ([vp, ci, i64, C.c_float, vp, vp], ci),
+        "ltm_block_save": ([vp, C.c_char_p], ci),
+        "ltm_block_load": ([vp, C.c_char_p], ci),
+        "ltm_block_save_memory": ([vp, C.c_char_p], ci),
+        "ltm_block_load_memory": ([vp, C.c_char_p], ci),
+        "ltm_block_decode_step_ragged": ([vp, vp, vp, vp, vp, i64, vp, ci, vp], ci),
         "ltm_model_destroy": ([vp], ci),
         "ltm_comm_unique_id": ([vp], ci),
         "ltm_comm_create": ([vp, ci, ci, ci, C.POINTER(vp)], ci),
@@ -161,6 +181,60 @@ def device_alloc_count() -> int:
     n = C.c_uint64(0)
     _check(lib().ltm_device_alloc_count(C.byref(n)))
     return n.value
+
+
+CALIB_MINMAX, CALIB_PERCENTILE, CALIB_MSE = 0, 1, 2
+
+
+class Calibrator:
+    """Activation-range calibrator on the device (MinMaxCalibrator /
+    PercentileCalibrator / MSECalibrator of the reference's quantizer):
+    collect() CUDA tensors, then compute_range() -> (min, max); the static
+    symmetric INT8 scale is max(|min|, |max|) / 127 (static_scale())."""
+
+    def __init__(self, method: int = CALIB_MINMAX, percentile: float = 99.9, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().ltm_calibrator_create(method, percentile, device, C.byref(h)))
+        self._h = h
+
+    def collect(self, x, stream=None) -> None:
+        _need_cuda(x)
+        _check(lib().ltm_calibrator_collect(self._h, _ptr(x), dtype_code(x.dtype), x.numel(),
+                                            _stream(stream)))
+
+    def compute_range(self, stream=None):
+        lo, hi = C.c_float(), C.c_float()
+        _check(lib().ltm_calibrator_compute_range(self._h, C.byref(lo), C.byref(hi),
+                                                  _stream(stream)))
+        return lo.value, hi.value
+
+    def static_scale(self, stream=None) -> float:
+        lo, hi = self.compute_range(stream)
+        return float(np.float32(max(abs(lo), abs(hi))) / np.float32(127.0))
+
+    def reset(self) -> None:
+        _check(lib().ltm_calibrator_reset(self._h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().ltm_calibrator_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def quantize_int8_static(x, scale: float, stream=None):
+    """Per-tensor INT8 with a calibrated scale: clamp(round(x / scale), -127, 127)."""
+    torch = _torch()
+    _need_cuda(x)
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    _check(lib().ltm_quantize_int8_static(_ptr(x), dtype_code(x.dtype), x.numel(), scale, _ptr(q),
+                                          _stream(stream)))
+    return q
 
 
 class KernelTimer:
@@ -529,16 +603,49 @@ class TitanBlock:
         _check(lib().ltm_block_load_weights(self._h, C.byref(st)))
         del keep
 
-    def forward(self, x, attention_mask=None, stream=None, out=None):
+    def forward(self, x, attention_mask=None, stream=None, out=None, k_cache=None,
+                v_cache=None):
         """x: CUDA tensor [B,S,H] in the act dtype -> y of the same shape
-        (written into `out` when given; it must not alias x)."""
+        (written into `out` when given; it must not alias x).  With k_cache /
+        v_cache ([B, heads, max_positions, head_dim]) the post-RoPE keys and
+        values of positions [0, S) are written there as well, so decode steps
+        can follow at cache_len = S."""
         torch = _torch()
-        _need_cuda(x, out)
+        _need_cuda(x, out, k_cache, v_cache)
         B, S, H = x.shape
         y = torch.empty_like(x) if out is None else out
-        _check(lib().ltm_block_forward(self._h, _ptr(x), _ptr(y), _ptr(attention_mask), B, S,
-                                       _stream(stream)))
+        if k_cache is None and v_cache is None:
+            _check(lib().ltm_block_forward(self._h, _ptr(x), _ptr(y), _ptr(attention_mask), B, S,
+                                           _stream(stream)))
+            return y
+        if attention_mask is not None:
+            raise LtmError(ERR_UNSUPPORTED, "explicit attention masks (self-attention is causal)")
+        self._check_caches(k_cache, v_cache, B)
+        _check(lib().ltm_block_forward_with_cache(self._h, _ptr(x), _ptr(y), B, S, _ptr(k_cache),
+                                                  _ptr(v_cache), k_cache.shape[2],
+                                                  _stream(stream)))
         return y
+
+    def forward_sp(self, x_local, B: int, S: int, out=None, stream=None):
+        """Sequence-parallel forward of a tensor-parallel block: x_local is
+        this rank's [B*S / nranks, H] rows of the [B*S, H] activations; the
+        result is this rank's rows of the block output."""
+        torch = _torch()
+        _need_cuda(x_local, out)
+        y = torch.empty_like(x_local) if out is None else out
+        _check(lib().ltm_block_forward_sp(self._h, _ptr(x_local), _ptr(y), B, S,
+                                          _stream(stream)))
+        return y
+
+    def _check_caches(self, k_cache, v_cache, B):
+        heads = self.config.num_heads // (self._comm.nranks if self._comm is not None else 1)
+        if (k_cache is None or v_cache is None or k_cache.shape != v_cache.shape
+                or k_cache.dim() != 4 or k_cache.shape[0] != B or k_cache.shape[1] != heads
+                or k_cache.shape[3] != self.config.head_dim):
+            raise LtmError(ERR_INVALID_ARG,
+                           "k_cache / v_cache must both be [B, heads, max_positions, head_dim]")
+        if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+            raise LtmError(ERR_INVALID_ARG, "the caches must be contiguous")
 
     __call__ = forward
 
@@ -563,6 +670,21 @@ class TitanBlock:
                                            k_cache.shape[2], int(cache_len), B, _stream(stream)))
         return y
 
+    def decode_step_ragged(self, x, k_cache, v_cache, cache_lens, stream=None, out=None):
+        """One decode step with a cache length per sequence: x [B, H], the
+        new token of sequence b at position cache_lens[b] (CUDA int32 [B])."""
+        torch = _torch()
+        _need_cuda(x, k_cache, v_cache, cache_lens, out)
+        B = x.shape[0]
+        self._check_caches(k_cache, v_cache, B)
+        if cache_lens.dtype != torch.int32 or cache_lens.numel() != B or not x.is_contiguous():
+            raise LtmError(ERR_INVALID_ARG, "cache_lens must be int32 [B]; x contiguous")
+        y = torch.empty_like(x) if out is None else out
+        _check(lib().ltm_block_decode_step_ragged(self._h, _ptr(x), _ptr(y), _ptr(k_cache),
+                                                  _ptr(v_cache), k_cache.shape[2],
+                                                  _ptr(cache_lens), B, _stream(stream)))
+        return y
+
     def memory_write(self, state, queries=None, stream=None) -> None:
         """Memory write of the block's bank towards `state` (fp32 [H]) with
         slot weights from the mean of the memory-query rows `queries` [T, Hl]
@@ -579,6 +701,21 @@ class TitanBlock:
                           dtype=torch_dtype(self.quant.act_dtype), device=f"cuda:{self.device}")
         _check(lib().ltm_block_get_memory(self._h, _ptr(out), _stream(stream)))
         return out
+
+    def save(self, path) -> None:
+        """Quantized checkpoint of the block (codes, scales, biases, LN, bank)."""
+        _check(lib().ltm_block_save(self._h, str(path).encode()))
+
+    def load(self, path) -> None:
+        """Restores a checkpoint written by save() (same dimensions, scheme,
+        dtype and tensor-parallel rank); the block is then ready to run."""
+        _check(lib().ltm_block_load(self._h, str(path).encode()))
+
+    def save_memory(self, path) -> None:
+        _check(lib().ltm_block_save_memory(self._h, str(path).encode()))
+
+    def load_memory(self, path) -> None:
+        _check(lib().ltm_block_load_memory(self._h, str(path).encode()))
 
     def intermediate(self, name: str, stream=None):
         """A copy of one intermediate of the last forward / decode step
@@ -698,6 +835,134 @@ class TitanModel:
         return out
 
     __call__ = forward
+
+    # ------------------------------------------------------- LM head, decode --
+    def load_lm_head(self, weight: np.ndarray) -> None:
+        """TitanForCausalLM.lm_head: host fp32 [vocab, H], no bias."""
+        w = np.ascontiguousarray(weight, dtype=np.float32)
+        if w.shape != (self.vocab, self.config.hidden_dim):
+            raise LtmError(ERR_INVALID_ARG, "LM head weight must be [vocab, hidden]")
+        _check(lib().ltm_model_load_lm_head(self._h, C.c_void_p(w.ctypes.data)))
+
+    def lm_head(self, hidden, out=None, stream=None):
+        """logits [..., vocab] of hidden rows [..., H] (the last dim contiguous;
+        rows may be strided, e.g. hidden[:, -1, :])."""
+        torch = _torch()
+        _need_cuda(out)
+        if not hidden.is_cuda:
+            raise ValueError("ltm_b200 operates on CUDA tensors only")
+        H = self.config.hidden_dim
+        rows = hidden.reshape(-1, H) if hidden.is_contiguous() else hidden
+        if rows.dim() != 2 or rows.stride(1) != 1:
+            raise LtmError(ERR_INVALID_ARG, "hidden rows must be a 2-D view with unit column stride")
+        R = rows.shape[0]
+        if out is None:
+            out = torch.empty((R, self.vocab), dtype=torch_dtype(self.quant.act_dtype),
+                              device=hidden.device)
+        _check(lib().ltm_model_lm_head(self._h, _ptr(rows), R, rows.stride(0), _ptr(out),
+                                       _stream(stream)))
+        return out.reshape(*hidden.shape[:-1], self.vocab) if hidden.is_contiguous() else out
+
+    def make_cache(self, batch_size: int, max_positions: int) -> "CacheManager":
+        cache = CacheManager(self.n_layers, self.config.num_heads, self.config.head_dim,
+                             torch_dtype(self.quant.act_dtype), device=self.device)
+        cache.allocate(batch_size, max_positions)
+        return cache
+
+    @staticmethod
+    def _cache_ptrs(cache: "CacheManager"):
+        n = len(cache._k)
+        ks = (C.c_void_p * n)(*[t.data_ptr() for t in cache._k])
+        vs = (C.c_void_p * n)(*[t.data_ptr() for t in cache._v])
+        return ks, vs
+
+    def prefill(self, tokens, cache: "CacheManager", hidden_out=None, logits=True, stream=None):
+        """Prompts tokens (CUDA int32 [B,S]) through the model, filling every
+        layer's cache at positions [0, S); returns (hidden [B,S,H] or None,
+        logits of each sequence's last position [B, vocab] or None)."""
+        torch = _torch()
+        _need_cuda(tokens, hidden_out)
+        B, S = tokens.shape
+        lg = (torch.empty((B, self.vocab), dtype=torch_dtype(self.quant.act_dtype),
+                          device=tokens.device) if logits else None)
+        ks, vs = self._cache_ptrs(cache)
+        _check(lib().ltm_model_prefill(self._h, _ptr(tokens), B, S, ks, vs, cache.max_positions,
+                                       _ptr(hidden_out), _ptr(lg), _stream(stream)))
+        cache.length = S
+        return hidden_out, lg
+
+    def decode_step(self, tokens, cache_lens, cache: "CacheManager", logits=None, hidden_out=None,
+                    stream=None):
+        """One decode step: tokens (CUDA int32 [B]) at positions cache_lens
+        (CUDA int32 [B]); returns the logits [B, vocab] (written into `logits`
+        when given)."""
+        torch = _torch()
+        _need_cuda(tokens, cache_lens, logits, hidden_out)
+        B = tokens.shape[0]
+        if logits is None:
+            logits = torch.empty((B, self.vocab), dtype=torch_dtype(self.quant.act_dtype),
+                                 device=tokens.device)
+        ks, vs = self._cache_ptrs(cache)
+        _check(lib().ltm_model_decode_step(self._h, _ptr(tokens), _ptr(cache_lens), B, ks, vs,
+                                           cache.max_positions, _ptr(hidden_out), _ptr(logits),
+                                           _stream(stream)))
+        return logits
+
+    def greedy_next(self, logits, tokens_out, cache_lens=None, stream=None):
+        """tokens_out[b] = argmax logits[b] (device); cache_lens += 1 when given."""
+        _need_cuda(logits, tokens_out, cache_lens)
+        _check(lib().ltm_greedy_next_tokens(_ptr(logits), dtype_code(logits.dtype),
+                                            logits.shape[0], logits.shape[1], _ptr(tokens_out),
+                                            _ptr(cache_lens), _stream(stream)))
+
+    def generate_greedy(self, prompt, new_tokens: int, max_positions: int | None = None,
+                        use_graph: bool = True, hidden_trace: bool = False):
+        """Greedy generation of `new_tokens` tokens after the prompts (CUDA
+        int32 [B,S]): a prefill that fills the caches, then one decode step
+        per token on the device (captured once in a CUDA graph and replayed
+        when use_graph).  Returns the generated tokens [B, new_tokens] and,
+        with hidden_trace, the last layer's hidden state of every step
+        [new_tokens, B, H]."""
+        torch = _torch()
+        B, S = prompt.shape
+        P = max_positions or S + new_tokens
+        cache = self.make_cache(B, P)
+        dev = prompt.device
+        _, logits = self.prefill(prompt, cache)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
+        lens = torch.full((B,), S, dtype=torch.int32, device=dev)
+        out = torch.empty((B, new_tokens), dtype=torch.int32, device=dev)
+        hid = torch.empty((B, self.config.hidden_dim), dtype=torch_dtype(self.quant.act_dtype),
+                          device=dev)
+        trace = [] if hidden_trace else None
+        if new_tokens == 0:
+            return out, trace
+        self.greedy_next(logits, tok)  # first generated token from the prompt's last logits
+        out[:, 0] = tok
+        step_logits = torch.empty((B, self.vocab), dtype=logits.dtype, device=dev)
+
+        def step():
+            self.decode_step(tok, lens, cache, logits=step_logits, hidden_out=hid)
+            self.greedy_next(step_logits, tok, lens)
+
+        graph = None
+        for i in range(1, new_tokens):
+            if use_graph and graph is None and i >= 2:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+                    step()
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
+            out[:, i] = tok
+            if hidden_trace:
+                trace.append(hid.clone())
+        if hidden_trace:
+            # the step of the last generated token's hidden state
+            self.decode_step(tok, lens, cache, logits=step_logits, hidden_out=hid)
+            trace.append(hid.clone())
+        return out, trace
 
     def close(self) -> None:
         if getattr(self, "_h", None):

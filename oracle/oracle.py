@@ -71,6 +71,11 @@ def _declare(L):
         "orc_attention": ([f, i64, f, f, i64, ci, ci, ci, ci, ci, ci, ci, ci, f, i64], None),
         "orc_memory_store": ([f, f, i64, f, i64, i64, f, ci, ci, ci, C.c_float, ci, ci], None),
         "orc_activation": ([f, i64, ci, f], None),
+        "orc_calib_minmax": ([f, i64, f, f], None),
+        "orc_calib_percentile": ([f, i64, C.c_float, f, f], None),
+        "orc_calib_mse_error": ([f, i64, C.c_float], C.c_double),
+        "orc_calib_mse": ([f, i64, f, f], None),
+        "orc_quant_int8_static": ([f, i64, C.c_float, i8], None),
         "orc_ema_rows": ([f, ci, i64, f, f, ci], None),
         "orc_block_forward": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci], ci),
         "orc_block_forward_kv": ([_p(OrcBlockCfg), _p(OrcBlockWeights), f, f, f, ci, ci, f], ci),
@@ -221,6 +226,33 @@ def attention(q, k, v, B, Sq, Skv, nh, dh, causal, dtype, kv_shared=False):
     lib().orc_attention(_ptr(q), q.shape[1], _ptr(k), _ptr(v), k.shape[1], B, Sq, Skv,
                         0 if kv_shared else Skv, nh, dh, int(causal), dtype, _ptr(out), nh * dh)
     return out
+
+
+def calibrate(x, method: str, percentile: float = 99.9):
+    """(min, max) of the MinMax / Percentile / MSE calibrators over x."""
+    x = _f32(x).reshape(-1)
+    lo, hi = C.c_float(), C.c_float()
+    if method == "minmax":
+        lib().orc_calib_minmax(_ptr(x), x.size, C.byref(lo), C.byref(hi))
+    elif method == "percentile":
+        lib().orc_calib_percentile(_ptr(x), x.size, percentile, C.byref(lo), C.byref(hi))
+    elif method == "mse":
+        lib().orc_calib_mse(_ptr(x), x.size, C.byref(lo), C.byref(hi))
+    else:
+        raise ValueError(method)
+    return lo.value, hi.value
+
+
+def calib_mse_error(x, clip: float) -> float:
+    x = _f32(x).reshape(-1)
+    return float(lib().orc_calib_mse_error(_ptr(x), x.size, clip))
+
+
+def quant_int8_static(x, scale: float):
+    x = _f32(x)
+    q = np.empty(x.shape, np.int8)
+    lib().orc_quant_int8_static(_ptr(x), x.size, scale, _ptr(q, C.c_int8))
+    return q
 
 
 def activation(x, act: int):

@@ -393,6 +393,72 @@ void ema_rows(float* rows, int Ms, int64_t n, const float* v, const std::vector<
 
 }  // namespace
 
+// ---- calibrators (src/core/quantization/calibrator.cu:61-264; the MSE
+// search restated as 100 clipping trials of the symmetric INT8 form)
+extern "C" void orc_calib_minmax(const float* x, int64_t n, float* mn, float* mx) {
+  float lo = INFINITY, hi = -INFINITY;
+  for (int64_t i = 0; i < n; ++i) {
+    lo = std::min(lo, x[i]);
+    hi = std::max(hi, x[i]);
+  }
+  *mn = n ? lo : 0.0f;
+  *mx = n ? hi : 0.0f;
+}
+
+extern "C" void orc_calib_percentile(const float* x, int64_t n, float p, float* lo, float* hi) {
+  if (n == 0) {
+    *lo = *hi = 0.0f;
+    return;
+  }
+  std::vector<float> v(x, x + n);
+  std::sort(v.begin(), v.end());
+  // calibrator.cu:136-141, fp32 index arithmetic; the upper index clamped
+  int64_t a = static_cast<int64_t>((100.0f - p) * static_cast<float>(n) / 100.0f);
+  int64_t b = static_cast<int64_t>(p * static_cast<float>(n) / 100.0f);
+  a = std::min<int64_t>(std::max<int64_t>(a, 0), n - 1);
+  b = std::min<int64_t>(std::max<int64_t>(b, 0), n - 1);
+  *lo = v[a];
+  *hi = v[b];
+}
+
+// squared error of the symmetric INT8 quantize-dequantize at clipping `clip`
+extern "C" double orc_calib_mse_error(const float* x, int64_t n, float clip) {
+  const float s = clip / 127.0f;
+  if (!(s > 0.0f)) return 0.0;
+  double acc = 0.0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float q = std::min(std::max(roundf(x[i] / s), -127.0f), 127.0f);
+    const float d = x[i] - q * s;
+    acc += static_cast<double>(d) * d;
+  }
+  return acc;
+}
+
+extern "C" void orc_calib_mse(const float* x, int64_t n, float* lo, float* hi) {
+  if (n == 0) {
+    *lo = *hi = 0.0f;
+    return;
+  }
+  float amax = 0.0f;
+  for (int64_t i = 0; i < n; ++i) amax = std::max(amax, std::fabs(x[i]));
+  int best = 0;
+  double best_err = 0.0;
+  for (int t = 0; t < 100; ++t) {
+    const double e = orc_calib_mse_error(x, n, amax * static_cast<float>(t + 1) / 100.0f);
+    if (t == 0 || e < best_err) {
+      best = t;
+      best_err = e;
+    }
+  }
+  const float clip = amax * static_cast<float>(best + 1) / 100.0f;
+  *lo = -clip;
+  *hi = clip;
+}
+
+extern "C" void orc_quant_int8_static(const float* x, int64_t n, float scale, int8_t* q) {
+  for (int64_t i = 0; i < n; ++i) q[i] = quant_sym(x[i], scale);
+}
+
 extern "C" void orc_activation(const float* x, int64_t n, int act, float* y) {
   // the epilogue activations: GELU-tanh (src/core/ops/fused_ops.cu:136-142), sigmoid
   for (int64_t i = 0; i < n; ++i) y[i] = act_fn(x[i], act);

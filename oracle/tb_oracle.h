@@ -69,6 +69,14 @@ void orc_attention(const float* q, int64_t ldq, const float* k, const float* v, 
 /* memory-bank store: slot weights from the mean query row against the keys
  * (use_scores) or update_rate; memory[s,:] = (1-w_s) memory[s,:] + w_s state,
  * rounded to dtype.  keys rows of stride ldk, queries [T, ldq], state [H]. */
+// calibrators: data range (MinMax), the reference's percentile order
+// statistics, the least-squared-error symmetric INT8 clipping of 100 trials
+void orc_calib_minmax(const float* x, int64_t n, float* mn, float* mx);
+void orc_calib_percentile(const float* x, int64_t n, float p, float* lo, float* hi);
+double orc_calib_mse_error(const float* x, int64_t n, float clip);
+void orc_calib_mse(const float* x, int64_t n, float* lo, float* hi);
+// static per-tensor INT8 with a given scale
+void orc_quant_int8_static(const float* x, int64_t n, float scale, int8_t* q);
 // y = act(x) elementwise (ORC_ACT_GELU: tanh form; ORC_ACT_SIGMOID)
 void orc_activation(const float* x, int64_t n, int act, float* y);
 // rows[s, :] = (1 - w[s]) rows[s, :] + w[s] v, rounded to dtype (rows [Ms, n])

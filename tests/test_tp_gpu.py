@@ -1,8 +1,10 @@
-"""Tensor-parallel Titan block on 2 GPUs (one process per GPU, NCCL through the
-library's communicator) against the TB-v1 oracle and the single-GPU block:
-every rank returns the same full output, the memory bank after the write is
-the same on every rank, and both match the oracle within the dtype tolerance.
-Skipped on a machine with fewer than two GPUs."""
+"""Tensor-parallel Titan block on 2, 4 and 8 GPUs (one process per GPU, NCCL
+through the library's communicator) against the TB-v1 oracle and the
+single-GPU block: every rank returns the same full output, the memory bank
+after the write is the same on every rank, and both match the oracle within
+the dtype tolerance.  The sequence-parallel forward (each rank holds its
+rows of the activations) is checked the same way on its gathered rows.
+Each case is skipped on a machine with fewer GPUs than it needs."""
 import os
 import sys
 from pathlib import Path
@@ -18,8 +20,10 @@ ROOT = Path(__file__).resolve().parents[1]
 TOL = {"f16": (2e-2, 1e-2), "bf16": (2e-2, 1e-2)}
 
 
-def _case(scheme, dt, memory_write):
-    H, nh, F, Ms, B, S = 512, 8, 1024, 128, 2, 96
+def _case(scheme, dt, memory_write, n=2):
+    # per-rank widths stay multiples of 32 (W8A8) / 128 (W4A16) up to 8 ranks
+    H = 1024 if (scheme == "w4a16" and n > 4) else 512
+    nh, F, Ms, B, S = 8, 1024, 128, 2, 96
     return dict(H=H, nh=nh, F=F, Ms=Ms, B=B, S=S, scheme=scheme, dt=dt,
                 memory_write=memory_write, seed=11)
 
@@ -33,7 +37,7 @@ def _build(ltm, c, comm=None):
     return cfg, q, sch
 
 
-def _worker(rank, n, uid, c, out):
+def _worker(rank, n, uid, c, out, sp=False):
     sys.path[:0] = [str(ROOT), str(ROOT / "obsidian-memory-transformer_b200")]
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
@@ -45,10 +49,17 @@ def _worker(rank, n, uid, c, out):
         cfg, q, _ = _build(ltm, c, comm)
         blk = ltm.TitanBlock(cfg, q, comm=comm)
         blk.load_weights(synthetic.block_weights(c["H"], c["F"], c["Ms"], c["seed"]))
-        x = synthetic.activations(c["B"] * c["S"], c["H"], c["seed"] + 1)
-        xd = to_device(x, c["dt"]).reshape(c["B"], c["S"], c["H"])
-        y1 = blk(xd)
-        y2 = blk(xd)  # reads the bank the first forward wrote (when enabled)
+        B, S, H = c["B"], c["S"], c["H"]
+        x = synthetic.activations(B * S, H, c["seed"] + 1)
+        xd = to_device(x, c["dt"])
+        if sp:  # this rank's rows only; the parent gathers the slices
+            Tr = B * S // n
+            xl = xd[rank * Tr:(rank + 1) * Tr].contiguous()
+            y1 = blk.forward_sp(xl, B, S)
+            y2 = blk.forward_sp(xl, B, S)
+        else:
+            y1 = blk(xd.reshape(B, S, H))
+            y2 = blk(xd.reshape(B, S, H))  # reads the bank the first forward wrote (when enabled)
         torch.cuda.synchronize()
         out.put((rank, as_f32(y1), as_f32(y2), as_f32(blk.memory()), ltm.device_error()))
         blk.close()
@@ -57,13 +68,13 @@ def _worker(rank, n, uid, c, out):
         out.put((rank, repr(e), None, None, -1))
 
 
-def _run_tp(c, n=2):
+def _run_tp(c, n=2, sp=False):
     import torch.multiprocessing as mp
     import ltm_b200 as ltm
     uid = ltm.comm_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, n, uid, c, q)) for r in range(n)]
+    procs = [ctx.Process(target=_worker, args=(r, n, uid, c, q, sp)) for r in range(n)]
     for p in procs:
         p.start()
     try:
@@ -81,19 +92,28 @@ def _run_tp(c, n=2):
     return res
 
 
+@pytest.mark.parametrize("n", [2, 4, 8])
+@pytest.mark.parametrize("sp", [False, True])
 @pytest.mark.parametrize("scheme,dt,memory_write",
                          [("w8a8", "f16", True), ("w8a8", "bf16", False), ("w4a16", "bf16", True)])
-def test_tp2_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_write):
+def test_tp_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_write, sp, n):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
     from ltm_b200 import synthetic
-    c = _case(scheme, dt, memory_write)
-    res = _run_tp(c)
-    y1, y2, mem = res[0]
-    for r in res:  # the allreduce gives every rank the same result
-        assert np.array_equal(res[r][0], y1) and np.array_equal(res[r][1], y2)
-        assert np.array_equal(res[r][2], mem)
+    c = _case(scheme, dt, memory_write, n)
+    res = _run_tp(c, n, sp)
+    if sp:  # gather the row slices into the full outputs
+        y1 = np.concatenate([res[r][0] for r in range(n)]).reshape(c["B"], c["S"], c["H"])
+        y2 = np.concatenate([res[r][1] for r in range(n)]).reshape(c["B"], c["S"], c["H"])
+        mem = res[0][2]
+        for r in res:  # the bank update is identical on every rank
+            assert np.array_equal(res[r][2], mem)
+    else:
+        y1, y2, mem = res[0]
+        for r in res:  # the allreduce gives every rank the same result
+            assert np.array_equal(res[r][0], y1) and np.array_equal(res[r][1], y2)
+            assert np.array_equal(res[r][2], mem)
     # single-GPU block and the oracle on the same inputs
     cfg, qc, sch = _build(ltm, c)
     w = synthetic.block_weights(c["H"], c["F"], c["Ms"], c["seed"])
@@ -107,12 +127,13 @@ def test_tp2_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_wr
                 update_rate=cfg.memory_update_rate, use_rotary=1, use_bias=1, use_layer_norm=1,
                 use_memory_gating=1)
     ref, mem_ref = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S)
-    assert_close(y1.reshape(ref.shape), ref, *TOL[dt], what=f"tp2 {scheme} {dt} vs oracle")
-    assert_close(y1, s1, *TOL[dt], what="tp2 vs single GPU")
+    what = f"tp{n}{' sp' if sp else ''} {scheme} {dt}"
+    assert_close(y1.reshape(ref.shape), ref, *TOL[dt], what=f"{what} vs oracle")
+    assert_close(y1, s1, *TOL[dt], what=f"{what} vs single GPU")
     if memory_write:
-        assert_close(mem, mem_ref, 2e-3, 1e-2, what="tp2 bank after write")
+        assert_close(mem, mem_ref, 2e-3, 1e-2, what=f"{what} bank after write")
         ref2, _ = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S, memory=mem_ref)
-        assert_close(y2.reshape(ref2.shape), ref2, *TOL[dt], what="tp2 second forward")
+        assert_close(y2.reshape(ref2.shape), ref2, *TOL[dt], what=f"{what} second forward")
     blk.close()
 
 
@@ -142,17 +163,18 @@ def _decode_worker(rank, n, uid, c, caches, xs, L0, out):
         out.put((rank, repr(e), None, -1))
 
 
+@pytest.mark.parametrize("n", [2, 8])
 @pytest.mark.parametrize("scheme,dt", [("w4a16", "bf16"), ("w8a8", "f16")])
-def test_tp2_decode_matches_oracle(ltm, orc, scheme, dt):
+def test_tp_decode_matches_oracle(ltm, orc, scheme, dt, n):
     """Tensor-parallel decode steps with the memory write: each rank holds its
     heads of the KV cache; every rank returns the same output, equal to the
     oracle's decode steps within the dtype tolerance."""
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
     from ltm_b200 import synthetic
-    c = _case(scheme, dt, True)
+    c = _case(scheme, dt, True, n)
     H, nh, B, L0, P, steps = c["H"], c["nh"], 3, 40, 48, 3
     dh = H // nh
     rng = np.random.default_rng(5)
@@ -161,8 +183,8 @@ def test_tp2_decode_matches_oracle(ltm, orc, scheme, dt):
     uid = ltm.comm_unique_id()
     ctx = mp.get_context("spawn")
     qu = ctx.Queue()
-    procs = [ctx.Process(target=_decode_worker, args=(r, 2, uid, c, caches, xs, L0, qu))
-             for r in range(2)]
+    procs = [ctx.Process(target=_decode_worker, args=(r, n, uid, c, caches, xs, L0, qu))
+             for r in range(n)]
     for p in procs:
         p.start()
     try:
@@ -178,7 +200,8 @@ def test_tp2_decode_matches_oracle(ltm, orc, scheme, dt):
             if p.is_alive():
                 p.kill()
     for i in range(steps):
-        assert np.array_equal(res[0][0][i], res[1][0][i])
+        for r in range(1, n):
+            assert np.array_equal(res[0][0][i], res[r][0][i])
     cfg, _, sch = _build(ltm, c)
     ocfg = dict(H=H, F=c["F"], nh=nh, dh=dh, Ms=c["Ms"], scheme=sch, dtype=orc_dtype(dt),
                 memory_write=1, use_attention_scores=1, update_rate=cfg.memory_update_rate,
@@ -189,5 +212,5 @@ def test_tp2_decode_matches_oracle(ltm, orc, scheme, dt):
     kh, vh = caches[0].copy(), caches[1].copy()
     for i, x in enumerate(xs):
         ref = orc.block_decode_step(ocfg, w, x, kh, vh, L0 + i, mem, kvm)
-        assert_close(res[0][0][i], ref, *TOL[dt], what=f"tp2 decode step {i}")
-    assert_close(res[0][1], mem, 2e-3, 1e-2, what="tp2 bank after the decode writes")
+        assert_close(res[0][0][i], ref, *TOL[dt], what=f"tp{n} decode step {i}")
+    assert_close(res[0][1], mem, 2e-3, 1e-2, what=f"tp{n} bank after the decode writes")
