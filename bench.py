@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the side workloads measured after the headline at N = 1")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="sequence parallel without the chunked collectives overlapping the GEMMs")
+    ap.add_argument("--comm-sms", type=int, default=16, help=argparse.SUPPRESS)
     ap.add_argument("--no-sp", action="store_true",
                     help="tensor parallel without sequence parallelism (every rank holds the "
                          "full activations; allreduce after the row-parallel projections)")
@@ -505,6 +508,7 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     q = ltm.QuantConfig(scheme=ltm.SCHEME_W4A16 if w4a16 else ltm.SCHEME_W8A8,
                         act_dtype=ltm.DTYPE_BF16)
     blk = ltm.TitanBlock(cfg, q, comm=comm)
+    blk.set_overlap(not args.no_overlap, args.comm_sms)
     w = synthetic.block_weights(H, F, Ms, 1000)
     blk.load_weights(w)
     want_cpu = rank == 0 and ws == 1 and not args.no_cpu_baseline and not side
@@ -592,8 +596,12 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     e2e_value = B * S * args.steps / (float(e2e_t.item()) * 1e-3)
 
     torch.cuda.synchronize()
+    # per-kernel times of one more forward with the collectives on the
+    # caller's stream (not overlapped), so they have times of their own
+    blk.set_overlap(False, args.comm_sms)
     with ltm.KernelTimer() as kt:
         forward_all(x)
+    blk.set_overlap(not args.no_overlap, args.comm_sms)
     kernels = {name: {"launches": n, "ms": round(ms, 4), "ms_per_launch": round(ms / n, 5)}
                for name, (n, ms) in kt.result.items()}
     comm_ms = sum(ms for name, (n, ms) in kt.result.items() if name.startswith("nccl"))
@@ -617,6 +625,11 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
                        "parallelism": f"tp{ws}" + ("-sp" if sp else ""),
                        "tokens_per_s_per_gpu": round(value / ws, 1),
                        "comm_fraction_of_rank0_step": round(comm_ms / all_ms, 4) if all_ms else None,
+                       "comm_fraction_note": "collectives' share of rank 0's step in a forward "
+                                             "with them serialised on the compute stream (the "
+                                             "timed steps overlap them with the GEMMs)"
+                                             if (sp and not args.no_overlap) else None,
+                       "comm_overlap": bool(sp and not args.no_overlap and not w4a16),
                        "weights": "one random-init block's shard applied at every layer",
                        "l2": "inputs (1 GiB per activation tensor) larger than L2"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",

@@ -461,6 +461,48 @@ struct ltm_block {
     launch_rows_ema(kvmb.ptr, 2 * Hl, 2 * Hl, kcv.ptr, wslot, cfg.memory_update_rate, Ms, dt, st);
   }
 
+  // ---- sequence parallelism
+  // Collectives of the overlapped sequence-parallel forward run on a stream
+  // of the block's own (every NCCL call of the block on one stream, in one
+  // order on every rank), ordered against the caller's stream by events.
+  bool overlap = true;
+  int comm_sms = 16;  // SMs the chunked GEMMs leave to the concurrent collectives
+  cudaStream_t comm_st = nullptr;
+  std::vector<cudaEvent_t> evs;
+
+  ~ltm_block() {
+    for (cudaEvent_t e : evs) cudaEventDestroy(e);
+    if (comm_st) cudaStreamDestroy(comm_st);
+  }
+
+  void ensure_comm_stream(int n_events) {
+    if (!comm_st) LTM_CUDA_TRY(cudaStreamCreateWithFlags(&comm_st, cudaStreamNonBlocking));
+    while (static_cast<int>(evs.size()) < n_events) {
+      cudaEvent_t e = nullptr;
+      LTM_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      evs.push_back(e);
+    }
+  }
+  // `to` waits for the work issued so far on `from` (through event k).
+  void order(cudaStream_t from, cudaStream_t to, int k) {
+    if (from == to) return;
+    LTM_CUDA_TRY(cudaEventRecord(evs[k], from));
+    LTM_CUDA_TRY(cudaStreamWaitEvent(to, evs[k], 0));
+  }
+
+  // All-gather of this rank's rows [r0, r0 + Tr) of the int8 rows q [T, H]
+  // and their scales s [T], as one broadcast per root rank on the comm
+  // stream (event k0 + root marks its arrival).
+  void gather_rows_chunked(int8_t* q, float* s, int64_t Tr, int k0) {
+    for (int j = 0; j < tp; ++j) {
+      comm_group_start();
+      comm_broadcast_bytes(comm, q + j * Tr * H, Tr * H, j, comm_st);
+      comm_broadcast_bytes(comm, s + j * Tr, Tr * sizeof(float), j, comm_st);
+      comm_group_end(nullptr, comm_st);
+      LTM_CUDA_TRY(cudaEventRecord(evs[k0 + j], comm_st));
+    }
+  }
+
   // Sequence-parallel tensor-parallel forward (Megatron sequence
   // parallelism): x_loc / out_loc are this rank's T / tp consecutive rows of
   // the [B*S, H] activations.  LayerNorms, the gate and the gated
@@ -470,6 +512,13 @@ struct ltm_block {
   // reduce-scattered back to the rows' owners, so no rank repeats another's
   // row work and the bytes on NVLink are the reduce-scatter + all-gather of
   // the collectives they replace (the LayerNorm all-gathers in int8).
+  //
+  // Overlap (W8A8): every all-gather is a broadcast per root rank and every
+  // reduce-scatter a reduce per root rank, on the block's comm stream; the
+  // GEMM that consumes (or produces) the rows of root j runs as its own
+  // launch, so the transfer of one rank's rows overlaps the GEMM of
+  // another's (this rank's own rows first on the gathering side), with
+  // comm_sms SMs left free for the collectives' kernels.
   void forward_sp(const void* x_loc, void* out_loc, int B, int S, cudaStream_t st) {
     const int64_t T = static_cast<int64_t>(B) * S;
     const int64_t Tr = T / tp, r0 = static_cast<int64_t>(tpr) * Tr;
@@ -479,16 +528,25 @@ struct ltm_block {
     sploc.ensure(static_cast<size_t>(2 * Tr) * H * a);
     if (cfg.use_rotary) ensure_rope(S);
     const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
+    const bool ovl = overlap && w8a8;
+    ensure_comm_stream(2 * tp + 8);
+    cudaStream_t ns = ovl ? comm_st : st;  // the stream of the collectives
+    const int kA = 8, kB = 8 + tp;    // per-root events of the two chunked phases
     // 1. LN1 of the local rows into rows [r0, r0 + Tr) of the full buffers
     //    (+ the int8 of x's local rows for the gate), then all-gather
     if (w8a8) {
       launch_ln_x2(x_loc, dt, Tr, H, ln1_g.as<float>(), ln1_b.as<float>(), nullptr,
                    hq.as<int8_t>() + r0 * H, hs.as<float>() + r0, xq.as<int8_t>(), xs.as<float>(),
                    cfg.use_layer_norm != 0, st);
-      comm_group_start();
-      comm_allgather_bytes(comm, hq.as<int8_t>() + r0 * H, hq.ptr, Tr * H, st);
-      comm_allgather_bytes(comm, hs.as<float>() + r0, hs.ptr, Tr * sizeof(float), st);
-      comm_group_end("nccl_allgather", st);
+      if (ovl) {
+        order(st, comm_st, 0);
+        gather_rows_chunked(hq.as<int8_t>(), hs.as<float>(), Tr, kA);
+      } else {
+        comm_group_start();
+        comm_allgather_bytes(comm, hq.as<int8_t>() + r0 * H, hq.ptr, Tr * H, st);
+        comm_allgather_bytes(comm, hs.as<float>() + r0, hs.ptr, Tr * sizeof(float), st);
+        comm_group_end("nccl_allgather", st);
+      }
     } else {
       char* hl = static_cast<char*>(h.ptr) + r0 * H * a;
       if (cfg.use_layer_norm)
@@ -498,10 +556,22 @@ struct ltm_block {
         LTM_CUDA_TRY(cudaMemcpyAsync(hl, x_loc, Tr * H * a, cudaMemcpyDeviceToDevice, st));
       comm_allgather_bytes(comm, hl, h.ptr, Tr * H * a, st);
     }
-    // 2-4. K_M | V_M, Q | K | V | Qm of all T rows for this rank's heads, the
-    //      two attentions
+    // 2-3. K_M | V_M (needs no gathered rows: overlaps the first transfers),
+    //      Q | K | V | Qm of all T rows for this rank's heads
     compute_kvm(st);
-    qkv_proj(h.ptr, T, S, 0, st);
+    if (ovl) {
+      ScopedSmReserve reserve(comm_sms);
+      for (int i = 0; i < tp; ++i) {
+        const int j = (tpr + i) % tp;  // own rows first: they need no transfer
+        if (j != tpr) LTM_CUDA_TRY(cudaStreamWaitEvent(st, evs[kA + j], 0));
+        qkv_rows(j * Tr, Tr, S, st);
+      }
+      // the remaining broadcasts read hq rows that the next layer rewrites:
+      // the caller's stream has waited for all of them above
+    } else {
+      qkv_proj(h.ptr, T, S, 0, st);
+    }
+    // 4. the two attentions of this rank's heads over all T rows
     {
       AttnParams p{};
       p.q = qkv.ptr;
@@ -519,28 +589,46 @@ struct ltm_block {
       launch_attention(p, B, dh, true, dt, st);
       mem_attention(B, S, st);
     }
-    // 5. output projections: partial sums of all rows, reduce-scattered to
-    //    the rows' owners (rank 0's partial carries the biases)
-    if (w8a8) {
-      quant_rows(os.ptr, T, Hl, osq.as<int8_t>(), oss.as<float>(), amax.as<float>(), st);
-      quant_rows(om_.ptr, T, Hl, omq.as<int8_t>(), oms.as<float>(), amax.as<float>() + T, st);
-    }
+    // 5. output projections: partial sums of all rows, reduced to the rows'
+    //    owners (rank 0's partial carries the biases)
     void* sp = spm.ptr;
     void* mp = static_cast<char*>(spm.ptr) + T * H * a;
     void* s_loc = sploc.ptr;
     void* m_loc = static_cast<char*>(sploc.ptr) + Tr * H * a;
-    {
+    if (w8a8) {  // per-token int8 of the head-split rows: global row maxima
+      float* amx = amax.as<float>();
+      launch_row_absmax(os.ptr, dt, T, Hl, amx, st);
+      launch_row_absmax(om_.ptr, dt, T, Hl, amx + T, st);
+      order(st, ns, 1);
+      comm_allreduce(comm, amx, amx, 2 * T, LTM_DTYPE_F32, true, ns);
+      order(ns, st, 2);
+      launch_rowwise_int8_amax(os.ptr, dt, T, Hl, amx, osq.as<int8_t>(), oss.as<float>(), st);
+      launch_rowwise_int8_amax(om_.ptr, dt, T, Hl, amx + T, omq.as<int8_t>(), oms.as<float>(), st);
+    }
+    if (ovl) {
+      ScopedSmReserve reserve(comm_sms);
+      for (int j = 0; j < tp; ++j) {
+        out_rows(o, osq.as<int8_t>(), oss.as<float>(), Hl, j * Tr, Tr, sp, st);
+        out_rows(om, omq.as<int8_t>(), oms.as<float>(), Hl, j * Tr, Tr, mp, st);
+        order(st, comm_st, kB + j);
+        comm_group_start();
+        comm_reduce(comm, static_cast<char*>(sp) + j * Tr * H * a, s_loc, Tr * H, dt, j, comm_st);
+        comm_reduce(comm, static_cast<char*>(mp) + j * Tr * H * a, m_loc, Tr * H, dt, j, comm_st);
+        comm_group_end(nullptr, comm_st);
+      }
+      order(comm_st, st, 3);
+    } else {
       Epilogue ep;
       ep.out = sp;
       ep.ldo = H;
       o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
       ep.out = mp;
       om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+      comm_group_start();
+      comm_reduce_scatter(comm, sp, s_loc, Tr * H, dt, st);
+      comm_reduce_scatter(comm, mp, m_loc, Tr * H, dt, st);
+      comm_group_end("nccl_reduce_scatter", st);
     }
-    comm_group_start();
-    comm_reduce_scatter(comm, sp, s_loc, Tr * H, dt, st);
-    comm_reduce_scatter(comm, mp, m_loc, Tr * H, dt, st);
-    comm_group_end("nccl_reduce_scatter", st);
     // 6. gate and gated integration of the local rows
     if (cfg.use_memory_gating) {
       Epilogue ep;
@@ -561,10 +649,15 @@ struct ltm_block {
       launch_ln_x2(y.ptr, dt, Tr, H, ln2_g.as<float>(), ln2_b.as<float>(), nullptr,
                    zq.as<int8_t>() + r0 * H, zs.as<float>() + r0, nullptr, nullptr,
                    cfg.use_layer_norm != 0, st);
-      comm_group_start();
-      comm_allgather_bytes(comm, zq.as<int8_t>() + r0 * H, zq.ptr, Tr * H, st);
-      comm_allgather_bytes(comm, zs.as<float>() + r0, zs.ptr, Tr * sizeof(float), st);
-      comm_group_end("nccl_allgather", st);
+      if (ovl) {
+        order(st, comm_st, 4);
+        gather_rows_chunked(zq.as<int8_t>(), zs.as<float>(), Tr, kA);
+      } else {
+        comm_group_start();
+        comm_allgather_bytes(comm, zq.as<int8_t>() + r0 * H, zq.ptr, Tr * H, st);
+        comm_allgather_bytes(comm, zs.as<float>() + r0, zs.ptr, Tr * sizeof(float), st);
+        comm_group_end("nccl_allgather", st);
+      }
     } else {
       char* zl = static_cast<char*>(z.ptr) + r0 * H * a;
       if (cfg.use_layer_norm)
@@ -574,31 +667,86 @@ struct ltm_block {
         LTM_CUDA_TRY(cudaMemcpyAsync(zl, y.ptr, Tr * H * a, cudaMemcpyDeviceToDevice, st));
       comm_allgather_bytes(comm, zl, z.ptr, Tr * H * a, st);
     }
-    {
+    if (ovl) {
+      ScopedSmReserve reserve(comm_sms);
+      for (int i = 0; i < tp; ++i) {
+        const int j = (tpr + i) % tp;
+        if (j != tpr) LTM_CUDA_TRY(cudaStreamWaitEvent(st, evs[kA + j], 0));
+        Epilogue ep;
+        ep.act = LTM_EPI_GELU;
+        ep.out = static_cast<char*>(u.ptr) + j * Tr * Fl * a;
+        ep.ldo = Fl;
+        w1.run(nullptr, zq.as<int8_t>() + j * Tr * H, zs.as<float>() + j * Tr, Tr, kEpiPlain, dt,
+               ep, st, &wdq);
+      }
+    } else {
       Epilogue ep;
       ep.act = LTM_EPI_GELU;
       ep.out = u.ptr;
       ep.ldo = Fl;
       w1.run(z.ptr, zq.as<int8_t>(), zs.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
     }
-    if (w8a8) quant_rows(u.ptr, T, Fl, uq.as<int8_t>(), us.as<float>(), amax.as<float>(), st);
-    // 8. FFN-down partial sums of all rows (rank 0's carry b2), reduce-
-    //    scattered; the owner adds its rows' residual
-    {
+    if (w8a8) {
+      float* amx = amax.as<float>();
+      launch_row_absmax(u.ptr, dt, T, Fl, amx, st);
+      order(st, ns, 5);
+      comm_allreduce(comm, amx, amx, T, LTM_DTYPE_F32, true, ns);
+      order(ns, st, 6);
+      launch_rowwise_int8_amax(u.ptr, dt, T, Fl, amx, uq.as<int8_t>(), us.as<float>(), st);
+    }
+    // 8. FFN-down partial sums of all rows (rank 0's carry b2), reduced to
+    //    the rows' owners; the owner adds its rows' residual
+    if (ovl) {
+      ScopedSmReserve reserve(comm_sms);
+      for (int j = 0; j < tp; ++j) {
+        out_rows(w2, uq.as<int8_t>(), us.as<float>(), Fl, j * Tr, Tr, sp, st);
+        order(st, comm_st, kB + j);
+        comm_reduce(comm, static_cast<char*>(sp) + j * Tr * H * a, out_loc, Tr * H, dt, j, comm_st);
+      }
+      order(comm_st, st, 7);
+    } else {
       Epilogue ep;
       ep.out = sp;
       ep.ldo = H;
       w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+      comm_reduce_scatter(comm, sp, out_loc, Tr * H, dt, st);
     }
-    comm_reduce_scatter(comm, sp, out_loc, Tr * H, dt, st);
     launch_add3(out_loc, y.ptr, nullptr, out_loc, Tr * H, dt, st);
     // 9. memory write: column sums of the local rows, summed over the ranks
     if (q.memory_write && cfg.use_memory_gating) {
+      order(st, ns, 1);
       mw.update_bank(memory.ptr, kvmb.ptr, 2 * Hl, static_cast<const char*>(qkv.ptr) + 3 * Hl * a,
                      4 * Hl, T, H, nhl, nh, dh, Ms, cfg.memory_update_rate,
-                     q.use_attention_scores != 0, dt, comm, st, /*colsum_partial=*/true);
+                     q.use_attention_scores != 0, dt, comm, ns, /*colsum_partial=*/true);
+      order(ns, st, 2);
       kvm_fresh = false;
     }
+  }
+
+  // Q | K | V | Qm (RoPE) of rows [row0, row0 + M) from the gathered int8
+  // LayerNorm rows (W8A8).
+  void qkv_rows(int64_t row0, int64_t M, int S, cudaStream_t st) {
+    Epilogue ep;
+    ep.out = static_cast<char*>(qkv.ptr) + row0 * 4 * Hl * act_bytes();
+    ep.ldo = 4 * Hl;
+    ep.rope = rope.as<float2>();
+    ep.rope_cols = cfg.use_rotary ? 2 * Hl : 0;
+    ep.seq_len = S;
+    ep.head_dim = dh;
+    ep.rope_rows = rope_S;
+    ep.rope_row0 = row0;
+    qkvm.run(nullptr, hq.as<int8_t>() + row0 * H, hs.as<float>() + row0, M,
+             cfg.use_rotary ? kEpiRope : kEpiPlain, dt, ep, st, &wdq);
+  }
+
+  // Row-parallel partial sums [M, H] of rows [row0, row0 + M) (int8 inputs
+  // of width K, per-token scales) into out rows [row0, row0 + M).
+  void out_rows(const QLinear& lin, const int8_t* aq, const float* as, int64_t K, int64_t row0,
+                int64_t M, void* out, cudaStream_t st) {
+    Epilogue ep;
+    ep.out = static_cast<char*>(out) + row0 * H * act_bytes();
+    ep.ldo = H;
+    lin.run(nullptr, aq + row0 * K, as + row0, M, kEpiPlain, dt, ep, st, &wdq);
   }
 
   // Memory write of a caller-given state (fp32 [H]) with slot weights from
@@ -1039,6 +1187,15 @@ extern "C" ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, 
     LTM_REQUIRE(blk->dt != LTM_DTYPE_F32, "sequence parallelism needs f16 or bf16 activations");
     DeviceGuard g(blk->device);
     blk->forward_sp(x_local, y_local, B, S, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_block_set_overlap(ltm_block* blk, int overlap, int comm_sms) {
+  return guarded([&] {
+    LTM_REQUIRE(blk, "block is NULL");
+    LTM_REQUIRE(comm_sms >= 0 && comm_sms < 128, "comm_sms out of range");
+    blk->overlap = overlap != 0;
+    blk->comm_sms = comm_sms;
   });
 }
 

@@ -28,6 +28,11 @@ void comm_allgather_bytes(ltm_comm* c, const void* send, void* recv, size_t byte
 // count_per_rank elements of send.
 void comm_reduce_scatter(ltm_comm* c, const void* send, void* recv, size_t count_per_rank,
                          ltm_dtype dt, cudaStream_t st);
+// In-place broadcast of `bytes` bytes at buf from rank root.
+void comm_broadcast_bytes(ltm_comm* c, void* buf, size_t bytes, int root, cudaStream_t st);
+// Sum of every rank's send into recv on rank root (recv unused elsewhere).
+void comm_reduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dtype dt, int root,
+                 cudaStream_t st);
 // NCCL group brackets: the collectives between them launch as one (at the
 // end, which marks them for the kernel timer under `what` on stream st).
 void comm_group_start();

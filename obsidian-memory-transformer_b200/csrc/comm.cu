@@ -37,6 +37,10 @@ struct NcclApi {
                              cudaStream_t) = nullptr;
   ncclResult_t (*reduce_scatter)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
                                  ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, int, ncclComm_t,
+                         cudaStream_t) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
@@ -58,12 +62,15 @@ const NcclApi& nccl() {
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
     api.reduce_scatter =
         reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+    api.broadcast = reinterpret_cast<decltype(api.broadcast)>(dlsym(h, "ncclBroadcast"));
+    api.reduce = reinterpret_cast<decltype(api.reduce)>(dlsym(h, "ncclReduce"));
     api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
     api.get_version = reinterpret_cast<decltype(api.get_version)>(dlsym(h, "ncclGetVersion"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce &&
-             api.all_gather && api.reduce_scatter && api.group_start && api.group_end &&
+             api.all_gather && api.reduce_scatter && api.broadcast && api.reduce &&
+             api.group_start && api.group_end &&
              api.error_string;
   });
   if (!api.ok) {
@@ -120,6 +127,25 @@ void comm_reduce_scatter(ltm_comm* c, const void* send, void* recv, size_t count
                                    static_cast<ncclComm_t>(c->handle), st),
              "ncclReduceScatter");
   note_collective("nccl_reduce_scatter", st);
+}
+
+void comm_broadcast_bytes(ltm_comm* c, void* buf, size_t bytes, int root, cudaStream_t st) {
+  LTM_REQUIRE(c != nullptr, "NULL communicator");
+  if (bytes == 0) return;
+  nccl_check(nccl().broadcast(buf, buf, bytes, ncclInt8, root, static_cast<ncclComm_t>(c->handle),
+                              st),
+             "ncclBroadcast");
+  note_collective("nccl_broadcast", st);
+}
+
+void comm_reduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dtype dt, int root,
+                 cudaStream_t st) {
+  LTM_REQUIRE(c != nullptr, "NULL communicator");
+  if (count == 0) return;
+  nccl_check(nccl().reduce(send, recv, count, nccl_type(dt), ncclSum, root,
+                           static_cast<ncclComm_t>(c->handle), st),
+             "ncclReduce");
+  note_collective("nccl_reduce", st);
 }
 
 void comm_group_start() {

@@ -221,7 +221,20 @@ void dispatch_dtype(ltm_dtype d, F&& f) {
 }
 
 // Number of SMs of the current device (cached per device).
+// SMs the library's persistent grids may use on the current device: all of
+// them, less the reserve of a ScopedSmReserve active on this thread (left to
+// collectives that run concurrently on another stream).
 int device_sm_count();
+int device_sm_count_total();
+struct ScopedSmReserve {
+  explicit ScopedSmReserve(int n);
+  ~ScopedSmReserve();
+  ScopedSmReserve(const ScopedSmReserve&) = delete;
+  ScopedSmReserve& operator=(const ScopedSmReserve&) = delete;
+
+ private:
+  int prev_;
+};
 
 // Grid size of a persistent kernel: resident CTAs per SM (from the occupancy
 // calculator for this kernel, block size and dynamic smem) x SMs, capped at

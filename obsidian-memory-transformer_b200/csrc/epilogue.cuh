@@ -40,6 +40,9 @@ struct Epilogue {
   // position outside [0, rope_rows) is clamped; the launchers flag it)
   const int* row_pos = nullptr;
   int rope_rows = 0;
+  // rows of this launch are rows row0 + m of the whole batch (a GEMM over a
+  // row chunk): the position is (row0 + m) % seq_len
+  int64_t rope_row0 = 0;
   // RESID (aux0 = R) / GATEMIX (aux0 = s, aux1 = mem, aux2 = x); all use ld_aux
   const void* aux0 = nullptr;
   const void* aux1 = nullptr;
@@ -55,7 +58,8 @@ __device__ __forceinline__ int rope_row(const Epilogue& ep, int64_t m, bool row_
     const int p = row_ok ? __ldg(ep.row_pos + m) : 0;
     return min(max(p, 0), ep.rope_rows - 1);
   }
-  return static_cast<int>(static_cast<uint32_t>(m) % static_cast<uint32_t>(ep.seq_len));
+  return static_cast<int>(static_cast<uint64_t>(m + ep.rope_row0) %
+                          static_cast<uint64_t>(ep.seq_len));
 }
 
 // Sum over the warp's 32 rows of v[c]; lane c receives column c (31 shuffles,

@@ -10,6 +10,8 @@
 // quant_i8_exact, which falls back to the division near rounding ties).
 #include <type_traits>
 
+#include <algorithm>
+
 #include "block.cuh"
 
 namespace ltm_b200 {
@@ -340,7 +342,20 @@ __global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x
   if constexpr (VEC) {
     constexpr int V = Vec16<T>::N;
     const uint4* xv = reinterpret_cast<const uint4*>(xr);
-    for (int64_t j = lane; j < K / V; j += 32) {
+    const int64_t nv = K / V;
+    int64_t j = lane;
+    for (; j + 96 < nv; j += 128) {  // four independent 16-byte loads in flight per lane
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) raw[u] = __ldg(xv + j + 32 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+        for (int i = 0; i < V; ++i) m = fmaxf(m, fabsf(to_f32(e[i])));
+      }
+    }
+    for (; j < nv; j += 32) {
       const uint4 raw = __ldg(xv + j);
       const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
@@ -369,17 +384,26 @@ __global__ void __launch_bounds__(256) rowwise_int8_amax_kernel(const T* __restr
   if constexpr (VEC) {
     constexpr int V = Vec16<T>::N;
     const uint4* xv = reinterpret_cast<const uint4*>(xr);
-    for (int64_t j = lane; j < K / V; j += 32) {
-      const uint4 raw = __ldg(xv + j);
+    const int64_t nv = K / V;
+    auto put = [&](int64_t jj, const uint4& raw) {
       const T* e = reinterpret_cast<const T*>(&raw);
       int8_t out[V];
 #pragma unroll
       for (int i = 0; i < V; ++i) out[i] = quant_i8_exact(to_f32(e[i]), s, inv);
       if constexpr (V == 8)
-        *reinterpret_cast<uint2*>(qr + j * V) = *reinterpret_cast<const uint2*>(out);
+        *reinterpret_cast<uint2*>(qr + jj * V) = *reinterpret_cast<const uint2*>(out);
       else
-        *reinterpret_cast<uint32_t*>(qr + j * V) = *reinterpret_cast<const uint32_t*>(out);
+        *reinterpret_cast<uint32_t*>(qr + jj * V) = *reinterpret_cast<const uint32_t*>(out);
+    };
+    int64_t j = lane;
+    for (; j + 96 < nv; j += 128) {  // four independent 16-byte loads in flight per lane
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) raw[u] = __ldg(xv + j + 32 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) put(j + 32 * u, raw[u]);
     }
+    for (; j < nv; j += 32) put(j, __ldg(xv + j));
   } else {
     for (int64_t j = lane; j < K; j += 32) qr[j] = quant_i8_exact(to_f32(xr[j]), s, inv);
   }

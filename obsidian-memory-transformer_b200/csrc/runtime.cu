@@ -78,7 +78,19 @@ void note_device_alloc() { g_device_allocs.fetch_add(1, std::memory_order_relaxe
 void set_error(const std::string& msg) { t_last_error = msg; }
 void clear_error() { t_last_error.clear(); }
 
+namespace {
+thread_local int t_sm_reserve = 0;
+}  // namespace
+
+ScopedSmReserve::ScopedSmReserve(int n) : prev_(t_sm_reserve) { t_sm_reserve = n; }
+ScopedSmReserve::~ScopedSmReserve() { t_sm_reserve = prev_; }
+
 int device_sm_count() {
+  const int n = device_sm_count_total();
+  return n - t_sm_reserve > 1 ? n - t_sm_reserve : 1;
+}
+
+int device_sm_count_total() {
   static std::mutex mu;
   static std::vector<int> cache;
   int dev = 0;

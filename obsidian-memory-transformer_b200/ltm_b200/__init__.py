@@ -115,6 +115,7 @@ def _declare(L):
         "ltm_greedy_next_tokens": ([vp, ci, ci, ci, vp, vp, vp], ci),
         "ltm_block_forward_with_cache": ([vp, vp, vp, ci, ci, vp, vp, i64, vp], ci),
         "ltm_block_forward_sp": ([vp, vp, vp, ci, ci, vp], ci),
+        "ltm_block_set_overlap": ([vp, ci, ci], ci),
         "ltm_calibrator_create": ([ci, C.c_float, ci, C.POINTER(vp)], ci),
         "ltm_calibrator_collect": ([vp, vp, ci, i64, vp], ci),
         "ltm_calibrator_compute_range": ([vp, C.POINTER(C.c_float), C.POINTER(C.c_float), vp],
@@ -636,6 +637,10 @@ class TitanBlock:
         _check(lib().ltm_block_forward_sp(self._h, _ptr(x_local), _ptr(y), B, S,
                                           _stream(stream)))
         return y
+
+    def set_overlap(self, overlap: bool = True, comm_sms: int = 16) -> None:
+        """Chunked collectives overlapping the GEMMs in forward_sp (W8A8)."""
+        _check(lib().ltm_block_set_overlap(self._h, int(overlap), comm_sms))
 
     def _check_caches(self, k_cache, v_cache, B):
         heads = self.config.num_heads // (self._comm.nranks if self._comm is not None else 1)

@@ -50,7 +50,7 @@ def test_int8_rounding_ties_and_clamp(ltm, orc):
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
-@pytest.mark.parametrize("K", [768, 3072])
+@pytest.mark.parametrize("K", [768, 3072, 12288, 28672, 49152])  # from 12288: the two-pass kernel
 def test_act_per_token_rounding_ties(ltm, orc, dt, K):
     """Per-token activation codes at exact .5 boundaries (row absmax 127, so
     s = 1 and every k + 0.5 is a tie) and just off them: the warp quantizer's
@@ -69,6 +69,22 @@ def test_act_per_token_rounding_ties(ltm, orc, dt, K):
     qo, so = orc.quant_int8_rows(as_f32(ad))
     np.testing.assert_array_equal(q.cpu().numpy(), qo)
     np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_act_per_token_long_rows_many_per_cta(ltm, orc, dt):
+    """The FFN-hidden width of the hidden-8192 block (28672 values, 56 KiB per
+    row) over many rows: the long-row kernel (a warp per row, max pass then
+    quantize pass)."""
+    a = np.random.default_rng(29).standard_normal((611, 28672)).astype(np.float32)
+    a[::7] *= 30.0
+    a[5] = 0.0
+    ad = to_device(a, dt)
+    q, s = ltm.quantize_act_int8_per_token(ad)
+    qo, so = orc.quant_int8_rows(as_f32(ad))
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+    assert ltm.device_error() == 0
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])

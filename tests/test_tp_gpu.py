@@ -20,10 +20,10 @@ ROOT = Path(__file__).resolve().parents[1]
 TOL = {"f16": (2e-2, 1e-2), "bf16": (2e-2, 1e-2)}
 
 
-def _case(scheme, dt, memory_write, n=2):
+def _case(scheme, dt, memory_write, n=2, F=1024):
     # per-rank widths stay multiples of 32 (W8A8) / 128 (W4A16) up to 8 ranks
     H = 1024 if (scheme == "w4a16" and n > 4) else 512
-    nh, F, Ms, B, S = 8, 1024, 128, 2, 96
+    nh, Ms, B, S = 8, 128, 2, 96
     return dict(H=H, nh=nh, F=F, Ms=Ms, B=B, S=S, scheme=scheme, dt=dt,
                 memory_write=memory_write, seed=11)
 
@@ -53,6 +53,7 @@ def _worker(rank, n, uid, c, out, sp=False):
         x = synthetic.activations(B * S, H, c["seed"] + 1)
         xd = to_device(x, c["dt"])
         if sp:  # this rank's rows only; the parent gathers the slices
+            blk.set_overlap(sp == "overlap")
             Tr = B * S // n
             xl = xd[rank * Tr:(rank + 1) * Tr].contiguous()
             y1 = blk.forward_sp(xl, B, S)
@@ -93,15 +94,19 @@ def _run_tp(c, n=2, sp=False):
 
 
 @pytest.mark.parametrize("n", [2, 4, 8])
-@pytest.mark.parametrize("sp", [False, True])
-@pytest.mark.parametrize("scheme,dt,memory_write",
-                         [("w8a8", "f16", True), ("w8a8", "bf16", False), ("w4a16", "bf16", True)])
-def test_tp_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_write, sp, n):
+@pytest.mark.parametrize("sp", [False, "overlap", "serial"])
+@pytest.mark.parametrize("scheme,dt,memory_write,F",
+                         [("w8a8", "f16", True, 1024), ("w8a8", "bf16", False, 1024),
+                          ("w4a16", "bf16", True, 1024),
+                          # 1024 FFN columns per rank at 8 ranks: the split row
+                          # quantizers' four-loads-per-lane loop
+                          ("w8a8", "bf16", False, 8192)])
+def test_tp_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_write, F, sp, n):
     import torch
     if torch.cuda.device_count() < n:
         pytest.skip(f"needs {n} GPUs")
     from ltm_b200 import synthetic
-    c = _case(scheme, dt, memory_write, n)
+    c = _case(scheme, dt, memory_write, n, F)
     res = _run_tp(c, n, sp)
     if sp:  # gather the row slices into the full outputs
         y1 = np.concatenate([res[r][0] for r in range(n)]).reshape(c["B"], c["S"], c["H"])
@@ -127,7 +132,7 @@ def test_tp_block_matches_single_gpu_and_oracle(ltm, orc, scheme, dt, memory_wri
                 update_rate=cfg.memory_update_rate, use_rotary=1, use_bias=1, use_layer_norm=1,
                 use_memory_gating=1)
     ref, mem_ref = orc.block_forward(ocfg, w, as_f32(xd).reshape(B * S, H), B, S)
-    what = f"tp{n}{' sp' if sp else ''} {scheme} {dt}"
+    what = f"tp{n}{' sp ' + sp if sp else ''} {scheme} {dt}"
     assert_close(y1.reshape(ref.shape), ref, *TOL[dt], what=f"{what} vs oracle")
     assert_close(y1, s1, *TOL[dt], what=f"{what} vs single GPU")
     if memory_write:
