@@ -60,8 +60,9 @@ def parse():
     ap.add_argument("--no-probe", action="store_true", help="skip the per-kernel roofline probe")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the side workloads measured after the headline at N = 1")
-    ap.add_argument("--no-overlap", action="store_true",
-                    help="sequence parallel without the chunked collectives overlapping the GEMMs")
+    ap.add_argument("--overlap", choices=["auto", "on", "off"], default="auto",
+                    help="chunked collectives overlapping the GEMMs in the sequence-parallel "
+                         "forward (auto: the library's choice, on from 4 GPUs)")
     ap.add_argument("--comm-sms", type=int, default=16, help=argparse.SUPPRESS)
     ap.add_argument("--no-sp", action="store_true",
                     help="tensor parallel without sequence parallelism (every rank holds the "
@@ -75,7 +76,7 @@ def parse():
                          "W4A16 batched decode step against a 32768-position KV cache (N > 1 = "
                          "replicas)")
     ap.add_argument("--ncu-case", nargs="?", const="prefill", default=None,
-                    choices=["prefill", "tp", "w4a16", "decode"],
+                    choices=["prefill", "tp", "tplayer", "w4a16", "decode"],
                     help="launch each kernel of one block once at the workload's shapes (for ncu); "
                          "tp: the tensor-parallel layer's attention and K = 8192 GEMM at batch 2; "
                          "w4a16: one long-context block forward at 1 x 8192 tokens; decode: "
@@ -249,9 +250,10 @@ def step_work_tp(layers: int, tp: int, wl: dict = TP_WL, gemm_class: str = "w8a8
             "attn_tc_kernel": {"amount": attn * layers, "unit": "flop"}}
 
 
-def roofline_of(result: dict, work: dict, torch) -> tuple:
+def roofline_of(result: dict, work: dict, torch, workload: str = "B8 S2048 H768") -> tuple:
     """Roofline entry of the dominant kernel class of one timed step (kernel
-    timer result) and the measured int8 peak."""
+    timer result) and the measured int8 peak; `workload` selects the ncu
+    traffic row of profiles/traffic.md."""
     pk, pk_src = peaks()
     i8 = int8_peak(torch)
     by_kind = {}
@@ -281,7 +283,7 @@ def roofline_of(result: dict, work: dict, torch) -> tuple:
         unit, bound = "GB/s", "hbm"
     roof = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2),
             "peak": round(peak, 2), "unit": unit, "frac": round(achieved / peak, 4),
-            "traffic": traffic_from_profiles(dom), "peak_source": peak_src,
+            "traffic": traffic_from_profiles(dom, workload), "peak_source": peak_src,
             "launches_per_step": d["launches"], "avg_launch_ms": round(avg_ms, 5),
             "algorithmic_per_launch": per_launch, "algorithmic_unit": work[dom]["unit"]}
     return roof, i8
@@ -402,6 +404,27 @@ def probe_tp_case(torch, ltm):
     torch.cuda.synchronize()
 
 
+def probe_tp_layer_case(torch, ltm):
+    """Two forwards of one hidden-8192 W8A8 block (the headline workload's
+    layer at tensor-parallel size 1) at batch 2 x seq 4096 (8192 tokens, an
+    eighth of the workload's rows): every kernel of the layer at its real
+    widths, a few GB on the device (for ncu DRAM counts, scaled by 8)."""
+    from ltm_b200 import synthetic
+    wl = TP_WL
+    H, F, Ms, nh, S = wl["H"], wl["F"], wl["Ms"], wl["nh"], wl["S"]
+    cfg = ltm.TitanBlockConfig(hidden_dim=H, ffn_dim=F, num_heads=nh, head_dim=H // nh,
+                               memory_slots=Ms)
+    q = ltm.QuantConfig(scheme=ltm.SCHEME_W8A8, act_dtype=ltm.DTYPE_BF16)
+    blk = ltm.TitanBlock(cfg, q)
+    blk.load_weights(synthetic.block_weights(H, F, Ms, 1000))
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.randn((2, S, H), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    blk(x)
+    blk(x)
+    torch.cuda.synchronize()
+    blk.close()
+
+
 def probe_w4a16_case(torch, ltm):
     """One forward of one long-context block (hidden 4096, 32 heads, FFN 11008,
     4096 slots, W4A16, bf16) at 1 x 8192 tokens, after a warm-up forward: the
@@ -444,15 +467,16 @@ def int8_peak(torch):
         return None
 
 
-def traffic_from_profiles(kernel: str):
-    """DRAM bytes per launch of `kernel` recorded from an ncu capture in
-    profiles/traffic.md (table rows: | kernel | workload | bytes/launch | ...)."""
+def traffic_from_profiles(kernel: str, workload: str = "B8 S2048 H768"):
+    """DRAM bytes per launch of `kernel` on the workload whose description
+    contains `workload`, recorded from an ncu capture in profiles/traffic.md
+    (table rows: | kernel | workload | bytes/launch | ...)."""
     f = ROOT / "profiles" / "traffic.md"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
         cells = [c.strip() for c in line.strip().strip("|").split("|")]
-        if len(cells) >= 3 and cells[0] == kernel:
+        if len(cells) >= 3 and cells[0] == kernel and workload in cells[1]:
             try:
                 return float(cells[2])
             except ValueError:
@@ -508,7 +532,9 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     q = ltm.QuantConfig(scheme=ltm.SCHEME_W4A16 if w4a16 else ltm.SCHEME_W8A8,
                         act_dtype=ltm.DTYPE_BF16)
     blk = ltm.TitanBlock(cfg, q, comm=comm)
-    blk.set_overlap(not args.no_overlap, args.comm_sms)
+    ovl_mode = {"auto": None, "on": True, "off": False}[args.overlap]
+    blk.set_overlap(ovl_mode, args.comm_sms)
+    overlapped = (ovl_mode if ovl_mode is not None else ws >= 4) and not w4a16
     w = synthetic.block_weights(H, F, Ms, 1000)
     blk.load_weights(w)
     want_cpu = rank == 0 and ws == 1 and not args.no_cpu_baseline and not side
@@ -601,7 +627,7 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     blk.set_overlap(False, args.comm_sms)
     with ltm.KernelTimer() as kt:
         forward_all(x)
-    blk.set_overlap(not args.no_overlap, args.comm_sms)
+    blk.set_overlap(ovl_mode, args.comm_sms)
     kernels = {name: {"launches": n, "ms": round(ms, 4), "ms_per_launch": round(ms / n, 5)}
                for name, (n, ms) in kt.result.items()}
     comm_ms = sum(ms for name, (n, ms) in kt.result.items() if name.startswith("nccl"))
@@ -609,7 +635,8 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     roofline = None
     if rank == 0 and not args.no_probe:
         work = step_work_tp(L, ws, wl, "gemm_f16_tc_kernel" if w4a16 else "w8a8_tc_kernel")
-        roofline, i8 = roofline_of(kt.result, work, torch)
+        roofline, i8 = roofline_of(kt.result, work, torch,
+                                   "B4 S8192 H4096" if w4a16 else f"hidden-8192 tp{ws}")
         if i8:
             kernels["int8_peak_tops_measured"] = round(i8, 1)
     if rank == 0:
@@ -628,8 +655,8 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
                        "comm_fraction_note": "collectives' share of rank 0's step in a forward "
                                              "with them serialised on the compute stream (the "
                                              "timed steps overlap them with the GEMMs)"
-                                             if (sp and not args.no_overlap) else None,
-                       "comm_overlap": bool(sp and not args.no_overlap and not w4a16),
+                                             if (sp and overlapped) else None,
+                       "comm_overlap": bool(sp and overlapped),
                        "weights": "one random-init block's shard applied at every layer",
                        "l2": "inputs (1 GiB per activation tensor) larger than L2"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
@@ -857,7 +884,7 @@ def run_decode(args, wl: dict = DEC_WL, side: bool = False):
     roofline = None
     if rank == 0 and not args.no_probe:
         work = {"decode_attn_kernel": {"amount": lb["kv"] * L, "unit": "byte"}}
-        roofline, _ = roofline_of(kt.result, work, torch)
+        roofline, _ = roofline_of(kt.result, work, torch, "decode B64 H4096")
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and not side:
         cpu = cpu_baseline_decode(wl)
@@ -1176,6 +1203,8 @@ def main():
         import ltm_b200 as ltm
         if args.ncu_case == "tp":
             probe_tp_case(torch, ltm)
+        elif args.ncu_case == "tplayer":
+            probe_tp_layer_case(torch, ltm)
         elif args.ncu_case == "w4a16":
             probe_w4a16_case(torch, ltm)
         elif args.ncu_case == "decode":

@@ -470,11 +470,12 @@ LTM_API ltm_status ltm_block_create_tp(const ltm_block_config* cfg, const ltm_qu
  * work.  Consecutive layers chain y_local -> x_local with no gather. */
 LTM_API ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, void* y_local, int B,
                                         int S, void* stream);
-/* Overlap of ltm_block_forward_sp (W8A8; on by default): the all-gathers run
- * as one broadcast per root rank and the reduce-scatters as one reduce per
- * root rank on a stream of the block's own, each overlapping the GEMM of
- * another rank's rows, whose grids leave comm_sms SMs (default 16) to the
- * collectives.  overlap = 0: the plain collectives on the caller's stream. */
+/* Overlap of ltm_block_forward_sp (W8A8): the all-gathers run as one
+ * broadcast per root rank and the reduce-scatters as one reduce per root rank
+ * on a stream of the block's own, each overlapping the GEMM of another rank's
+ * rows, whose grids leave comm_sms SMs (default 16) to the collectives.
+ * overlap = 1: on; 0: the plain collectives on the caller's stream; -1
+ * (default): on from 4 ranks. */
 LTM_API ltm_status ltm_block_set_overlap(ltm_block* blk, int overlap, int comm_sms);
 
 /* ----------------------------------------------------------------- model -- */

@@ -465,7 +465,10 @@ struct ltm_block {
   // Collectives of the overlapped sequence-parallel forward run on a stream
   // of the block's own (every NCCL call of the block on one stream, in one
   // order on every rank), ordered against the caller's stream by events.
-  bool overlap = true;
+  // -1: automatic (overlap from 4 ranks on; at 2 ranks half of each
+  // collective stays exposed and the SM reserve costs as much as the rest
+  // saves, measured); 0 / 1: set by ltm_block_set_overlap
+  int overlap = -1;
   int comm_sms = 16;  // SMs the chunked GEMMs leave to the concurrent collectives
   cudaStream_t comm_st = nullptr;
   std::vector<cudaEvent_t> evs;
@@ -528,7 +531,7 @@ struct ltm_block {
     sploc.ensure(static_cast<size_t>(2 * Tr) * H * a);
     if (cfg.use_rotary) ensure_rope(S);
     const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
-    const bool ovl = overlap && w8a8;
+    const bool ovl = (overlap < 0 ? tp >= 4 : overlap != 0) && w8a8;
     ensure_comm_stream(2 * tp + 8);
     cudaStream_t ns = ovl ? comm_st : st;  // the stream of the collectives
     const int kA = 8, kB = 8 + tp;    // per-root events of the two chunked phases
@@ -1194,7 +1197,7 @@ extern "C" ltm_status ltm_block_set_overlap(ltm_block* blk, int overlap, int com
   return guarded([&] {
     LTM_REQUIRE(blk, "block is NULL");
     LTM_REQUIRE(comm_sms >= 0 && comm_sms < 128, "comm_sms out of range");
-    blk->overlap = overlap != 0;
+    blk->overlap = overlap < 0 ? -1 : (overlap != 0 ? 1 : 0);
     blk->comm_sms = comm_sms;
   });
 }

@@ -442,9 +442,28 @@ struct TmaTileEpilogue {
   float rs_next = 1.0f;
   float cs_next[NCH], bs_next[NCH];
 
-  // Fetches the row scale of row m and the scale/bias of columns nw + 32c + lane.
+  // Fetches the row scale of row m and the scale/bias of columns nw + 32c + lane,
+  // and asks L2 for the residual / gate-mix rows the tile's chunks will load
+  // (one bulk prefetch per tensor of this lane's row segment), so that their
+  // loads, issued a chunk ahead, meet L2 latency rather than DRAM latency.
   __device__ __forceinline__ void prefetch(const Epilogue& ep, int64_t m, int64_t nw, int M, int N,
                                            int lane) {
+    if constexpr (MODE == kEpiResid || MODE == kEpiGateMix) {
+      if (m < M && nw < N) {
+        const int64_t ncols = (N - nw) < CW ? (N - nw) : CW;
+        const uint32_t bytes = static_cast<uint32_t>(ncols * sizeof(OutT)) & ~15u;
+        const void* src[3] = {ep.aux0, ep.aux1, ep.aux2};
+        constexpr int kT = MODE == kEpiResid ? 1 : 3;
+#pragma unroll
+        for (int a = 0; a < kT; ++a) {
+          const uint8_t* row = reinterpret_cast<const uint8_t*>(
+              static_cast<const OutT*>(src[a]) + m * ep.ld_aux + nw);
+          if (bytes && (reinterpret_cast<uintptr_t>(row) & 15u) == 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row), "r"(bytes)
+                         : "memory");
+        }
+      }
+    }
     if constexpr (kMath) {
       rs_next = (ep.row_scale && m < M) ? __ldg(ep.row_scale + m) : 1.0f;
 #pragma unroll

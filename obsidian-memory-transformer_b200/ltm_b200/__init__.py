@@ -638,9 +638,11 @@ class TitanBlock:
                                           _stream(stream)))
         return y
 
-    def set_overlap(self, overlap: bool = True, comm_sms: int = 16) -> None:
-        """Chunked collectives overlapping the GEMMs in forward_sp (W8A8)."""
-        _check(lib().ltm_block_set_overlap(self._h, int(overlap), comm_sms))
+    def set_overlap(self, overlap=True, comm_sms: int = 16) -> None:
+        """Chunked collectives overlapping the GEMMs in forward_sp (W8A8):
+        True, False, or None for the library's choice (on from 4 ranks)."""
+        _check(lib().ltm_block_set_overlap(self._h, -1 if overlap is None else int(overlap),
+                                           comm_sms))
 
     def _check_caches(self, k_cache, v_cache, B):
         heads = self.config.num_heads // (self._comm.nranks if self._comm is not None else 1)
