@@ -84,6 +84,20 @@ void read_all(FILE* f, void* p, size_t n, const char* path) {
 
 size_t pad16(size_t n) { return (16 - n % 16) % 16; }
 
+// Makes `dev` current for a scope and restores the caller's device on every
+// exit, the error paths included.
+struct DeviceScope {
+  int prev = -1;
+  explicit DeviceScope(int dev) {
+    LTM_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != dev) LTM_CUDA_TRY(cudaSetDevice(dev));
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 void save(ltm_block* b, const char* path, uint32_t kind) {
   LTM_REQUIRE(b && path, "NULL argument");
   ltm_block_config cfg;
@@ -93,9 +107,7 @@ void save(ltm_block* b, const char* path, uint32_t kind) {
   block_identity(b, &cfg, &q, &tp, &tpr, &device, &loaded);
   const bool weights = kind == kKindBlock;
   LTM_REQUIRE(loaded, "block not loaded: nothing to save");
-  int prev = 0;
-  LTM_CUDA_TRY(cudaGetDevice(&prev));
-  LTM_CUDA_TRY(cudaSetDevice(device));
+  DeviceScope on(device);
   LTM_CUDA_TRY(cudaDeviceSynchronize());  // the state of all work issued so far
   const std::vector<StateSection> secs = block_state(b, weights, true, false);
   FileHeader h;
@@ -113,7 +125,6 @@ void save(ltm_block* b, const char* path, uint32_t kind) {
   File out;
   out.f = std::fopen(path, "wb");
   if (!out.f) {
-    cudaSetDevice(prev);
     set_error(std::string("cannot open checkpoint for writing: ") + path);
     throw Fail{LTM_ERR_INVALID_ARG};
   }
@@ -137,7 +148,6 @@ void save(ltm_block* b, const char* path, uint32_t kind) {
     set_error(std::string("checkpoint write failed: ") + path);
     throw Fail{LTM_ERR_INVALID_ARG};
   }
-  cudaSetDevice(prev);
 }
 
 void load(ltm_block* b, const char* path, uint32_t kind) {
@@ -177,28 +187,33 @@ void load(ltm_block* b, const char* path, uint32_t kind) {
     LTM_REQUIRE(h.tp == tp && h.tpr == tpr,
                 "checkpoint tensor-parallel size / rank differ from the block's");
   }
-  int prev = 0;
-  LTM_CUDA_TRY(cudaGetDevice(&prev));
-  LTM_CUDA_TRY(cudaSetDevice(device));
+  DeviceScope on(device);
   const std::vector<StateSection> secs = block_state(b, weights, true, true);
   LTM_REQUIRE(h.n_sections == secs.size(), "checkpoint section count differs from the block's");
+  // Two passes over the sections: the first checks every name, size and
+  // checksum, the second copies; a damaged file fails before any of the
+  // block's buffers is written, so the block keeps its previous state.
+  const long first = std::ftell(in.f);
+  LTM_REQUIRE(first >= 0, "checkpoint file is not seekable");
   std::vector<unsigned char> host;
   unsigned char pad[16];
-  for (const StateSection& s : secs) {
-    SectionHeader sh;
-    read_all(in.f, &sh, sizeof(sh), path);
-    sh.name[sizeof(sh.name) - 1] = '\0';
-    LTM_REQUIRE(s.name == sh.name, "checkpoint section order differs: expected " + s.name);
-    LTM_REQUIRE(sh.bytes == s.bytes, "checkpoint section size differs: " + s.name);
-    host.resize(s.bytes);
-    read_all(in.f, host.data(), host.size(), path);
-    read_all(in.f, pad, pad16(host.size()), path);
-    LTM_REQUIRE(fnv1a(host.data(), host.size()) == sh.checksum,
-                "checkpoint section checksum mismatch: " + s.name);
-    LTM_CUDA_TRY(cudaMemcpy(s.ptr, host.data(), s.bytes, cudaMemcpyHostToDevice));
+  for (int pass = 0; pass < 2; ++pass) {
+    LTM_REQUIRE(std::fseek(in.f, first, SEEK_SET) == 0, "checkpoint file is not seekable");
+    for (const StateSection& s : secs) {
+      SectionHeader sh;
+      read_all(in.f, &sh, sizeof(sh), path);
+      sh.name[sizeof(sh.name) - 1] = '\0';
+      LTM_REQUIRE(s.name == sh.name, "checkpoint section order differs: expected " + s.name);
+      LTM_REQUIRE(sh.bytes == s.bytes, "checkpoint section size differs: " + s.name);
+      host.resize(s.bytes);
+      read_all(in.f, host.data(), host.size(), path);
+      read_all(in.f, pad, pad16(host.size()), path);
+      LTM_REQUIRE(fnv1a(host.data(), host.size()) == sh.checksum,
+                  "checkpoint section checksum mismatch: " + s.name);
+      if (pass == 1) LTM_CUDA_TRY(cudaMemcpy(s.ptr, host.data(), s.bytes, cudaMemcpyHostToDevice));
+    }
   }
   block_state_loaded(b, weights);
-  cudaSetDevice(prev);
 }
 
 }  // namespace

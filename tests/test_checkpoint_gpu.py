@@ -2,7 +2,8 @@
 ltm_block_save_memory / _load_memory): a block restored from a file gives
 bit-identical outputs without its fp32 master weights, the bank written by a
 forward survives the round trip, and damaged or mismatched files are refused
-with LTM_ERR_INVALID_ARG (checksums, dimensions, scheme, kind)."""
+with LTM_ERR_INVALID_ARG (checksums, dimensions, scheme, kind) without
+touching the block."""
 import numpy as np
 import pytest
 
@@ -95,5 +96,13 @@ def test_damaged_and_mismatched_checkpoints_are_refused(ltm, tmp_path):
     blk.save_memory(bank)
     assert "bank" in refused(bank.read_bytes(), blk)
     assert "block" in refused(data, blk, "load_memory")
-    for b in (blk, other_dims, other_scheme):
+    # a file damaged in its last section leaves a block with other weights as
+    # it was: every section is checked before the first one is copied
+    from ltm_b200 import synthetic
+    x = to_device(synthetic.activations(32, 256, 8), "f16").reshape(1, 32, 256)
+    keep, _, _ = _block(ltm, "w8a8", "f16", 11)
+    y_before = as_f32(keep(x))
+    refused(flipped, keep)
+    assert np.array_equal(as_f32(keep(x)), y_before), "a refused load changed the block"
+    for b in (blk, other_dims, other_scheme, keep):
         b.close()
