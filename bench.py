@@ -62,7 +62,7 @@ def parse():
                     help="skip the side workloads measured after the headline at N = 1")
     ap.add_argument("--overlap", choices=["auto", "on", "off"], default="auto",
                     help="chunked collectives overlapping the GEMMs in the sequence-parallel "
-                         "forward (auto: the library's choice, on from 4 GPUs)")
+                         "forward (auto: the library's default, off)")
     ap.add_argument("--comm-sms", type=int, default=16, help=argparse.SUPPRESS)
     ap.add_argument("--no-sp", action="store_true",
                     help="tensor parallel without sequence parallelism (every rank holds the "
@@ -534,7 +534,7 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     blk = ltm.TitanBlock(cfg, q, comm=comm)
     ovl_mode = {"auto": None, "on": True, "off": False}[args.overlap]
     blk.set_overlap(ovl_mode, args.comm_sms)
-    overlapped = (ovl_mode if ovl_mode is not None else ws >= 4) and not w4a16
+    overlapped = bool(ovl_mode) and not w4a16
     w = synthetic.block_weights(H, F, Ms, 1000)
     blk.load_weights(w)
     want_cpu = rank == 0 and ws == 1 and not args.no_cpu_baseline and not side

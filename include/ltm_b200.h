@@ -471,12 +471,24 @@ LTM_API ltm_status ltm_block_create_tp(const ltm_block_config* cfg, const ltm_qu
 LTM_API ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, void* y_local, int B,
                                         int S, void* stream);
 /* Overlap of ltm_block_forward_sp (W8A8): the all-gathers run as one
- * broadcast per root rank and the reduce-scatters as one reduce per root rank
- * on a stream of the block's own, each overlapping the GEMM of another rank's
- * rows, whose grids leave comm_sms SMs (default 16) to the collectives.
- * overlap = 1: on; 0: the plain collectives on the caller's stream; -1
- * (default): on from 4 ranks. */
+ * broadcast per root rank and the row-block exchanges as one gather per root
+ * rank on a stream of the block's own, each overlapping the GEMM of another
+ * rank's rows, whose grids leave comm_sms SMs (default 16) to the
+ * collectives.  overlap = 1: on; 0 or -1 (default): the plain collectives on
+ * the caller's stream (measured faster at 2 and 8 ranks).  The row-parallel
+ * partial sums reach their rows' owner as one slot per rank (all-to-all) and
+ * are summed there in fp32 with one rounding, in either mode. */
 LTM_API ltm_status ltm_block_set_overlap(ltm_block* blk, int overlap, int comm_sms);
+/* Row-parallel reductions of ltm_block_forward_sp.  LTM_TP_REDUCE_ACT
+ * (default): the ranks' partial sums in the activation type, summed in fp32
+ * at the rows' owner and rounded once.  LTM_TP_REDUCE_EXACT (W8A8 only): the
+ * int32 GEMM accumulators are exchanged and summed exactly and the unsplit
+ * GEMM's epilogue (scales, bias, residual) is applied at the owner, so
+ * forward_sp's rows equal the single-GPU block's bit for bit (the memory-bank
+ * update aside, whose column sums are accumulated in no fixed order); the
+ * three row-parallel exchanges carry twice the bytes. */
+typedef enum { LTM_TP_REDUCE_ACT = 0, LTM_TP_REDUCE_EXACT = 1 } ltm_tp_reduction;
+LTM_API ltm_status ltm_block_set_tp_reduction(ltm_block* blk, int mode);
 
 /* ----------------------------------------------------------------- model -- */
 /* Multi-layer model (token embedding gather + n_layers Titan blocks), the

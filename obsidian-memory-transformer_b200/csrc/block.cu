@@ -51,6 +51,87 @@ __global__ void add3_kernel(const T* __restrict__ a, const T* __restrict__ b,
     y[i] = from_f32<T>(to_f32(a[i]) + to_f32(b[i]) + (c ? to_f32(c[i]) : 0.0f));
 }
 
+// 16-bit rows summed over the ranks' partial slots (8 values per 16-byte
+// load, every slot's load in flight before the adds).
+template <class T>
+__global__ void sum_slots_kernel(const uint4* __restrict__ slots, const uint4* __restrict__ own,
+                                 int nslots, int own_slot, int64_t stride8,
+                                 const uint4* __restrict__ add, uint4* __restrict__ y, int64_t n8) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < nslots) v[j] = __ldcs(j == own_slot ? own + i : slots + j * stride8 + i);
+    for (int j = 0; j < nslots; ++j) {
+      const uint4 w = j < 8 ? v[j] : __ldcs(j == own_slot ? own + i : slots + j * stride8 + i);
+      const T* e16 = reinterpret_cast<const T*>(&w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += to_f32(e16[e]);
+    }
+    if (add) {
+      const uint4 w = __ldg(add + i);
+      const T* e16 = reinterpret_cast<const T*>(&w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += to_f32(e16[e]);
+    }
+    uint4 o;
+    T* o16 = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o16[e] = from_f32<T>(acc[e]);
+    y[i] = o;
+  }
+}
+
+// int32 accumulator rows summed over the ranks' slots (4 columns per
+// thread), then the tensor-core epilogue's arithmetic.
+template <class T>
+__global__ void sum_slots_i32_kernel(const int4* __restrict__ slots, const int4* __restrict__ own,
+                                     int nslots, int own_slot, int64_t stride4,
+                                     const float* __restrict__ rs, const float4* __restrict__ cs,
+                                     const float4* __restrict__ bias, const T* __restrict__ add,
+                                     T* __restrict__ y, int64_t rows, int64_t cols4) {
+  const int64_t n = rows * cols4;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols4, c4 = i - r * cols4;
+    int4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < nslots) v[j] = __ldcs(j == own_slot ? own + i : slots + j * stride4 + i);
+    int acc[4] = {0, 0, 0, 0};
+    for (int j = 0; j < nslots; ++j) {
+      const int4 w = j < 8 ? v[j] : __ldcs(j == own_slot ? own + i : slots + j * stride4 + i);
+      acc[0] += w.x;
+      acc[1] += w.y;
+      acc[2] += w.z;
+      acc[3] += w.w;
+    }
+    const float rsv = rs ? __ldg(rs + r) : 1.0f;
+    const float4 csv = cs ? __ldg(cs + c4) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+    const float4 bv = bias ? __ldg(bias + c4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float o[4];
+    o[0] = fmaf(static_cast<float>(acc[0]) * rsv, csv.x, bv.x);
+    o[1] = fmaf(static_cast<float>(acc[1]) * rsv, csv.y, bv.y);
+    o[2] = fmaf(static_cast<float>(acc[2]) * rsv, csv.z, bv.z);
+    o[3] = fmaf(static_cast<float>(acc[3]) * rsv, csv.w, bv.w);
+    if (add) {
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(add) + i);
+      const T* e16 = reinterpret_cast<const T*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] += to_f32(e16[e]);
+    }
+    uint2 out;
+    T* o16 = reinterpret_cast<T*>(&out);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o16[e] = from_f32<T>(o[e]);
+    reinterpret_cast<uint2*>(y)[i] = out;
+  }
+}
+
 int grid_for(int64_t n) {
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
   int64_t g = (n + 255) / 256;
@@ -85,6 +166,49 @@ void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n
                                                     static_cast<const T*>(c), static_cast<T*>(y), n);
   });
   check_launch("add3_kernel", stream);
+}
+
+void launch_sum_slots(const void* slots, const void* own, int nslots, int own_slot,
+                      int64_t slot_stride, const void* add, void* y, int64_t n, ltm_dtype dt,
+                      cudaStream_t stream) {
+  LTM_REQUIRE(dt != LTM_DTYPE_F32, "slot sums are for 16-bit rows");
+  LTM_REQUIRE(n % 8 == 0 && slot_stride % 8 == 0, "slot rows must be whole 16-byte units");
+  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  LTM_REQUIRE(al(slots) && al(own) && al(y) && (!add || al(add)), "slot buffers must be 16-byte aligned");
+  if (n == 0) return;
+  const int64_t n8 = n / 8;
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    if constexpr (sizeof(T) == 2)
+      sum_slots_kernel<T><<<grid_for(n8), 256, 0, stream>>>(
+          static_cast<const uint4*>(slots), static_cast<const uint4*>(own), nslots, own_slot,
+          slot_stride / 8, static_cast<const uint4*>(add), static_cast<uint4*>(y), n8);
+  });
+  check_launch("sum_slots_kernel", stream);
+}
+
+void launch_sum_slots_i32(const int32_t* slots, const int32_t* own, int nslots, int own_slot,
+                          int64_t slot_stride, const float* row_scale, const float* col_scale,
+                          const float* bias, const void* add, void* y, int64_t rows, int64_t cols,
+                          ltm_dtype dt, cudaStream_t stream) {
+  LTM_REQUIRE(dt != LTM_DTYPE_F32, "slot sums are for 16-bit rows");
+  LTM_REQUIRE(cols % 4 == 0 && slot_stride % 4 == 0, "slot rows must be whole 16-byte units");
+  auto al = [](const void* q, unsigned m) { return (reinterpret_cast<uintptr_t>(q) & m) == 0; };
+  LTM_REQUIRE(al(slots, 15) && al(own, 15) && al(y, 7) && (!add || al(add, 7)) &&
+                  (!col_scale || al(col_scale, 15)) && (!bias || al(bias, 15)),
+              "slot buffers misaligned");
+  const int64_t n = rows * (cols / 4);
+  if (n == 0) return;
+  dispatch_dtype(dt, [&](auto tag) {
+    using T = decltype(tag);
+    if constexpr (sizeof(T) == 2)
+      sum_slots_i32_kernel<T><<<grid_for(n), 256, 0, stream>>>(
+          reinterpret_cast<const int4*>(slots), reinterpret_cast<const int4*>(own), nslots,
+          own_slot, slot_stride / 4, row_scale, reinterpret_cast<const float4*>(col_scale),
+          reinterpret_cast<const float4*>(bias), static_cast<const T*>(add), static_cast<T*>(y),
+          rows, cols / 4);
+  });
+  check_launch("sum_slots_i32_kernel", stream);
 }
 
 // ------------------------------------------------------------ quantized W --
@@ -170,7 +294,7 @@ constexpr int64_t kW4DequantM = 1024;
 
 void QLinear::run(const void* a_act, const int8_t* aq, const float* as, int64_t M, int mode,
                   ltm_dtype dt, Epilogue ep, cudaStream_t stream, DevBuf* wdq) const {
-  ep.bias = bias.as<float>();
+  ep.bias = apply_bias ? bias.as<float>() : nullptr;
   if (scheme == LTM_SCHEME_W8A8) {
     ep.row_scale = as;
     ep.col_scale = s8.as<float>();
@@ -222,6 +346,7 @@ struct ltm_block {
   DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, spm, y, zq, zs, z,
       u, uq, us, amax;
   DevBuf sploc;  // sequence parallel: this rank's rows of s | m [2, T/tp, H]
+  DevBuf spr;    // sequence parallel: the ranks' partials of those rows [2, tp, T/tp, H]
   MemoryWriteState mw;
   // decode: K_M | V_M kept resident between steps (kvm_fresh: kvmb holds them
   // for the current bank), the state row of the write and its projection,
@@ -465,10 +590,19 @@ struct ltm_block {
   // Collectives of the overlapped sequence-parallel forward run on a stream
   // of the block's own (every NCCL call of the block on one stream, in one
   // order on every rank), ordered against the caller's stream by events.
-  // -1: automatic (overlap from 4 ranks on; at 2 ranks half of each
-  // collective stays exposed and the SM reserve costs as much as the rest
-  // saves, measured); 0 / 1: set by ltm_block_set_overlap
+  // -1 (default) and 0: the collectives on the caller's stream, one per
+  // phase; 1: overlapped (set by ltm_block_set_overlap).  The overlapped form
+  // splits every GEMM into tp launches and reserves SMs for the collectives,
+  // which cost more than the hidden transfers saved at 2 and at 8 ranks
+  // (measured), so it is not the default.
   int overlap = -1;
+  // row-parallel reductions of the sequence-parallel forward: 0 = partial
+  // sums in the activation type, summed in fp32 at the row owner (one
+  // rounding); 1 = exact (W8A8): int32 accumulators exchanged and summed,
+  // then the unsplit GEMM's epilogue, so the output equals the single-GPU
+  // block's bit for bit at twice the bytes of those exchanges
+  int tp_reduce = 0;
+  DevBuf spi, spri;  // exact reduction: int32 partials [2, T, H] and the ranks' slots
   int comm_sms = 16;  // SMs the chunked GEMMs leave to the concurrent collectives
   cudaStream_t comm_st = nullptr;
   std::vector<cudaEvent_t> evs;
@@ -529,9 +663,16 @@ struct ltm_block {
     last_T = T;
     const size_t a = act_bytes();
     sploc.ensure(static_cast<size_t>(2 * Tr) * H * a);
+    if (tp_reduce == 1 && q.scheme == LTM_SCHEME_W8A8) {
+      spi.ensure(static_cast<size_t>(2 * T) * H * sizeof(int32_t));
+      spri.ensure(static_cast<size_t>(2 * T) * H * sizeof(int32_t));
+    } else {
+      spr.ensure(static_cast<size_t>(2 * T) * H * a);
+    }
     if (cfg.use_rotary) ensure_rope(S);
     const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
-    const bool ovl = (overlap < 0 ? tp >= 4 : overlap != 0) && w8a8;
+    const bool ovl = overlap > 0 && w8a8;
+    const bool exact = tp_reduce == 1 && w8a8;
     ensure_comm_stream(2 * tp + 8);
     cudaStream_t ns = ovl ? comm_st : st;  // the stream of the collectives
     const int kA = 8, kB = 8 + tp;    // per-root events of the two chunked phases
@@ -608,29 +749,53 @@ struct ltm_block {
       launch_rowwise_int8_amax(os.ptr, dt, T, Hl, amx, osq.as<int8_t>(), oss.as<float>(), st);
       launch_rowwise_int8_amax(om_.ptr, dt, T, Hl, amx + T, omq.as<int8_t>(), oms.as<float>(), st);
     }
+    // Every rank's partial of this rank's rows lands in a slot of sr / mr
+    // (all-to-all) and the owner sums the slots in fp32 and rounds once, so
+    // the row sums carry one rounding whatever the rank count (a ring
+    // reduce-scatter in 16 bits rounds after every hop).
+    // Exact mode exchanges the int32 accumulators instead (esz 4).
+    const size_t esz = exact ? sizeof(int32_t) : a;
+    void* sp5 = exact ? spi.ptr : sp;  // partials of s | m, all rows
+    void* mp5 = static_cast<char*>(sp5) + T * H * esz;
+    void* sr = exact ? spri.ptr : spr.ptr;
+    void* mr = static_cast<char*>(sr) + T * H * esz;
     if (ovl) {
       ScopedSmReserve reserve(comm_sms);
       for (int j = 0; j < tp; ++j) {
-        out_rows(o, osq.as<int8_t>(), oss.as<float>(), Hl, j * Tr, Tr, sp, st);
-        out_rows(om, omq.as<int8_t>(), oms.as<float>(), Hl, j * Tr, Tr, mp, st);
+        out_rows(o, osq.as<int8_t>(), oss.as<float>(), Hl, j * Tr, Tr, sp5, st, exact);
+        out_rows(om, omq.as<int8_t>(), oms.as<float>(), Hl, j * Tr, Tr, mp5, st, exact);
         order(st, comm_st, kB + j);
         comm_group_start();
-        comm_reduce(comm, static_cast<char*>(sp) + j * Tr * H * a, s_loc, Tr * H, dt, j, comm_st);
-        comm_reduce(comm, static_cast<char*>(mp) + j * Tr * H * a, m_loc, Tr * H, dt, j, comm_st);
+        comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, j, comm_st);
+        comm_send_recv_slots(comm, mp5, mr, Tr * H * esz, j, comm_st);
         comm_group_end(nullptr, comm_st);
       }
       order(comm_st, st, 3);
     } else {
       Epilogue ep;
-      ep.out = sp;
+      ep.out = sp5;
       ep.ldo = H;
-      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
-      ep.out = mp;
-      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
+      const int mode = exact ? kEpiAccI32 : kEpiPlain;
+      o.run(os.ptr, osq.as<int8_t>(), oss.as<float>(), T, mode, dt, ep, st, &wdq);
+      ep.out = mp5;
+      om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, mode, dt, ep, st, &wdq);
       comm_group_start();
-      comm_reduce_scatter(comm, sp, s_loc, Tr * H, dt, st);
-      comm_reduce_scatter(comm, mp, m_loc, Tr * H, dt, st);
-      comm_group_end("nccl_reduce_scatter", st);
+      comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, -1, st);
+      comm_send_recv_slots(comm, mp5, mr, Tr * H * esz, -1, st);
+      comm_group_end("nccl_send_recv", st);
+    }
+    if (exact) {
+      launch_sum_slots_i32(static_cast<const int32_t*>(sr), static_cast<const int32_t*>(sp5) + r0 * H,
+                           tp, tpr, Tr * H, oss.as<float>() + r0, o.s8.as<float>(),
+                           o.bias.as<float>(), nullptr, s_loc, Tr, H, dt, st);
+      launch_sum_slots_i32(static_cast<const int32_t*>(mr), static_cast<const int32_t*>(mp5) + r0 * H,
+                           tp, tpr, Tr * H, oms.as<float>() + r0, om.s8.as<float>(),
+                           om.bias.as<float>(), nullptr, m_loc, Tr, H, dt, st);
+    } else {
+      launch_sum_slots(sr, static_cast<char*>(sp) + r0 * H * a, tp, tpr, Tr * H, nullptr, s_loc,
+                       Tr * H, dt, st);
+      launch_sum_slots(mr, static_cast<char*>(mp) + r0 * H * a, tp, tpr, Tr * H, nullptr, m_loc,
+                       Tr * H, dt, st);
     }
     // 6. gate and gated integration of the local rows
     if (cfg.use_memory_gating) {
@@ -702,19 +867,27 @@ struct ltm_block {
     if (ovl) {
       ScopedSmReserve reserve(comm_sms);
       for (int j = 0; j < tp; ++j) {
-        out_rows(w2, uq.as<int8_t>(), us.as<float>(), Fl, j * Tr, Tr, sp, st);
+        out_rows(w2, uq.as<int8_t>(), us.as<float>(), Fl, j * Tr, Tr, sp5, st, exact);
         order(st, comm_st, kB + j);
-        comm_reduce(comm, static_cast<char*>(sp) + j * Tr * H * a, out_loc, Tr * H, dt, j, comm_st);
+        comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, j, comm_st);
       }
       order(comm_st, st, 7);
     } else {
       Epilogue ep;
-      ep.out = sp;
+      ep.out = sp5;
       ep.ldo = H;
-      w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, kEpiPlain, dt, ep, st, &wdq);
-      comm_reduce_scatter(comm, sp, out_loc, Tr * H, dt, st);
+      w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, exact ? kEpiAccI32 : kEpiPlain, dt, ep, st,
+             &wdq);
+      comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, -1, st);
     }
-    launch_add3(out_loc, y.ptr, nullptr, out_loc, Tr * H, dt, st);
+    // the slots' sum plus the residual, rounded once
+    if (exact)
+      launch_sum_slots_i32(static_cast<const int32_t*>(sr), static_cast<const int32_t*>(sp5) + r0 * H,
+                           tp, tpr, Tr * H, us.as<float>() + r0, w2.s8.as<float>(),
+                           w2.bias.as<float>(), y.ptr, out_loc, Tr, H, dt, st);
+    else
+      launch_sum_slots(sr, static_cast<char*>(sp) + r0 * H * a, tp, tpr, Tr * H, y.ptr, out_loc,
+                       Tr * H, dt, st);
     // 9. memory write: column sums of the local rows, summed over the ranks
     if (q.memory_write && cfg.use_memory_gating) {
       order(st, ns, 1);
@@ -745,11 +918,12 @@ struct ltm_block {
   // Row-parallel partial sums [M, H] of rows [row0, row0 + M) (int8 inputs
   // of width K, per-token scales) into out rows [row0, row0 + M).
   void out_rows(const QLinear& lin, const int8_t* aq, const float* as, int64_t K, int64_t row0,
-                int64_t M, void* out, cudaStream_t st) {
+                int64_t M, void* out, cudaStream_t st, bool acc_i32 = false) {
     Epilogue ep;
-    ep.out = static_cast<char*>(out) + row0 * H * act_bytes();
+    ep.out = static_cast<char*>(out) + row0 * H * (acc_i32 ? sizeof(int32_t) : act_bytes());
     ep.ldo = H;
-    lin.run(nullptr, aq + row0 * K, as + row0, M, kEpiPlain, dt, ep, st, &wdq);
+    lin.run(nullptr, aq + row0 * K, as + row0, M, acc_i32 ? kEpiAccI32 : kEpiPlain, dt, ep, st,
+            &wdq);
   }
 
   // Memory write of a caller-given state (fp32 [H]) with slot weights from
@@ -878,11 +1052,12 @@ std::vector<StateSection> block_state(ltm_block* b, bool weights, bool bank, boo
     if (weights) {
       shape_linear(b->qkvm, sc, 4 * Hl, H, ub);
       shape_linear(b->kvm, sc, 2 * Hl, H, ub);
-      shape_linear(b->o, sc, H, tp1 ? H : Hl, ub && (tp1 || lead));
-      shape_linear(b->om, sc, H, tp1 ? H : Hl, ub && (tp1 || lead));
+      shape_linear(b->o, sc, H, tp1 ? H : Hl, ub);
+      shape_linear(b->om, sc, H, tp1 ? H : Hl, ub);
       shape_linear(b->g, sc, H, H, ub);
       shape_linear(b->w1, sc, Fl, H, ub);
-      shape_linear(b->w2, sc, H, tp1 ? F : Fl, ub && (tp1 || lead));
+      shape_linear(b->w2, sc, H, tp1 ? F : Fl, ub);
+      b->o.apply_bias = b->om.apply_bias = b->w2.apply_bias = tp1 || lead;
       if (b->cfg.use_layer_norm)
         for (DevBuf* d : {&b->ln1_g, &b->ln1_b, &b->ln2_g, &b->ln2_b}) d->ensure(H * sizeof(float));
     }
@@ -1014,9 +1189,12 @@ void load_block(ltm_block* b, const ltm_block_weights* w, cudaStream_t st) {
     b->om.load(b->q, w->w_om, ub ? w->b_om : nullptr, H, H, st);
     b->w2.load(b->q, w->w_2, ub ? w->b_2 : nullptr, H, F, st);
   } else {  // row-parallel: input columns of this rank's heads / FFN columns
-    b->o.load_cols(b->q, w->w_o, (ub && lead) ? w->b_o : nullptr, H, H, hr0, Hl, st);
-    b->om.load_cols(b->q, w->w_om, (ub && lead) ? w->b_om : nullptr, H, H, hr0, Hl, st);
-    b->w2.load_cols(b->q, w->w_2, (ub && lead) ? w->b_2 : nullptr, H, F, fr0, Fl, st);
+    // every rank keeps the full biases (the exact reduction adds them at
+    // the row owner); the partial sums carry them on the first rank only
+    b->o.load_cols(b->q, w->w_o, ub ? w->b_o : nullptr, H, H, hr0, Hl, st);
+    b->om.load_cols(b->q, w->w_om, ub ? w->b_om : nullptr, H, H, hr0, Hl, st);
+    b->w2.load_cols(b->q, w->w_2, ub ? w->b_2 : nullptr, H, F, fr0, Fl, st);
+    b->o.apply_bias = b->om.apply_bias = b->w2.apply_bias = lead;
   }
   b->g.load(b->q, w->w_g, ub ? w->b_g : nullptr, H, H, st);
   b->w1.load(b->q, w->w_1 + fr0 * H, ub ? w->b_1 + fr0 : nullptr, Fl, H, st);
@@ -1190,6 +1368,16 @@ extern "C" ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, 
     LTM_REQUIRE(blk->dt != LTM_DTYPE_F32, "sequence parallelism needs f16 or bf16 activations");
     DeviceGuard g(blk->device);
     blk->forward_sp(x_local, y_local, B, S, as_stream(stream));
+  });
+}
+
+extern "C" ltm_status ltm_block_set_tp_reduction(ltm_block* blk, int mode) {
+  return guarded([&] {
+    LTM_REQUIRE(blk, "block is NULL");
+    LTM_REQUIRE(mode == LTM_TP_REDUCE_ACT || mode == LTM_TP_REDUCE_EXACT, "unknown reduction mode");
+    LTM_REQUIRE(mode == LTM_TP_REDUCE_ACT || blk->q.scheme == LTM_SCHEME_W8A8,
+                "the exact reduction needs the W8A8 scheme");
+    blk->tp_reduce = mode;
   });
 }
 

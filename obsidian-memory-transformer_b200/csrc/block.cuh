@@ -33,6 +33,26 @@ void comm_broadcast_bytes(ltm_comm* c, void* buf, size_t bytes, int root, cudaSt
 // Sum of every rank's send into recv on rank root (recv unused elsewhere).
 void comm_reduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dtype dt, int root,
                  cudaStream_t st);
+// Rank-to-rank exchange of row blocks (all-to-all, no reduction): for every
+// peer j, block j of `send` (`bytes` bytes) goes to rank j and rank j's
+// block for this rank lands in slot j of `recv` ([nranks, bytes]; this
+// rank's own slot is left untouched).  root >= 0 restricts it to the
+// transfers into rank `root` (the blocks of one row owner).
+void comm_send_recv_slots(ltm_comm* c, const void* send, void* recv, size_t bytes, int root,
+                          cudaStream_t st);
+// y[i] = sum over slots j of (j == own ? own[i] : slots[j * slot_stride + i])
+// (+ add[i]), summed in fp32 in slot order and rounded once (16-bit types).
+void launch_sum_slots(const void* slots, const void* own, int nslots, int own_slot,
+                      int64_t slot_stride, const void* add, void* y, int64_t n, ltm_dtype dt,
+                      cudaStream_t stream);
+// Rows [rows, cols] of int32 GEMM accumulators summed over the ranks' slots
+// (exact), then the W8A8 epilogue of the unsplit GEMM: y = round(fma(acc *
+// row_scale[r], col_scale[c], bias[c]) (+ add[r, c])), the arithmetic of the
+// tensor-core epilogue, so the rows equal the single-GPU GEMM's bit for bit.
+void launch_sum_slots_i32(const int32_t* slots, const int32_t* own, int nslots, int own_slot,
+                          int64_t slot_stride, const float* row_scale, const float* col_scale,
+                          const float* bias, const void* add, void* y, int64_t rows, int64_t cols,
+                          ltm_dtype dt, cudaStream_t stream);
 // NCCL group brackets: the collectives between them launch as one (at the
 // end, which marks them for the kernel timer under `what` on stream st).
 void comm_group_start();
@@ -59,6 +79,9 @@ struct QLinear {
   int64_t N = 0, K = 0;
   int scheme = LTM_SCHEME_W8A8;
   DevBuf q8, s8, q4, s4, z4, bias;
+  // false: run() leaves the bias out (the row-parallel shards of ranks other
+  // than the first, whose partial sums are added to the first rank's)
+  bool apply_bias = true;
   void load(const ltm_quant_config& q, const float* w_host, const float* b_host, int64_t n,
             int64_t k, cudaStream_t stream);
   // Input columns [c0, c0 + nc) of a host [n, k] weight with the unsplit

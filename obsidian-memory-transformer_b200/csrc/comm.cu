@@ -41,6 +41,8 @@ struct NcclApi {
                             cudaStream_t) = nullptr;
   ncclResult_t (*reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, int, ncclComm_t,
                          cudaStream_t) = nullptr;
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
@@ -64,13 +66,15 @@ const NcclApi& nccl() {
         reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
     api.broadcast = reinterpret_cast<decltype(api.broadcast)>(dlsym(h, "ncclBroadcast"));
     api.reduce = reinterpret_cast<decltype(api.reduce)>(dlsym(h, "ncclReduce"));
+    api.send = reinterpret_cast<decltype(api.send)>(dlsym(h, "ncclSend"));
+    api.recv = reinterpret_cast<decltype(api.recv)>(dlsym(h, "ncclRecv"));
     api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
     api.get_version = reinterpret_cast<decltype(api.get_version)>(dlsym(h, "ncclGetVersion"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce &&
              api.all_gather && api.reduce_scatter && api.broadcast && api.reduce &&
-             api.group_start && api.group_end &&
+             api.send && api.recv && api.group_start && api.group_end &&
              api.error_string;
   });
   if (!api.ok) {
@@ -146,6 +150,25 @@ void comm_reduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dt
                            static_cast<ncclComm_t>(c->handle), st),
              "ncclReduce");
   note_collective("nccl_reduce", st);
+}
+
+void comm_send_recv_slots(ltm_comm* c, const void* send, void* recv, size_t bytes, int root,
+                          cudaStream_t st) {
+  LTM_REQUIRE(c != nullptr, "NULL communicator");
+  if (bytes == 0) return;
+  const ncclComm_t h = static_cast<ncclComm_t>(c->handle);
+  comm_group_start();
+  for (int j = 0; j < c->nranks; ++j) {
+    if (j == c->rank) continue;
+    if (root < 0 || root == j)  // this rank's rows of j's block go to j
+      nccl_check(nccl().send(static_cast<const char*>(send) + j * bytes, bytes, ncclInt8, j, h, st),
+                 "ncclSend");
+    if (root < 0 || root == c->rank)  // j's partial of this rank's rows into slot j
+      nccl_check(nccl().recv(static_cast<char*>(recv) + j * bytes, bytes, ncclInt8, j, h, st),
+                 "ncclRecv");
+  }
+  comm_group_end(nullptr, st);
+  note_collective("nccl_send_recv", st);
 }
 
 void comm_group_start() {

@@ -27,6 +27,8 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 EPI_NONE, EPI_GELU, EPI_SIGMOID = 0, 1, 2
 # ltm_scheme
 SCHEME_W8A32, SCHEME_W8A8, SCHEME_W4A16 = 0, 1, 2
+# ltm_tp_reduction
+TP_REDUCE_ACT, TP_REDUCE_EXACT = 0, 1
 
 
 class LtmError(RuntimeError):
@@ -116,6 +118,7 @@ def _declare(L):
         "ltm_block_forward_with_cache": ([vp, vp, vp, ci, ci, vp, vp, i64, vp], ci),
         "ltm_block_forward_sp": ([vp, vp, vp, ci, ci, vp], ci),
         "ltm_block_set_overlap": ([vp, ci, ci], ci),
+        "ltm_block_set_tp_reduction": ([vp, ci], ci),
         "ltm_calibrator_create": ([ci, C.c_float, ci, C.POINTER(vp)], ci),
         "ltm_calibrator_collect": ([vp, vp, ci, i64, vp], ci),
         "ltm_calibrator_compute_range": ([vp, C.POINTER(C.c_float), C.POINTER(C.c_float), vp],
@@ -640,9 +643,16 @@ class TitanBlock:
 
     def set_overlap(self, overlap=True, comm_sms: int = 16) -> None:
         """Chunked collectives overlapping the GEMMs in forward_sp (W8A8):
-        True, False, or None for the library's choice (on from 4 ranks)."""
+        True, False, or None for the library's default (off)."""
         _check(lib().ltm_block_set_overlap(self._h, -1 if overlap is None else int(overlap),
                                            comm_sms))
+
+    def set_tp_reduction(self, exact: bool = True) -> None:
+        """Row-parallel reductions of forward_sp: exact (W8A8: int32
+        accumulators summed exactly, the result equal to the single-GPU
+        block's) or, with exact=False, partial sums in the activation type."""
+        _check(lib().ltm_block_set_tp_reduction(self._h,
+                                                TP_REDUCE_EXACT if exact else TP_REDUCE_ACT))
 
     def _check_caches(self, k_cache, v_cache, B):
         heads = self.config.num_heads // (self._comm.nranks if self._comm is not None else 1)

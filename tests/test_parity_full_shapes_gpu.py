@@ -166,7 +166,9 @@ def _cat(*a):
 
 @pytest.mark.parametrize("scheme,H,nh,F,S", [("w8a8", 4096, 32, 11008, 256),
                                              ("w4a16", 4096, 32, 11008, 256),
-                                             ("w8a8", 8192, 64, 28672, 128)])
+                                             ("w8a8", 8192, 64, 28672, 128),
+                                             # the tensor-parallel tests' FFN-8192 block
+                                             ("w8a8", 512, 8, 8192, 96)])
 def test_wide_block_stage_by_stage(ltm, orc, scheme, H, nh, F, S):
     import torch
     from ltm_b200 import synthetic
