@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(256) rowwise_int8_kernel(const T* __restrict__
 // current row is reduced and quantized.  WPR warps share one row (WPR = 1:
 // every warp owns its rows; WPR = 4: a 128-thread CTA owns a row and reduces
 // the row max through shared memory); lane l of the row group holds the
-// 16-byte vectors l, l + 32*WPR, ... (NV of them).
+// 16-byte vectors l, l + 32*WPR, ... (NV of them).  WPR = 8: a 256-thread
+// CTA per row.
 template <class T, int NV>
 __device__ __forceinline__ void load_row_vecs(const T* __restrict__ x, int64_t row, int64_t K,
                                               int nvec, int gl, int stride, uint4 (&raw)[NV]) {
@@ -98,7 +99,7 @@ __device__ __forceinline__ void load_row_vecs(const T* __restrict__ x, int64_t r
 }
 
 template <class T, int NV, int WPR>
-__global__ void __launch_bounds__(WPR == 1 ? 256 : 128) rowwise_int8_pipe_kernel(
+__global__ void __launch_bounds__(WPR == 1 ? 256 : 32 * WPR) rowwise_int8_pipe_kernel(
     const T* __restrict__ x, int64_t rows, int64_t K, int8_t* __restrict__ q,
     float* __restrict__ scales) {
   constexpr int V = Vec16<T>::N;
@@ -309,6 +310,13 @@ void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, i
       else if (nv <= 2) warp_launch(std::integral_constant<int, 2>{});
       else if (nv <= 3) warp_launch(std::integral_constant<int, 3>{});
       else warp_launch(std::integral_constant<int, 4>{});
+    } else if (vec && nvec > 4 * 128 && nvec <= 4 * 256) {
+      // eight warps per row (rows of 4096-8192 16-bit values): twice the
+      // throughput of four warps with eight vectors each at 8192 (measured,
+      // same codes)
+      auto kern = rowwise_int8_pipe_kernel<T, 4, 8>;
+      const int grid = persistent_grid(kern, 256, 0, rows);
+      kern<<<grid, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
     } else if (vec && nvec <= 8 * 128) {
       const int64_t nv = (nvec + 127) / 128;
       if (nv <= 2) cta_launch(std::integral_constant<int, 2>{});

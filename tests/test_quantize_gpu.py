@@ -50,7 +50,9 @@ def test_int8_rounding_ties_and_clamp(ltm, orc):
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
-@pytest.mark.parametrize("K", [768, 3072, 12288, 28672, 49152])  # from 12288: the two-pass kernel
+# 4096-8192 (16-bit) / 2048-4096 (fp32): eight warps per row; from 12288
+# (16-bit): the two-pass kernel
+@pytest.mark.parametrize("K", [768, 3072, 4096, 6144, 8192, 12288, 28672, 49152])
 def test_act_per_token_rounding_ties(ltm, orc, dt, K):
     """Per-token activation codes at exact .5 boundaries (row absmax 127, so
     s = 1 and every k + 0.5 is a tie) and just off them: the warp quantizer's
