@@ -475,13 +475,11 @@ LTM_API ltm_status ltm_block_forward_sp(ltm_block* blk, const void* x_local, voi
  * rank on a stream of the block's own, each overlapping the GEMM of another
  * rank's rows, whose grids leave comm_sms SMs (default 16) to the
  * collectives.  overlap = 1: on; 0 or -1 (default): the plain collectives on
- * the caller's stream (measured faster at 2 and 8 ranks).  The row-parallel
- * partial sums reach their rows' owner as one slot per rank (all-to-all) and
- * are summed there in fp32 with one rounding, in either mode. */
+ * the caller's stream (measured faster at 2 and 8 ranks). */
 LTM_API ltm_status ltm_block_set_overlap(ltm_block* blk, int overlap, int comm_sms);
 /* Row-parallel reductions of ltm_block_forward_sp.  LTM_TP_REDUCE_ACT
- * (default): the ranks' partial sums in the activation type, summed in fp32
- * at the rows' owner and rounded once.  LTM_TP_REDUCE_EXACT (W8A8 only): the
+ * (default): the ranks' partial sums in the activation type, reduce-scattered
+ * by NCCL (16-bit adds along the way).  LTM_TP_REDUCE_EXACT (W8A8 only): the
  * int32 GEMM accumulators are exchanged and summed exactly and the unsplit
  * GEMM's epilogue (scales, bias, residual) is applied at the owner, so
  * forward_sp's rows equal the single-GPU block's bit for bit (the memory-bank

@@ -51,41 +51,6 @@ __global__ void add3_kernel(const T* __restrict__ a, const T* __restrict__ b,
     y[i] = from_f32<T>(to_f32(a[i]) + to_f32(b[i]) + (c ? to_f32(c[i]) : 0.0f));
 }
 
-// 16-bit rows summed over the ranks' partial slots (8 values per 16-byte
-// load, every slot's load in flight before the adds).
-template <class T>
-__global__ void sum_slots_kernel(const uint4* __restrict__ slots, const uint4* __restrict__ own,
-                                 int nslots, int own_slot, int64_t stride8,
-                                 const uint4* __restrict__ add, uint4* __restrict__ y, int64_t n8) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-    uint4 v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j < nslots) v[j] = __ldcs(j == own_slot ? own + i : slots + j * stride8 + i);
-    for (int j = 0; j < nslots; ++j) {
-      const uint4 w = j < 8 ? v[j] : __ldcs(j == own_slot ? own + i : slots + j * stride8 + i);
-      const T* e16 = reinterpret_cast<const T*>(&w);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += to_f32(e16[e]);
-    }
-    if (add) {
-      const uint4 w = __ldg(add + i);
-      const T* e16 = reinterpret_cast<const T*>(&w);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += to_f32(e16[e]);
-    }
-    uint4 o;
-    T* o16 = reinterpret_cast<T*>(&o);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o16[e] = from_f32<T>(acc[e]);
-    y[i] = o;
-  }
-}
-
 // int32 accumulator rows summed over the ranks' slots (4 columns per
 // thread), then the tensor-core epilogue's arithmetic.
 template <class T>
@@ -166,25 +131,6 @@ void launch_add3(const void* a, const void* b, const void* c, void* y, int64_t n
                                                     static_cast<const T*>(c), static_cast<T*>(y), n);
   });
   check_launch("add3_kernel", stream);
-}
-
-void launch_sum_slots(const void* slots, const void* own, int nslots, int own_slot,
-                      int64_t slot_stride, const void* add, void* y, int64_t n, ltm_dtype dt,
-                      cudaStream_t stream) {
-  LTM_REQUIRE(dt != LTM_DTYPE_F32, "slot sums are for 16-bit rows");
-  LTM_REQUIRE(n % 8 == 0 && slot_stride % 8 == 0, "slot rows must be whole 16-byte units");
-  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-  LTM_REQUIRE(al(slots) && al(own) && al(y) && (!add || al(add)), "slot buffers must be 16-byte aligned");
-  if (n == 0) return;
-  const int64_t n8 = n / 8;
-  dispatch_dtype(dt, [&](auto tag) {
-    using T = decltype(tag);
-    if constexpr (sizeof(T) == 2)
-      sum_slots_kernel<T><<<grid_for(n8), 256, 0, stream>>>(
-          static_cast<const uint4*>(slots), static_cast<const uint4*>(own), nslots, own_slot,
-          slot_stride / 8, static_cast<const uint4*>(add), static_cast<uint4*>(y), n8);
-  });
-  check_launch("sum_slots_kernel", stream);
 }
 
 void launch_sum_slots_i32(const int32_t* slots, const int32_t* own, int nslots, int own_slot,
@@ -346,7 +292,6 @@ struct ltm_block {
   DevBuf hq, hs, xq, xs, h, qkv, kvmb, mq, ms, os, om_, osq, oss, omq, oms, spm, y, zq, zs, z,
       u, uq, us, amax;
   DevBuf sploc;  // sequence parallel: this rank's rows of s | m [2, T/tp, H]
-  DevBuf spr;    // sequence parallel: the ranks' partials of those rows [2, tp, T/tp, H]
   MemoryWriteState mw;
   // decode: K_M | V_M kept resident between steps (kvm_fresh: kvmb holds them
   // for the current bank), the state row of the write and its projection,
@@ -597,8 +542,8 @@ struct ltm_block {
   // (measured), so it is not the default.
   int overlap = -1;
   // row-parallel reductions of the sequence-parallel forward: 0 = partial
-  // sums in the activation type, summed in fp32 at the row owner (one
-  // rounding); 1 = exact (W8A8): int32 accumulators exchanged and summed,
+  // sums in the activation type, reduce-scattered by NCCL; 1 = exact (W8A8):
+  // int32 accumulators exchanged rank to rank and summed at the row owner,
   // then the unsplit GEMM's epilogue, so the output equals the single-GPU
   // block's bit for bit at twice the bytes of those exchanges
   int tp_reduce = 0;
@@ -666,8 +611,6 @@ struct ltm_block {
     if (tp_reduce == 1 && q.scheme == LTM_SCHEME_W8A8) {
       spi.ensure(static_cast<size_t>(2 * T) * H * sizeof(int32_t));
       spri.ensure(static_cast<size_t>(2 * T) * H * sizeof(int32_t));
-    } else {
-      spr.ensure(static_cast<size_t>(2 * T) * H * a);
     }
     if (cfg.use_rotary) ensure_rope(S);
     const bool w8a8 = q.scheme == LTM_SCHEME_W8A8;
@@ -749,15 +692,15 @@ struct ltm_block {
       launch_rowwise_int8_amax(os.ptr, dt, T, Hl, amx, osq.as<int8_t>(), oss.as<float>(), st);
       launch_rowwise_int8_amax(om_.ptr, dt, T, Hl, amx + T, omq.as<int8_t>(), oms.as<float>(), st);
     }
-    // Every rank's partial of this rank's rows lands in a slot of sr / mr
-    // (all-to-all) and the owner sums the slots in fp32 and rounds once, so
-    // the row sums carry one rounding whatever the rank count (a ring
-    // reduce-scatter in 16 bits rounds after every hop).
-    // Exact mode exchanges the int32 accumulators instead (esz 4).
+    // Activation-type mode: the partial sums of all rows are reduce-scattered
+    // to the rows' owners (NCCL, in the switch where NVLS is available).
+    // Exact mode: every rank's int32 accumulators of this rank's rows land in
+    // a slot of sr / mr (all-to-all), summed exactly by the owner, which then
+    // applies the unsplit GEMM's epilogue.
     const size_t esz = exact ? sizeof(int32_t) : a;
     void* sp5 = exact ? spi.ptr : sp;  // partials of s | m, all rows
     void* mp5 = static_cast<char*>(sp5) + T * H * esz;
-    void* sr = exact ? spri.ptr : spr.ptr;
+    void* sr = spri.ptr;  // exact mode only
     void* mr = static_cast<char*>(sr) + T * H * esz;
     if (ovl) {
       ScopedSmReserve reserve(comm_sms);
@@ -766,8 +709,13 @@ struct ltm_block {
         out_rows(om, omq.as<int8_t>(), oms.as<float>(), Hl, j * Tr, Tr, mp5, st, exact);
         order(st, comm_st, kB + j);
         comm_group_start();
-        comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, j, comm_st);
-        comm_send_recv_slots(comm, mp5, mr, Tr * H * esz, j, comm_st);
+        if (exact) {
+          comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, j, comm_st);
+          comm_send_recv_slots(comm, mp5, mr, Tr * H * esz, j, comm_st);
+        } else {
+          comm_reduce(comm, static_cast<char*>(sp) + j * Tr * H * a, s_loc, Tr * H, dt, j, comm_st);
+          comm_reduce(comm, static_cast<char*>(mp) + j * Tr * H * a, m_loc, Tr * H, dt, j, comm_st);
+        }
         comm_group_end(nullptr, comm_st);
       }
       order(comm_st, st, 3);
@@ -780,9 +728,14 @@ struct ltm_block {
       ep.out = mp5;
       om.run(om_.ptr, omq.as<int8_t>(), oms.as<float>(), T, mode, dt, ep, st, &wdq);
       comm_group_start();
-      comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, -1, st);
-      comm_send_recv_slots(comm, mp5, mr, Tr * H * esz, -1, st);
-      comm_group_end("nccl_send_recv", st);
+      if (exact) {
+        comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, -1, st);
+        comm_send_recv_slots(comm, mp5, mr, Tr * H * esz, -1, st);
+      } else {
+        comm_reduce_scatter(comm, sp, s_loc, Tr * H, dt, st);
+        comm_reduce_scatter(comm, mp, m_loc, Tr * H, dt, st);
+      }
+      comm_group_end(exact ? "nccl_send_recv" : "nccl_reduce_scatter", st);
     }
     if (exact) {
       launch_sum_slots_i32(static_cast<const int32_t*>(sr), static_cast<const int32_t*>(sp5) + r0 * H,
@@ -791,11 +744,6 @@ struct ltm_block {
       launch_sum_slots_i32(static_cast<const int32_t*>(mr), static_cast<const int32_t*>(mp5) + r0 * H,
                            tp, tpr, Tr * H, oms.as<float>() + r0, om.s8.as<float>(),
                            om.bias.as<float>(), nullptr, m_loc, Tr, H, dt, st);
-    } else {
-      launch_sum_slots(sr, static_cast<char*>(sp) + r0 * H * a, tp, tpr, Tr * H, nullptr, s_loc,
-                       Tr * H, dt, st);
-      launch_sum_slots(mr, static_cast<char*>(mp) + r0 * H * a, tp, tpr, Tr * H, nullptr, m_loc,
-                       Tr * H, dt, st);
     }
     // 6. gate and gated integration of the local rows
     if (cfg.use_memory_gating) {
@@ -869,7 +817,11 @@ struct ltm_block {
       for (int j = 0; j < tp; ++j) {
         out_rows(w2, uq.as<int8_t>(), us.as<float>(), Fl, j * Tr, Tr, sp5, st, exact);
         order(st, comm_st, kB + j);
-        comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, j, comm_st);
+        if (exact)
+          comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, j, comm_st);
+        else
+          comm_reduce(comm, static_cast<char*>(sp) + j * Tr * H * a, out_loc, Tr * H, dt, j,
+                      comm_st);
       }
       order(comm_st, st, 7);
     } else {
@@ -878,16 +830,17 @@ struct ltm_block {
       ep.ldo = H;
       w2.run(u.ptr, uq.as<int8_t>(), us.as<float>(), T, exact ? kEpiAccI32 : kEpiPlain, dt, ep, st,
              &wdq);
-      comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, -1, st);
+      if (exact)
+        comm_send_recv_slots(comm, sp5, sr, Tr * H * esz, -1, st);
+      else
+        comm_reduce_scatter(comm, sp, out_loc, Tr * H, dt, st);
     }
-    // the slots' sum plus the residual, rounded once
-    if (exact)
+    if (exact)  // the slots' exact sum, the epilogue and the residual, rounded once
       launch_sum_slots_i32(static_cast<const int32_t*>(sr), static_cast<const int32_t*>(sp5) + r0 * H,
                            tp, tpr, Tr * H, us.as<float>() + r0, w2.s8.as<float>(),
                            w2.bias.as<float>(), y.ptr, out_loc, Tr, H, dt, st);
-    else
-      launch_sum_slots(sr, static_cast<char*>(sp) + r0 * H * a, tp, tpr, Tr * H, y.ptr, out_loc,
-                       Tr * H, dt, st);
+    else  // the owner adds its rows' residual
+      launch_add3(out_loc, y.ptr, nullptr, out_loc, Tr * H, dt, st);
     // 9. memory write: column sums of the local rows, summed over the ranks
     if (q.memory_write && cfg.use_memory_gating) {
       order(st, ns, 1);

@@ -40,11 +40,6 @@ void comm_reduce(ltm_comm* c, const void* send, void* recv, size_t count, ltm_dt
 // transfers into rank `root` (the blocks of one row owner).
 void comm_send_recv_slots(ltm_comm* c, const void* send, void* recv, size_t bytes, int root,
                           cudaStream_t st);
-// y[i] = sum over slots j of (j == own ? own[i] : slots[j * slot_stride + i])
-// (+ add[i]), summed in fp32 in slot order and rounded once (16-bit types).
-void launch_sum_slots(const void* slots, const void* own, int nslots, int own_slot,
-                      int64_t slot_stride, const void* add, void* y, int64_t n, ltm_dtype dt,
-                      cudaStream_t stream);
 // Rows [rows, cols] of int32 GEMM accumulators summed over the ranks' slots
 // (exact), then the W8A8 epilogue of the unsplit GEMM: y = round(fma(acc *
 // row_scale[r], col_scale[c], bias[c]) (+ add[r, c])), the arithmetic of the
