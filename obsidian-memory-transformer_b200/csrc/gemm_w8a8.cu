@@ -266,27 +266,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairStages = 4;
 constexpr int kPairBN = 256;
 constexpr int kPairAccBufs = 2;  // TMEM accumulators per CTA (kPairAccBufs x 256 columns)
+constexpr int kShortK = 2048;    // int8 K up to which the pair kernel runs 16 epilogue warps
 
+// EW epilogue warps per CTA (8: two column halves of the tile; 16: four
+// column quarters, for 16-bit outputs only: one 4 KiB staging box per warp).
+template <int EW>
 struct W8A8PairSmem {
+  static constexpr int kParts = EW / 4;                // column parts of the tile
+  static constexpr int kCW = kPairBN / kParts;         // columns per epilogue warp
   static constexpr uint32_t kA = kBM * kBK;            // this CTA's 128 rows of qa
   static constexpr uint32_t kB = (kPairBN / 2) * kBK;  // this CTA's 128 rows of qw
   static constexpr uint32_t kStage = kA + kB;          // multiple of 1024
   static constexpr uint32_t kStgOff = kPairStages * kStage;
-  static constexpr uint32_t kStgWarp = 2 * 32 * 128;  // two 4 KiB TMA-store boxes per warp
-  static constexpr uint32_t kColOff = kStgOff + kEpiWarps * kStgWarp;
-  static constexpr uint32_t kColWarp = 2 * (kPairBN / 2) * 4;
-  static constexpr uint32_t kBarOff = kColOff + kEpiWarps * kColWarp;
+  static constexpr uint32_t kStgWarp = (EW == 8 ? 2 : 1) * 32 * 128;  // 4 KiB TMA-store boxes
+  static constexpr uint32_t kColOff = kStgOff + EW * kStgWarp;
+  static constexpr uint32_t kColWarp = 2 * kCW * 4;
+  static constexpr uint32_t kBarOff = kColOff + EW * kColWarp;
   static constexpr uint32_t kBytes = kBarOff + 256 + 1024;
 };
 
-template <int MODE, class OutT, class AT>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int MODE, class OutT, class AT, int EW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
     w8a8_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmO, int M, int N, int K, int gm,
                         Epilogue ep, int* err) {
-  using L = W8A8PairSmem;
+  using L = W8A8PairSmem<EW>;
+  static_assert(EW == 8 || (EW == 16 && MODE != kEpiAccI32 && sizeof(OutT) == 2),
+                "16 epilogue warps stage one box of 16-bit values per tile");
   constexpr int BN = kPairBN;
+  constexpr int CW = L::kCW;
   constexpr int STAGES = kPairStages;
   constexpr int kKe = kBK / static_cast<int>(sizeof(AT));  // K elements per stage
   extern __shared__ uint8_t smem_raw[];
@@ -318,7 +327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf + b, 1);
-      mbar_init(acce + b, 2 * kEpiWarps);
+      mbar_init(acce + b, 2 * EW);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -400,14 +409,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Epilogue warps 2..9 of each CTA: TMEM lane quarter q = warp % 4 (this
-    // CTA's tile rows 32q..32q+31), column half (warp - 2) / 4.
+    // Epilogue warps 2..EW+1 of each CTA: TMEM lane quarter q = warp % 4
+    // (this CTA's tile rows 32q..32q+31), column part (warp - 2) / 4 of CW
+    // columns.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     uint8_t* stg = smem + L::kStgOff + (warp - 2) * L::kStgWarp;
     float* cvec = reinterpret_cast<float*>(smem + L::kColOff + (warp - 2) * L::kColWarp);
     const uint32_t acce0 = mapa_shared(acce, 0);  // the even CTA's acce[0]
-    TmaTileEpilogue<MODE, OutT, BN / 2, sizeof(AT) == 1, 128> epi;
+    TmaTileEpilogue<MODE, OutT, CW, sizeof(AT) == 1, 128> epi;
     auto rows_of = [&](int t) {
       int mb, nb;
       tile_coords(t, num_m, num_n, gm, mb, nb);
@@ -416,7 +426,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto cols_of = [&](int t) {
       int mb, nb;
       tile_coords(t, num_m, num_n, gm, mb, nb);
-      return nb * BN + half * (BN / 2);
+      return nb * BN + half * CW;
     };
     if (pair < tiles) epi.prefetch(ep, rows_of(pair) + lane, cols_of(pair), M, N, lane);
     int lt = 0;
@@ -429,7 +439,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                                      kErrWaitAccum)))
         break;
       tc_fence_after();
-      epi.run(ep, &tmO, tmem + b * BN + half * (BN / 2) + (static_cast<uint32_t>(q * 32) << 16),
+      epi.run(ep, &tmO, tmem + b * BN + half * CW + (static_cast<uint32_t>(q * 32) << 16),
               row0 + lane, row0, nw, M, N, cvec, stg, lane,
               [&] {
                 if (lane == 0) mbar_arrive_cluster(acce0 + static_cast<uint32_t>(b) * 8u);
@@ -474,23 +484,24 @@ int raster_group(int rows_per_block, int N, int K) {
   return static_cast<int>(std::max<int64_t>(1, (48ll << 20) / band));
 }
 
-template <int MODE, class OutT, class AT>
+template <int MODE, class OutT, class AT, int EW = 8>
 void launch_w8a8_pair(const void* qa, const void* qw, int M, int N, int K, const Epilogue& ep,
                       cudaStream_t stream) {
   using StoreT = typename std::conditional<MODE == kEpiAccI32, int32_t, OutT>::type;
-  using L = W8A8PairSmem;
+  using L = W8A8PairSmem<EW>;
   static_assert(L::kBytes <= 232448, "shared memory budget exceeded");
   CUtensorMap ta, tb, to;
   operand_maps<AT>(&ta, &tb, qa, qw, M, N, K, kPairBN / 2);
   constexpr int ob = static_cast<int>(sizeof(StoreT));
   make_tma_2d(&to, ep.out, tma_dtype_of<StoreT>(), ob, M, N, ep.ldo, 128 / ob, 32);
-  auto kern = w8a8_tc_pair_kernel<MODE, OutT, AT>;
+  auto kern = w8a8_tc_pair_kernel<MODE, OutT, AT, EW>;
   LTM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kPairBN - 1) / kPairBN);
   const int pairs_max = device_sm_count() / 2;
   const int grid = 2 * (tiles < pairs_max ? tiles : pairs_max);
   const int gm = raster_group<AT>(2 * kBM, N, K);
-  kern<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, to, M, N, K, gm, ep, device_error_ptr());
+  kern<<<grid, 64 + 32 * EW, L::kBytes, stream>>>(ta, tb, to, M, N, K, gm, ep,
+                                                   device_error_ptr());
   check_launch(sizeof(AT) == 1 ? kNamesI8[MODE] : kNamesF16[MODE], stream);
 }
 
@@ -540,8 +551,20 @@ void launch_gemm_tc(const void* qa, const void* qw, int64_t M, int64_t N, int64_
     constexpr int MODE = decltype(mode_c)::value;
     using OutT = decltype(out_tag);
     if constexpr (sizeof(AT) == 1 || (MODE != kEpiAccI32 && !std::is_same<OutT, float>::value)) {
-      if (N % 256 == 0 && M >= 2 * kBM)
+      // (plain epilogues: the operand-carrying modes would spill at the
+      // 96 registers a 576-thread CTA leaves)
+      constexpr bool kEpi16 = sizeof(AT) == 1 && MODE == kEpiPlain && sizeof(OutT) == 2;
+      if (N % 256 == 0 && M >= 2 * kBM) {
+        // short K: the tile's epilogue outlasts its MMAs, so sixteen
+        // epilogue warps share it
+        if constexpr (kEpi16) {
+          if (K <= kShortK) {
+            launch_w8a8_pair<MODE, OutT, AT, 16>(qa, qw, m, n, k, ep, stream);
+            return;
+          }
+        }
         launch_w8a8_pair<MODE, OutT, AT>(qa, qw, m, n, k, ep, stream);
+      }
       else if (N % 256 == 0)
         launch_w8a8_inst<256, 3, MODE, OutT, AT>(qa, qw, m, n, k, ep, stream);
       else

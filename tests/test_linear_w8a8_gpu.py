@@ -67,3 +67,24 @@ def test_rejects_bad_shapes(ltm):
     qw = torch.zeros((40, 32), dtype=torch.int8, device="cuda")
     with pytest.raises(ltm.LtmError):
         ltm.linear_w8a8_acc_i32(torch.zeros((4, 32), dtype=torch.int8, device="cuda"), qw)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 768, 768), (4100, 768, 768), (600, 512, 2048),
+                                   (1024, 3072, 768)])
+@pytest.mark.parametrize("out", ["f16", "bf16"])
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_short_k_16bit_epilogue_equals_rounded_f32(ltm, orc, M, N, K, out, act):
+    """At K <= 2048 the CTA-pair kernel's plain 16-bit epilogue runs on
+    sixteen warps (four column quarters per tile); its outputs must be the
+    fp32 epilogue's values (eight warps) rounded to 16 bits, bit for bit."""
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    qa, sa = orc.quant_int8_rows(a)
+    qw, sw = orc.quant_int8_rows(w)
+    dev = lambda x: torch.from_numpy(x).cuda()  # noqa: E731
+    y32 = ltm.linear_w8a8(dev(qa), dev(sa), dev(qw), dev(sw), dev(b), act, torch.float32)
+    y16 = ltm.linear_w8a8(dev(qa), dev(sa), dev(qw), dev(sw), dev(b), act, torch_dtype(out))
+    assert torch.equal(y16, y32.to(torch_dtype(out))), "16-bit epilogue differs from rounded fp32"
