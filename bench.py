@@ -64,6 +64,10 @@ def parse():
                     help="chunked collectives overlapping the GEMMs in the sequence-parallel "
                          "forward (auto: the library's default, off)")
     ap.add_argument("--comm-sms", type=int, default=16, help=argparse.SUPPRESS)
+    ap.add_argument("--tp-reduce", choices=["act", "exact"], default="act",
+                    help="row-parallel reductions of the sequence-parallel forward: partial sums "
+                         "in the activation type (NCCL reduce-scatter) or exact int32 "
+                         "accumulators (output equal to one GPU's)")
     ap.add_argument("--no-sp", action="store_true",
                     help="tensor parallel without sequence parallelism (every rank holds the "
                          "full activations; allreduce after the row-parallel projections)")
@@ -534,6 +538,8 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
     blk = ltm.TitanBlock(cfg, q, comm=comm)
     ovl_mode = {"auto": None, "on": True, "off": False}[args.overlap]
     blk.set_overlap(ovl_mode, args.comm_sms)
+    if not w4a16:
+        blk.set_tp_reduction(args.tp_reduce == "exact")
     overlapped = bool(ovl_mode) and not w4a16
     w = synthetic.block_weights(H, F, Ms, 1000)
     blk.load_weights(w)
@@ -657,6 +663,7 @@ def run_tp(args, wl: dict = TP_WL, w4a16: bool = False, side: bool = False):
                                              "timed steps overlap them with the GEMMs)"
                                              if (sp and overlapped) else None,
                        "comm_overlap": bool(sp and overlapped),
+                       "tp_reduction": args.tp_reduce if sp else None,
                        "weights": "one random-init block's shard applied at every layer",
                        "l2": "inputs (1 GiB per activation tensor) larger than L2"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
